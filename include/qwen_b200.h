@@ -1,0 +1,176 @@
+/* qwen_b200.h — C ABI of the B200 (sm_100a) Qwen3-0.6B batch-1 decode engine.
+ *
+ * Plain C: pointers, sizes and status codes only; no C++ or torch types.
+ * Every entry point returns QWEN_OK (0) or a negative status; qwen_last_error()
+ * gives the message of the last failure on the calling thread.  Nothing here
+ * calls exit().  A handle owns all of its device memory and one CUDA stream on
+ * one device; it is not thread-safe (one handle per GPU, one host thread each).
+ *
+ * Each declaration names the reference interface it replaces
+ * (Ramshankar07/qwen600-ROCm-inference, file:line).
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QWEN_OK             0
+#define QWEN_E_ARG         -1   /* bad argument: token/pos out of range, NULL pointer, bad shape */
+#define QWEN_E_IO          -2   /* cannot open / read / map the checkpoint */
+#define QWEN_E_FORMAT      -3   /* checkpoint header or tensor table does not match the model */
+#define QWEN_E_CUDA        -4   /* a CUDA runtime call failed */
+#define QWEN_E_TIMEOUT     -5   /* a bounded device-side wait ran out; device state was reset */
+#define QWEN_E_UNSUPPORTED -6   /* valid request this build does not serve (e.g. top_k > 64 on device) */
+#define QWEN_E_STATE       -7   /* call out of order (e.g. pos not contiguous with the cache) */
+
+typedef struct qwen_ctx qwen_t;
+
+/* Sampling parameters of sampler.h's Sampler (sampler.h:17-24, 99-112).
+ * temperature == 0 or top_k == 1 selects argmax (sampler.h:125-128);
+ * top_k == 0 means the whole vocabulary (sampler.h:109);
+ * topp outside (0, 1) disables the nucleus cut (sampler.h:153). */
+typedef struct {
+    float temperature;
+    float topp;
+    int   top_k;
+} qwen_sampling_t;
+
+/* Message of the last error on this thread ("" if none). */
+const char* qwen_last_error(void);
+
+/* ABI version (major*10000 + minor*100 + patch). */
+int qwen_abi_version(void);
+
+/* ---- checkpoint (static_loader.h) --------------------------------------- */
+
+/* Number of tensors in the model's canonical weight layout (static_loader.h:81, NUM_TENSORS = 311). */
+int qwen_num_tensors(void);
+
+/* Total bytes of the canonical device weight block (static_loader.h:80, TOTAL_WEIGHTS_BYTES). */
+size_t qwen_total_weight_bytes(void);
+
+/* Entry i of the canonical table: name, byte offset from the block start, size in bytes
+ * (static_loader.h:83-400, TENSOR_METADATA).  The offsets are the order-sorted
+ * safetensors layout of Qwen3-0.6B; the table is derived, not stored. */
+int qwen_tensor_info(int index, const char** name, size_t* offset, size_t* bytes);
+
+/* Parse and validate a safetensors checkpoint on the host only (no GPU needed):
+ * the JSON header, every tensor's dtype/shape, and the file size.  The tensors
+ * may appear in any order.  Replaces the header read of static_loader.h:415-427. */
+int qwen_checkpoint_validate(const char* path);
+
+/* Load a checkpoint into ONE device allocation laid out in the canonical order
+ * (static_loader.h:402-494, load_qwen_weights).  *dev_block receives the device
+ * pointer (free with qwen_weights_free); tensor i sits at qwen_tensor_info(i).offset. */
+int qwen_weights_load(const char* path, int device, void** dev_block);
+int qwen_weights_free(void* dev_block);
+
+/* Write a synthetic Qwen3-0.6B checkpoint (valid safetensors, canonical layout):
+ * every matrix ~ N(0, 0.02) rounded to bf16 from a counter-based generator keyed
+ * by `seed`, every RMSNorm / QK-norm gain 1.0, lm_head.weight == embed_tokens.weight.
+ * Stands in for the exporter's weights (export.py:39-146) where no real
+ * checkpoint is available. */
+int qwen_write_synthetic_checkpoint(const char* path, uint64_t seed);
+
+/* ---- model (qwen_model.cuh) --------------------------------------------- */
+
+/* Load weights, allocate the KV cache and work buffers on `device`
+ * (qwen_model.cuh:82-92, build_transformer). */
+int qwen_create(const char* safetensors_path, int device, qwen_t** out);
+
+/* Free everything the handle owns (qwen_model.cuh:94-111, free_transformer). */
+void qwen_destroy(qwen_t* ctx);
+
+/* Device the handle lives on. */
+int qwen_device(const qwen_t* ctx);
+
+/* One position of the decode chain (qwen_model.cuh:772-851, forward): embeds
+ * `token`, appends its K/V at `pos` and computes the VOCAB_SIZE fp32 logits.
+ * Positions must arrive in order 0..pos (pos <= the number of cached
+ * positions).  If logits_host is non-NULL the logits are copied there before
+ * return (the reference's blocking D2H, qwen_model.cuh:848). */
+int qwen_forward(qwen_t* ctx, int token, int pos, float* logits_host);
+
+/* Pinned host buffer of VOCAB_SIZE floats owned by the handle (qwen_model.cuh:59,
+ * Transformer.h_logits); qwen_forward(ctx, t, p, qwen_host_logits(ctx)) is the
+ * reference's forward() contract. */
+float* qwen_host_logits(qwen_t* ctx);
+
+/* Device pointer to the fp32 logits of the last forward / decode step. */
+const float* qwen_device_logits(qwen_t* ctx);
+
+/* forward(token, pos) followed by sample() on the device (main.cu:144-145 with
+ * sampler.h:120-175): *next_token receives the sampled id and *rng_state the
+ * advanced xorshift64* state.  Only 4 + 8 bytes come back to the host.
+ * Device sampling supports argmax and 1 <= top_k <= 64. */
+int qwen_decode_step(qwen_t* ctx, int token, int pos, const qwen_sampling_t* sp,
+                     unsigned long long* rng_state, int* next_token);
+
+/* n_steps chained decode steps without host round trips: step i feeds the
+ * token sampled by step i-1 (step 0 feeds `token` at `pos`).  tokens_out
+ * receives the n_steps sampled ids (host memory). */
+int qwen_generate(qwen_t* ctx, int token, int pos, int n_steps, const qwen_sampling_t* sp,
+                  unsigned long long* rng_state, int* tokens_out);
+
+/* Prompt ingestion: positions pos0 .. pos0+n-1 of `tokens` enter the KV cache
+ * (no reference counterpart: the reference loops forward() per prompt
+ * position, main.cu:141-145).  If logits_host is non-NULL it receives the
+ * logits of the last prompt position. */
+int qwen_prefill(qwen_t* ctx, const int* tokens, int n, int pos0, float* logits_host);
+
+/* Number of positions currently held in the KV cache. */
+int qwen_cached_positions(const qwen_t* ctx);
+
+/* ---- vocabulary-sharded LM head (multi-GPU, no reference counterpart) ---- */
+
+/* Restrict this handle's LM head to vocabulary rows [row_begin, row_end).
+ * qwen_shard_topk then reports the shard's top-k (logit, global id) pairs of the
+ * last forward, in descending order, ties by ascending id. */
+int qwen_set_vocab_shard(qwen_t* ctx, int row_begin, int row_end);
+int qwen_shard_topk(qwen_t* ctx, int k, float* values_host, int* ids_host);
+
+/* ---- host sampler (sampler.h) ------------------------------------------- */
+
+/* sampler.h:120-175 on host logits, restated: argmax / top-k (Hoare quickselect)
+ * / temperature softmax / top-p / inverse-CDF draw with xorshift64*.  This is
+ * the reference's host API, kept for drop-in callers of sample(). */
+int qwen_sample_host(const float* logits, int n, const qwen_sampling_t* sp,
+                     unsigned long long* rng_state, int* token_out);
+
+/* Merge per-shard candidate lists (values/ids, n entries, any order) into the
+ * final sampled token with the device sampler's math, on the host: used after
+ * the NVLink all-gather of shard top-k lists. */
+int qwen_sample_candidates(const float* values, const int* ids, int n, const qwen_sampling_t* sp,
+                           unsigned long long* rng_state, int* token_out);
+
+/* ---- diagnostics ---------------------------------------------------------- */
+
+/* Per-CTA ring accounting of the last decode launch: out[2c] = chunks the
+ * producer issued, out[2c+1] = chunks the consumers took (they must agree).
+ * Returns the number of CTAs (or a negative status). No reference counterpart. */
+int qwen_debug_chunk_counts(qwen_t* ctx, int* out, int max_ctas);
+
+/* Keep a copy of the residual stream after every layer (enable = 1) for
+ * qwen_debug_read; resid: N_LAYERS*DIM floats, qkv: N_LAYERS*4096 floats of raw
+ * q|k|v projections of the last launch (either may be NULL). */
+int qwen_debug_capture(qwen_t* ctx, int enable);
+int qwen_debug_read(qwen_t* ctx, float* resid, float* qkv);
+
+/* ---- isolated kernels ---------------------------------------------------- */
+
+/* y[n] = bf16(W[n][k] . x[k]) with fp32 accumulation; W row-major bf16, x and y
+ * bf16, all device pointers; k a multiple of 256, k <= 4096.  `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  The GEMV of matmul_cublas
+ * (qwen_model.cuh:706-757) with alpha = 1, beta = 0. */
+int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_B200_H */

@@ -1,0 +1,546 @@
+// engine.cu — the C ABI of include/qwen_b200.h: checkpoint upload, device
+// buffers, the decode launches and the isolated GEMV.
+//
+// Reference counterparts (Ramshankar07/qwen600-ROCm-inference):
+//   qwen_create        build_transformer + malloc_run_state (qwen_model.cuh:63-92)
+//                      + load_qwen_weights (static_loader.h:402-494)
+//   qwen_forward       forward (qwen_model.cuh:772-851)
+//   qwen_decode_step   forward + sample (main.cu:144-145, sampler.h:120-175)
+//   qwen_destroy       free_transformer (qwen_model.cuh:94-111)
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/qwen_b200.h"
+#include "decode_kernel.cuh"
+#include "gemv_kernel.cuh"
+#include "model_format.h"
+
+using namespace qb;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_err;
+static int fail(int code, const std::string& msg) { g_err = msg; return code; }
+#define CU(call)                                                                                        \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess) return fail(QWEN_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+extern "C" const char* qwen_last_error(void) { return g_err.c_str(); }
+extern "C" int qwen_abi_version(void) { return 10000; }
+
+// ---------------------------------------------------------------------------
+// tensor table / checkpoint
+// ---------------------------------------------------------------------------
+extern "C" int qwen_num_tensors(void) { return (int)canonical_table().size(); }
+extern "C" size_t qwen_total_weight_bytes(void) { return canonical_total_bytes(); }
+extern "C" int qwen_tensor_info(int index, const char** name, size_t* offset, size_t* bytes) {
+    const auto& t = canonical_table();
+    if (index < 0 || index >= (int)t.size()) return fail(QWEN_E_ARG, "tensor index out of range");
+    if (name) *name = t[index].name.c_str();
+    if (offset) *offset = t[index].offset;
+    if (bytes) *bytes = t[index].bytes;
+    return QWEN_OK;
+}
+extern "C" int qwen_checkpoint_validate(const char* path) {
+    if (!path) return fail(QWEN_E_ARG, "path is NULL");
+    CheckpointMap m; std::string err;
+    const int rc = parse_checkpoint(path, m, err);
+    return rc == QWEN_OK ? QWEN_OK : fail(rc, err);
+}
+extern "C" int qwen_write_synthetic_checkpoint(const char* path, uint64_t seed) {
+    if (!path) return fail(QWEN_E_ARG, "path is NULL");
+    std::string err;
+    const int rc = write_synthetic(path, seed, err);
+    return rc == QWEN_OK ? QWEN_OK : fail(rc, err);
+}
+
+// Stream the checkpoint's tensors to their canonical offsets in `dev` through
+// two pinned staging buffers (read of one overlaps the copy of the other).
+static int upload_checkpoint(const std::string& path, const CheckpointMap& m, uint8_t* dev, cudaStream_t st) {
+    const auto& t = canonical_table();
+    struct Seg { size_t f, d, n; };
+    std::vector<Seg> segs;
+    std::vector<int> order(t.size());
+    for (size_t i = 0; i < t.size(); i++) order[i] = (int)i;
+    std::sort(order.begin(), order.end(), [&](int a, int b) { return m.file_offset[a] < m.file_offset[b]; });
+    for (int i : order) {
+        const Seg s{m.file_offset[i], t[i].offset, t[i].bytes};
+        if (!segs.empty() && segs.back().f + segs.back().n == s.f && segs.back().d + segs.back().n == s.d) segs.back().n += s.n;
+        else segs.push_back(s);
+    }
+    const int fd = open(path.c_str(), O_RDONLY);
+    if (fd < 0) return fail(QWEN_E_IO, "cannot open checkpoint: " + path);
+    const size_t CH = (size_t)64 << 20;
+    void* stage[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    bool used[2] = {false, false};
+    int rc = QWEN_OK;
+    for (int i = 0; i < 2 && rc == QWEN_OK; i++) {
+        if (cudaHostAlloc(&stage[i], CH, cudaHostAllocDefault) != cudaSuccess || cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess)
+            rc = fail(QWEN_E_CUDA, "pinned staging allocation failed");
+    }
+    int b = 0;
+    for (const Seg& s : segs) {
+        for (size_t off = 0; off < s.n && rc == QWEN_OK; off += CH) {
+            const size_t len = std::min(CH, s.n - off);
+            if (used[b] && cudaEventSynchronize(ev[b]) != cudaSuccess) { rc = fail(QWEN_E_CUDA, "staging event wait failed"); break; }
+            size_t got = 0;
+            while (got < len) {
+                const ssize_t r = pread(fd, (char*)stage[b] + got, len - got, (off_t)(s.f + off + got));
+                if (r <= 0) { rc = fail(QWEN_E_IO, "short read from checkpoint (truncated file?)"); break; }
+                got += (size_t)r;
+            }
+            if (rc != QWEN_OK) break;
+            if (cudaMemcpyAsync(dev + s.d + off, stage[b], len, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaEventRecord(ev[b], st) != cudaSuccess) { rc = fail(QWEN_E_CUDA, "weight upload failed"); break; }
+            used[b] = true;
+            b ^= 1;
+        }
+        if (rc != QWEN_OK) break;
+    }
+    if (cudaStreamSynchronize(st) != cudaSuccess && rc == QWEN_OK) rc = fail(QWEN_E_CUDA, "weight upload sync failed");
+    for (int i = 0; i < 2; i++) { if (ev[i]) cudaEventDestroy(ev[i]); if (stage[i]) cudaFreeHost(stage[i]); }
+    close(fd);
+    return rc;
+}
+
+extern "C" int qwen_weights_load(const char* path, int device, void** dev_block) {
+    if (!path || !dev_block) return fail(QWEN_E_ARG, "NULL argument");
+    *dev_block = nullptr;
+    CheckpointMap m; std::string err;
+    int rc = parse_checkpoint(path, m, err);
+    if (rc != QWEN_OK) return fail(rc, err);
+    CU(cudaSetDevice(device));
+    void* blk = nullptr;
+    CU(cudaMalloc(&blk, canonical_total_bytes()));
+    cudaStream_t st;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) { cudaFree(blk); return fail(QWEN_E_CUDA, "stream creation failed"); }
+    rc = upload_checkpoint(path, m, (uint8_t*)blk, st);
+    cudaStreamDestroy(st);
+    if (rc != QWEN_OK) { cudaFree(blk); return rc; }
+    *dev_block = blk;
+    return QWEN_OK;
+}
+extern "C" int qwen_weights_free(void* dev_block) {
+    if (dev_block) CU(cudaFree(dev_block));
+    return QWEN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// load-time repacking
+// ---------------------------------------------------------------------------
+// Wo [DIM][Q_DIM] -> [8][DIM][256]: group g's 256 input columns contiguous per row.
+__global__ void pack_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __restrict__ wo_g) {
+    const size_t n = (size_t)DIM * Q_DIM;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / Q_DIM), col = (int)(i % Q_DIM), g = col / 256, cc = col % 256;
+        wo_g[((size_t)g * DIM + r) * 256 + cc] = wo[i];
+    }
+}
+// Wd [DIM][HIDDEN] -> Wd^T [HIDDEN][DIM].
+__global__ void pack_wd_kernel(const uint16_t* __restrict__ wd, uint16_t* __restrict__ wdt) {
+    const size_t n = (size_t)DIM * HIDDEN_DIM;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i / DIM), r = (int)(i % DIM);
+        wdt[i] = wd[(size_t)r * HIDDEN_DIM + j];
+    }
+}
+
+// RoPE cos/sin of every position, computed the way the reference writes it
+// (qwen_model.cuh:331-334): freq = 1/powf(theta, 2j/128), angle = pos*freq in
+// fp32.  The libm calls go through volatile pointers so the compiler cannot
+// fold them at a different precision.
+static void rope_table(std::vector<float>& tab) {
+    float (*volatile p_pow)(float, float) = powf;
+    void (*volatile p_sincos)(float, float*, float*) = sincosf;
+    tab.assign((size_t)SEQ_LEN * HEAD_DIM, 0.f);
+    for (int j = 0; j < HEAD_DIM / 2; j++) {
+        const float freq = 1.0f / p_pow(ROPE_THETA, (float)(j * 2) / (float)HEAD_DIM);
+        for (int pos = 0; pos < SEQ_LEN; pos++) {
+            const float val = (float)pos * freq;
+            float s, c;
+            p_sincos(val, &s, &c);
+            tab[(size_t)pos * HEAD_DIM + j] = c;
+            tab[(size_t)pos * HEAD_DIM + 64 + j] = s;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+struct qwen_ctx {
+    int device = 0;
+    int nsm = 0;
+    cudaStream_t stream = nullptr;
+    uint8_t* wblock = nullptr;
+    uint16_t *wo_g = nullptr, *wd_t = nullptr, *kc = nullptr, *vc = nullptr;
+    float *rope = nullptr, *qkv = nullptr, *part = nullptr, *ybuf = nullptr, *acc = nullptr, *logits = nullptr;
+    float *cand_v = nullptr, *top_v = nullptr;
+    int *cand_i = nullptr, *top_i = nullptr, *prompt = nullptr, *tokens = nullptr, *chunk_count = nullptr;
+    uint32_t* ctr = nullptr;
+    StepIn* d_in = nullptr;
+    StepOut* d_out = nullptr;
+    StepIn* h_in = nullptr;
+    StepOut* h_out = nullptr;
+    float* h_logits = nullptr;
+    int* h_tokens = nullptr;
+    DecodeParams params{};
+    int cached = 0;
+    int last_k = 0;
+};
+
+static void ctx_free(qwen_t* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->params.dbg_resid) cudaFree(c->params.dbg_resid);
+    void* dev[] = {c->wblock, c->wo_g, c->wd_t, c->kc, c->vc, c->rope, c->qkv, c->part, c->ybuf, c->acc, c->logits,
+                   c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
+    for (void* p : dev) if (p) cudaFree(p);
+    void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
+    for (void* p : host) if (p) cudaFreeHost(p);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+static int reset_device_state(qwen_t* c) {
+    CU(cudaMemsetAsync(c->ctr, 0, (size_t)kNumCtr * kCtrStride * sizeof(uint32_t), c->stream));
+    CU(cudaMemsetAsync(c->acc, 0, (size_t)N_LAYERS * DIM * sizeof(float), c->stream));
+    StepOut o{};
+    o.epoch = 1;
+    *c->h_out = o;
+    CU(cudaMemcpyAsync(c->d_out, c->h_out, sizeof(StepOut), cudaMemcpyHostToDevice, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return QWEN_OK;
+}
+
+template <typename T>
+static int dalloc(T** p, size_t n) {
+    CU(cudaMalloc((void**)p, n * sizeof(T)));
+    return QWEN_OK;
+}
+#define TRY(x) do { const int rc_ = (x); if (rc_ != QWEN_OK) { ctx_free(c); return rc_; } } while (0)
+
+extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
+    if (!path || !out) return fail(QWEN_E_ARG, "NULL argument");
+    *out = nullptr;
+    CheckpointMap m; std::string err;
+    int rc = parse_checkpoint(path, m, err);
+    if (rc != QWEN_OK) return fail(rc, err);
+    int ndev = 0;
+    CU(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(QWEN_E_ARG, "device index out of range");
+    CU(cudaSetDevice(device));
+    qwen_t* c = new qwen_ctx();
+    c->device = device;
+    if (cudaDeviceGetAttribute(&c->nsm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "device query failed"); }
+    if (c->nsm < 8 * kMinGS || c->nsm > 8 * kMaxGS || (VOCAB_SIZE + c->nsm - 1) / c->nsm > kMaxLocalRows ||
+        (HIDDEN_DIM + c->nsm - 1) / c->nsm > kMaxMlpRows) {
+        ctx_free(c); return fail(QWEN_E_UNSUPPORTED, "unsupported SM count " + std::to_string(c->nsm));
+    }
+    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemBytes) != cudaSuccess) {
+        ctx_free(c); return fail(QWEN_E_CUDA, "cannot reserve " + std::to_string(kDecodeSmemBytes) + " B of shared memory");
+    }
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_kernel, kThreads, kDecodeSmemBytes) != cudaSuccess || nb < 1) {
+        ctx_free(c); return fail(QWEN_E_CUDA, "decode kernel cannot be resident on every SM");
+    }
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "stream creation failed"); }
+
+    const size_t total = canonical_total_bytes();
+    TRY(dalloc(&c->wblock, total));
+    TRY(upload_checkpoint(path, m, c->wblock, c->stream));
+    TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * DIM * Q_DIM));
+    TRY(dalloc(&c->wd_t, (size_t)N_LAYERS * DIM * HIDDEN_DIM));
+    const size_t kv = (size_t)N_LAYERS * N_KV_HEADS * SEQ_LEN * HEAD_DIM;
+    TRY(dalloc(&c->kc, kv));
+    TRY(dalloc(&c->vc, kv));
+    TRY(dalloc(&c->rope, (size_t)SEQ_LEN * HEAD_DIM));
+    TRY(dalloc(&c->qkv, (size_t)N_LAYERS * 4096));
+    TRY(dalloc(&c->part, (size_t)N_LAYERS * kGroups * kMaxGS * kPartStride));
+    TRY(dalloc(&c->ybuf, (size_t)N_LAYERS * kGroups * DIM));
+    TRY(dalloc(&c->acc, (size_t)N_LAYERS * DIM));
+    TRY(dalloc(&c->logits, (size_t)VOCAB_SIZE));
+    TRY(dalloc(&c->cand_v, (size_t)c->nsm * kMaxCand));
+    TRY(dalloc(&c->cand_i, (size_t)c->nsm * kMaxCand));
+    TRY(dalloc(&c->top_v, (size_t)kMaxCand));
+    TRY(dalloc(&c->top_i, (size_t)kMaxCand));
+    TRY(dalloc(&c->prompt, (size_t)SEQ_LEN));
+    TRY(dalloc(&c->tokens, (size_t)SEQ_LEN));
+    TRY(dalloc(&c->ctr, (size_t)kNumCtr * kCtrStride));
+    TRY(dalloc(&c->chunk_count, (size_t)2 * c->nsm));
+    TRY(dalloc(&c->d_in, 1));
+    TRY(dalloc(&c->d_out, 1));
+    if (cudaHostAlloc((void**)&c->h_in, sizeof(StepIn), 0) != cudaSuccess || cudaHostAlloc((void**)&c->h_out, sizeof(StepOut), 0) != cudaSuccess ||
+        cudaHostAlloc((void**)&c->h_logits, (size_t)VOCAB_SIZE * sizeof(float), 0) != cudaSuccess ||
+        cudaHostAlloc((void**)&c->h_tokens, (size_t)SEQ_LEN * sizeof(int), 0) != cudaSuccess) {
+        ctx_free(c); return fail(QWEN_E_CUDA, "pinned host allocation failed");
+    }
+    if (cudaMemsetAsync(c->kc, 0, kv * 2, c->stream) != cudaSuccess || cudaMemsetAsync(c->vc, 0, kv * 2, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->prompt, 0, SEQ_LEN * sizeof(int), c->stream) != cudaSuccess) {
+        ctx_free(c); return fail(QWEN_E_CUDA, "memset failed");
+    }
+    std::vector<float> tab;
+    rope_table(tab);
+    if (cudaMemcpyAsync(c->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+        ctx_free(c); return fail(QWEN_E_CUDA, "rope upload failed");
+    }
+
+    DecodeParams& P = c->params;
+    auto W = [&](int idx) { return (const uint16_t*)(c->wblock + canonical_table()[idx].offset); };
+    P.embed = W(embed_index());
+    P.lm = W(lm_head_index());
+    P.final_ln = W(final_norm_index());
+    for (int l = 0; l < N_LAYERS; l++) {
+        const LayerIndex li = layer_index(l);
+        P.in_ln[l] = W(li.in_ln); P.post_ln[l] = W(li.post_ln);
+        P.wq[l] = W(li.q_proj); P.wk[l] = W(li.k_proj); P.wv[l] = W(li.v_proj);
+        P.qn[l] = W(li.q_norm); P.kn[l] = W(li.k_norm);
+        P.wg[l] = W(li.gate); P.wu[l] = W(li.up);
+        pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * DIM * Q_DIM);
+        pack_wd_kernel<<<1024, 256, 0, c->stream>>>(W(li.down), c->wd_t + (size_t)l * DIM * HIDDEN_DIM);
+    }
+    if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
+    P.wo_g = c->wo_g; P.wd_t = c->wd_t; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
+    P.qkv = c->qkv; P.part = c->part; P.ybuf = c->ybuf; P.acc = c->acc; P.logits = c->logits;
+    P.cand_v = c->cand_v; P.cand_i = c->cand_i; P.top_v = c->top_v; P.top_i = c->top_i; P.ctr = c->ctr;
+    P.in = c->d_in; P.out = c->d_out; P.tokens_out = c->tokens; P.tokens_cap = SEQ_LEN;
+    P.lm_begin = 0; P.lm_end = VOCAB_SIZE;
+    P.chunk_count = c->chunk_count;
+    TRY(reset_device_state(c));
+    *out = c;
+    return QWEN_OK;
+}
+
+extern "C" void qwen_destroy(qwen_t* c) { ctx_free(c); }
+extern "C" int qwen_device(const qwen_t* c) { return c ? c->device : -1; }
+extern "C" float* qwen_host_logits(qwen_t* c) { return c ? c->h_logits : nullptr; }
+extern "C" const float* qwen_device_logits(qwen_t* c) { return c ? c->logits : nullptr; }
+extern "C" int qwen_cached_positions(const qwen_t* c) { return c ? c->cached : -1; }
+
+static int launch_decode(qwen_t* c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)c->nsm);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kDecodeSmemBytes;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    CU(cudaLaunchKernelEx(&cfg, decode_kernel, c->params));
+    return QWEN_OK;
+}
+
+// After a synchronised launch sequence: surface a device-side wait timeout.
+static int check_step(qwen_t* c) {
+    if (c->h_out->err) {
+        const unsigned e = c->h_out->err; const int w = c->h_out->err_where;
+        reset_device_state(c);
+        c->cached = 0;
+        return fail(QWEN_E_TIMEOUT, "device wait expired (code " + std::to_string(e) + ", slot " + std::to_string(w) +
+                                        "); device state reset, KV cache invalidated");
+    }
+    return QWEN_OK;
+}
+
+static int check_sampling(const qwen_sampling_t* sp) {
+    if (!sp) return QWEN_OK;
+    if (!(sp->temperature >= 0.0f)) return fail(QWEN_E_ARG, "temperature must be >= 0");
+    const bool greedy = sp->temperature == 0.0f || sp->top_k == 1;
+    if (!greedy && (sp->top_k < 1 || sp->top_k > kMaxCand))
+        return fail(QWEN_E_UNSUPPORTED, "device sampling serves 1 <= top_k <= 64 (top_k = 0 means the full vocabulary)");
+    return QWEN_OK;
+}
+
+static void fill_in(qwen_t* c, int token, int pos, const qwen_sampling_t* sp, unsigned long long rng, int flags) {
+    StepIn& in = *c->h_in;
+    in.token = token; in.pos = pos; in.flags = flags; in.rng = rng;
+    if (sp) { in.temperature = sp->temperature; in.topp = sp->topp; in.top_k = sp->top_k; }
+    else { in.temperature = 0.f; in.topp = 1.f; in.top_k = 1; }
+}
+
+extern "C" int qwen_forward(qwen_t* c, int token, int pos, float* logits_host) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (token < 0 || token >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
+    if (pos < 0 || pos >= SEQ_LEN) return fail(QWEN_E_ARG, "pos out of range [0, SEQ_LEN)");
+    if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
+    if (c->params.lm_begin != 0 || c->params.lm_end != VOCAB_SIZE) {
+        if (logits_host) return fail(QWEN_E_STATE, "full logits requested from a vocabulary-sharded handle");
+    }
+    CU(cudaSetDevice(c->device));
+    fill_in(c, token, pos, nullptr, 0, kFlagWriteLogits);
+    CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+    int rc = launch_decode(c);
+    if (rc != QWEN_OK) return rc;
+    if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    c->last_k = 1;
+    if ((rc = check_step(c)) != QWEN_OK) return rc;
+    c->cached = pos + 1;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_decode_step(qwen_t* c, int token, int pos, const qwen_sampling_t* sp, unsigned long long* rng_state, int* next) {
+    if (!c || !next) return fail(QWEN_E_ARG, "NULL argument");
+    if (token < 0 || token >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
+    if (pos < 0 || pos >= SEQ_LEN) return fail(QWEN_E_ARG, "pos out of range [0, SEQ_LEN)");
+    if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
+    int rc = check_sampling(sp);
+    if (rc != QWEN_OK) return rc;
+    CU(cudaSetDevice(c->device));
+    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, 0);
+    CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+    if ((rc = launch_decode(c)) != QWEN_OK) return rc;
+    CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    c->last_k = (!sp || sp->temperature == 0.0f || sp->top_k == 1) ? 1 : sp->top_k;
+    if ((rc = check_step(c)) != QWEN_OK) return rc;
+    *next = c->h_out->out_token;
+    if (rng_state) *rng_state = c->h_out->rng;
+    c->cached = pos + 1;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_generate(qwen_t* c, int token, int pos, int n_steps, const qwen_sampling_t* sp, unsigned long long* rng_state,
+                             int* tokens_out) {
+    if (!c || !tokens_out) return fail(QWEN_E_ARG, "NULL argument");
+    if (n_steps <= 0) return fail(QWEN_E_ARG, "n_steps must be positive");
+    if (token < 0 || token >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
+    if (pos < 0 || (long long)pos + n_steps > SEQ_LEN) return fail(QWEN_E_ARG, "pos + n_steps exceeds SEQ_LEN");
+    if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
+    int rc = check_sampling(sp);
+    if (rc != QWEN_OK) return rc;
+    CU(cudaSetDevice(c->device));
+    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, 0);
+    CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemsetAsync(&c->d_out->n_done, 0, sizeof(int), c->stream));
+    for (int i = 0; i < n_steps; i++)
+        if ((rc = launch_decode(c)) != QWEN_OK) return rc;
+    CU(cudaMemcpyAsync(c->h_tokens, c->tokens, (size_t)n_steps * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    c->last_k = (!sp || sp->temperature == 0.0f || sp->top_k == 1) ? 1 : sp->top_k;
+    if ((rc = check_step(c)) != QWEN_OK) return rc;
+    memcpy(tokens_out, c->h_tokens, (size_t)n_steps * sizeof(int));
+    if (rng_state) *rng_state = c->h_out->rng;
+    c->cached = pos + n_steps;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float* logits_host) {
+    if (!c || !tokens) return fail(QWEN_E_ARG, "NULL argument");
+    if (n <= 0 || pos0 < 0 || (long long)pos0 + n > SEQ_LEN) return fail(QWEN_E_ARG, "prompt does not fit [0, SEQ_LEN)");
+    if (pos0 > c->cached) return fail(QWEN_E_STATE, "pos0 skips uncached positions");
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= VOCAB_SIZE) return fail(QWEN_E_ARG, "prompt token out of range");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpyAsync(c->prompt + pos0, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    int rc;
+    if (n > 1) {
+        fill_in(c, 0, pos0, nullptr, 0, kFlagPromptToken | kFlagNoHead);
+        CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+        for (int i = 0; i < n - 1; i++)
+            if ((rc = launch_decode(c)) != QWEN_OK) return rc;
+    }
+    // last prompt position with the LM head (logits of the prompt's end)
+    CU(cudaStreamSynchronize(c->stream));
+    fill_in(c, 0, pos0 + n - 1, nullptr, 0, kFlagPromptToken | kFlagWriteLogits);
+    CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+    if ((rc = launch_decode(c)) != QWEN_OK) return rc;
+    if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    c->last_k = 1;
+    if ((rc = check_step(c)) != QWEN_OK) return rc;
+    c->cached = pos0 + n;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_set_vocab_shard(qwen_t* c, int row_begin, int row_end) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (row_begin < 0 || row_end > VOCAB_SIZE || row_end - row_begin < c->nsm * kMaxCand / 16 || row_begin >= row_end)
+        return fail(QWEN_E_ARG, "bad vocabulary shard");
+    c->params.lm_begin = row_begin;
+    c->params.lm_end = row_end;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_shard_topk(qwen_t* c, int k, float* values_host, int* ids_host) {
+    if (!c || !values_host || !ids_host) return fail(QWEN_E_ARG, "NULL argument");
+    if (k < 1 || k > c->last_k) return fail(QWEN_E_ARG, "k exceeds the candidates kept by the last step");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpyAsync(values_host, c->top_v, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaMemcpyAsync(ids_host, c->top_i, (size_t)k * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return QWEN_OK;
+}
+
+extern "C" int qwen_debug_capture(qwen_t* c, int enable) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    CU(cudaSetDevice(c->device));
+    if (enable && !c->params.dbg_resid) CU(cudaMalloc(&c->params.dbg_resid, (size_t)N_LAYERS * DIM * sizeof(float)));
+    if (!enable && c->params.dbg_resid) { CU(cudaFree(c->params.dbg_resid)); c->params.dbg_resid = nullptr; }
+    return QWEN_OK;
+}
+
+extern "C" int qwen_debug_read(qwen_t* c, float* resid, float* qkv) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    CU(cudaSetDevice(c->device));
+    if (resid) {
+        if (!c->params.dbg_resid) return fail(QWEN_E_STATE, "capture not enabled");
+        CU(cudaMemcpy(resid, c->params.dbg_resid, (size_t)N_LAYERS * DIM * sizeof(float), cudaMemcpyDeviceToHost));
+    }
+    if (qkv) CU(cudaMemcpy(qkv, c->qkv, (size_t)N_LAYERS * 4096 * sizeof(float), cudaMemcpyDeviceToHost));
+    return QWEN_OK;
+}
+
+extern "C" int qwen_debug_chunk_counts(qwen_t* c, int* out, int max_ctas) {
+    if (!c || !out) return fail(QWEN_E_ARG, "NULL argument");
+    if (max_ctas < c->nsm) return fail(QWEN_E_ARG, "buffer too small");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpy(out, c->chunk_count, (size_t)2 * c->nsm * sizeof(int), cudaMemcpyDeviceToHost));
+    return c->nsm;
+}
+
+// ---------------------------------------------------------------------------
+// isolated GEMV
+// ---------------------------------------------------------------------------
+extern "C" int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* stream) {
+    if (!W || !x || !y) return fail(QWEN_E_ARG, "NULL argument");
+    if (n <= 0 || k <= 0 || k % 256 != 0 || k > 4096) return fail(QWEN_E_ARG, "k must be a positive multiple of 256, <= 4096");
+    if (((uintptr_t)W | (uintptr_t)x) & 15) return fail(QWEN_E_ARG, "W and x must be 16-byte aligned");
+    static thread_local int attr_dev = -1;
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (attr_dev != dev) {
+        CU(cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmemBytes));
+        attr_dev = dev;
+    }
+    static uint32_t* err_flag[64] = {nullptr};
+    if (dev < 64 && !err_flag[dev]) {
+        CU(cudaMalloc(&err_flag[dev], sizeof(uint32_t)));
+        CU(cudaMemset(err_flag[dev], 0, sizeof(uint32_t)));
+    }
+    int nsm = 0;
+    CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = n < nsm ? n : nsm;
+    gemv_bf16_kernel<<<grid, kThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
+                                                                                err_flag[dev < 64 ? dev : 0]);
+    CU(cudaGetLastError());
+    return QWEN_OK;
+}
