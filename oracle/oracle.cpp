@@ -429,7 +429,10 @@ int oracle_sample(const float* logits, int n, float temperature, float topp, int
     std::vector<PI> pi(n);
     for (int i = 0; i < n; i++) { pi[i].p = logits[i]; pi[i].i = i; }
     int nc = top_k < n ? top_k : n;
-    hoare_select(pi.data(), n, nc);
+    // With nc == n the reference's quick_select reads its pivot one past the end
+    // (sampler.h:63 with k = n) and does not terminate; every entry is a
+    // candidate then, kept in index order.
+    if (nc < n) hoare_select(pi.data(), n, nc);
     if (order_mode == 1) {
         std::sort(pi.begin(), pi.begin() + nc, [](const PI& a, const PI& b) { return a.p > b.p || (a.p == b.p && a.i < b.i); });
     }

@@ -86,7 +86,9 @@ extern "C" int qwen_sample_host(const float* logits, int n, const qwen_sampling_
     std::vector<Cand> c(n);
     for (int i = 0; i < n; i++) { c[i].p = logits[i]; c[i].i = i; }
     const int nc = top_k < n ? top_k : n;
-    select_top(c.data(), n, nc);
+    // top_k >= n: every entry is a candidate, in index order (the reference's
+    // quick_select would read its pivot past the end for k == n, sampler.h:63).
+    if (nc < n) select_top(c.data(), n, nc);
     *token_out = draw(c.data(), nc, sp->temperature, sp->topp, rng, true);
     return QWEN_OK;
 }
