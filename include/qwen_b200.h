@@ -104,6 +104,12 @@ float* qwen_host_logits(qwen_t* ctx);
 /* Device pointer to the fp32 logits of the last forward / decode step. */
 const float* qwen_device_logits(qwen_t* ctx);
 
+/* Copy the fp32 logits of the last forward / decode / generate step (the rows
+ * this handle serves: all VOCAB_SIZE, or its vocabulary shard) to host memory;
+ * returns the number of floats copied.  The reference's forward() hands these
+ * back every call (qwen_model.cuh:848); here the copy is on request. */
+int qwen_read_logits(qwen_t* ctx, float* logits_host);
+
 /* forward(token, pos) followed by sample() on the device (main.cu:144-145 with
  * sampler.h:120-175): *next_token receives the sampled id and *rng_state the
  * advanced xorshift64* state.  Only 4 + 8 bytes come back to the host.

@@ -403,7 +403,7 @@ extern "C" int qwen_decode_step(qwen_t* c, int token, int pos, const qwen_sampli
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
     CU(cudaSetDevice(c->device));
-    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, 0);
+    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, kFlagWriteLogits);
     CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
     if ((rc = launch_decode(c)) != QWEN_OK) return rc;
     CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
@@ -426,7 +426,7 @@ extern "C" int qwen_generate(qwen_t* c, int token, int pos, int n_steps, const q
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
     CU(cudaSetDevice(c->device));
-    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, 0);
+    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, kFlagWriteLogits);
     CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
     CU(cudaMemsetAsync(&c->d_out->n_done, 0, sizeof(int), c->stream));
     for (int i = 0; i < n_steps; i++)
@@ -469,6 +469,15 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     if ((rc = check_step(c)) != QWEN_OK) return rc;
     c->cached = pos0 + n;
     return QWEN_OK;
+}
+
+extern "C" int qwen_read_logits(qwen_t* c, float* logits_host) {
+    if (!c || !logits_host) return fail(QWEN_E_ARG, "NULL argument");
+    CU(cudaSetDevice(c->device));
+    const int n = c->params.lm_end - c->params.lm_begin;
+    CU(cudaMemcpyAsync(logits_host, c->logits + c->params.lm_begin, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    return n;
 }
 
 extern "C" int qwen_set_vocab_shard(qwen_t* c, int row_begin, int row_end) {

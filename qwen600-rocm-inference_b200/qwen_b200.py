@@ -48,6 +48,7 @@ _SIGS = {
     "qwen_forward": (_c.c_int, [_P, _c.c_int, _c.c_int, _P]),
     "qwen_host_logits": (_P, [_P]),
     "qwen_device_logits": (_P, [_P]),
+    "qwen_read_logits": (_c.c_int, [_P, _P]),
     "qwen_decode_step": (_c.c_int, [_P, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _c.POINTER(_c.c_int)]),
     "qwen_generate": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _P]),
     "qwen_prefill": (_c.c_int, [_P, _P, _c.c_int, _c.c_int, _P]),
@@ -203,6 +204,14 @@ class Engine:
     def forward_into(self, token, pos, out):
         """forward with the logits copied straight into `out` (float32 host array)."""
         _check(self._lib.qwen_forward(self._h, int(token), int(pos), _ptr(out)))
+
+    def read_logits(self):
+        """fp32 logits of the last step (all rows this handle serves)."""
+        out = np.zeros(VOCAB_SIZE, dtype=np.float32)
+        n = self._lib.qwen_read_logits(self._h, _ptr(out))
+        if n < 0:
+            _check(n)
+        return out[:n]
 
     def device_logits_ptr(self):
         return self._lib.qwen_device_logits(self._h)

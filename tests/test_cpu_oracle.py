@@ -1,0 +1,129 @@
+"""The oracle pinned against the reference's own code, and the host samplers
+(CPU only).
+
+* sampler: the oracle's restatement of sample() (sampler.h:27-175) and the
+  product's host sampler must reproduce the reference's own tokens and RNG
+  states (golden/sampler_cases.json, made by the reference's compiled sampler.h).
+* forward: the oracle's bf16-faithful mode must track the reference's own CUDA
+  forward() (golden/ref_forward_seed0.npz, made on a B200 from the reference's
+  qwen_model.cuh) on the seed-0 synthetic checkpoint.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, rel_rms
+
+VOCAB = 151936
+
+
+def _cases():
+    return json.load(open(os.path.join(GOLDEN, "sampler_cases.json")))["cases"]
+
+
+def test_oracle_sampler_matches_reference_golden(O):
+    import make_golden as M
+    for c in _cases():
+        lg = M.sampler_logits(c["logit_seed"], c["scale"], c["bf16"])
+        rng = c["rng"]
+        for tok, st in c["draws"]:
+            t, rng = O.sample(lg, c["temperature"], c["topp"], c["top_k"], rng, order_mode=0)
+            assert (t, rng) == (tok, st), c
+
+
+def test_host_sampler_matches_reference_golden(qb):
+    import make_golden as M
+    for c in _cases():
+        lg = M.sampler_logits(c["logit_seed"], c["scale"], c["bf16"])
+        sp = qb.Sampling(c["temperature"], c["topp"], c["top_k"])
+        rng = c["rng"]
+        for tok, st in c["draws"]:
+            t, rng = qb.sample_host(lg, sp, rng)
+            assert (t, rng) == (tok, st), c
+
+
+def test_oracle_sampler_matches_reference_live(O):
+    """More seeds against the reference's compiled sampler.h when it is built here."""
+    import ctypes
+    L = O.ref_sampler()
+    if L is None:
+        pytest.skip("oracle/_ref/libref_sampler.so not built (no reference tree)")
+    g = np.random.default_rng(123)
+    for i in range(40):
+        lg = (g.standard_normal(VOCAB) * g.uniform(0.3, 3.0)).astype(np.float32)
+        T = float(g.choice([0.0, 0.3, 0.6, 1.0, 1.5]))
+        p = float(g.choice([0.0, 0.5, 0.9, 0.95, 1.0]))
+        k = int(g.choice([1, 2, 5, 20, 50, 64, 100]))
+        seed = int(g.integers(1, 2 ** 63))
+        r = ctypes.c_ulonglong(seed)
+        want = L.ref_sample(lg.ctypes.data, T, p, k, ctypes.byref(r))
+        got, st = O.sample(lg, T, p, k, seed, order_mode=0)
+        assert (got, st) == (want, r.value), (i, T, p, k)
+
+
+def test_top_k_zero_terminates(O, qb):
+    """top_k = 0 (whole vocabulary): both restatements finish and agree."""
+    lg = (np.random.default_rng(5).standard_normal(VOCAB) * 0.64).astype(np.float32)
+    a = O.sample(lg, 0.6, 0.95, 0, 99, order_mode=0)
+    b = qb.sample_host(lg, qb.Sampling(0.6, 0.95, 0), 99)
+    assert a == b
+
+
+def test_candidate_merge_matches_full_vocab_sampler(O, qb):
+    """qwen_sample_candidates on the union of per-shard top-k lists equals the
+    descending-order sampler on the full logits (the sharded head's merge)."""
+    g = np.random.default_rng(9)
+    for i in range(30):
+        lg = (g.standard_normal(VOCAB) * 0.64).astype(np.float32)
+        k = int(g.choice([1, 5, 20, 64]))
+        T = float(g.choice([0.0, 0.6, 1.0]))
+        p = float(g.choice([0.9, 0.95, 1.0]))
+        seed = int(g.integers(1, 2 ** 63))
+        want = O.sample(lg, T, p, k, seed, order_mode=1)
+        vals, ids = [], []
+        for s in np.array_split(np.arange(VOCAB), 4):
+            top = s[np.argsort(-lg[s], kind="stable")[:k]]
+            vals.append(lg[top]); ids.append(top)
+        got = qb.sample_candidates(np.concatenate(vals), np.concatenate(ids), qb.Sampling(T, p, k), seed)
+        assert got == want
+
+
+def test_rope_angles_follow_reference_formula(O):
+    for pos in (0, 1, 17, 1023, 4095, 8191):
+        for j in (0, 1, 31, 63):
+            freq = np.float32(1.0) / np.power(np.float32(1e6), np.float32(2 * j) / np.float32(128))
+            a = np.float32(pos) * freq
+            c, s = O.rope_cs(pos, j)
+            assert abs(c - np.cos(np.float64(a))) < 2e-6 and abs(s - np.sin(np.float64(a))) < 2e-6
+
+
+def test_oracle_forward_tracks_reference_cuda(O, checkpoint):
+    """Oracle (bf16-faithful and fp32 modes) vs the reference's own CUDA
+    forward on the same checkpoint and tokens."""
+    path = os.path.join(GOLDEN, "ref_forward_seed0.npz")
+    if not os.path.exists(path):
+        pytest.skip("golden/ref_forward_seed0.npz not generated yet")
+    G = np.load(path)
+    toks, probe = G["tokens"], G["probe_idx"]
+    ob = O.Oracle(checkpoint, O.BF16, 64)
+    of = O.Oracle(checkpoint, O.FP32, 64)
+    agree_b = agree_f = 0
+    for pos, tok in enumerate(toks):
+        lb = ob.forward(int(tok), pos)
+        lf = of.forward(int(tok), pos)
+        ref_probe = G["probe_v"][pos]
+        # bf16-faithful restatement: same rounding points as the reference
+        assert np.abs(lb[probe] - ref_probe).max() < 0.05, pos
+        assert rel_rms(lb[probe], ref_probe) < 0.02, pos
+        # fp32 oracle: within the bf16 rounding the reference applies
+        assert np.abs(lf[probe] - ref_probe).max() < 0.08, pos
+        assert rel_rms(lf[probe], ref_probe) < 0.03, pos
+        top_ref = G["top_i"][pos][0]
+        agree_b += int(np.argmax(lb) == top_ref)
+        agree_f += int(np.argmax(lf) == top_ref)
+        s = G["stats"][pos]
+        assert abs(lb.astype(np.float64).sum() - s[0]) < 0.01 * np.sqrt(s[1]) * 50, pos
+    # the greedy choices agree almost everywhere (bf16 ties can flip a few)
+    assert agree_b >= len(toks) - 3 and agree_f >= len(toks) - 4, (agree_b, agree_f)
