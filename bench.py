@@ -1,0 +1,312 @@
+#!/usr/bin/env python
+"""Batch-1 decode benchmark of the Qwen3-0.6B engine (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+
+Workload: Qwen3-0.6B architecture, bf16 weights from the seed-0 synthetic
+checkpoint, a 1024-token seeded prompt, then greedy decode at context 1024-1279
+(positions are rewound to 1024 after every 256 tokens, so every step decodes at
+1K context).  A step is one decoded token: the whole forward (28 layers, LM
+head) plus the device sampler, one kernel launch.  Weights (1.19 GB) stream
+from HBM every step, far larger than the 126 MB L2.
+
+--impl mine       the engine.  value = device time of K chained steps from CUDA
+                  events (max over ranks; N ranks = N independent replicas);
+                  e2e = qwen_decode_step per token through the C ABI with the
+                  token in and out of pinned host memory.
+--impl reference  the reference's path on the host cores: the oracle's
+                  restatement of forward() in the reference's own bf16 rounding
+                  (qwen_model.cuh:772-851; the reference has no CPU forward) and
+                  the reference's own sampler.h compiled from its sources, all
+                  host threads, same workload.  Rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+
+METRIC = "batch-1 decode tok/s (Qwen3-0.6B bf16) and % of B200 HBM roofline; prefill tok/s"
+PROMPT_LEN = 1024
+WINDOW = 256
+WEIGHT_BYTES = 1_192_101_888      # weights read per token (28 layers + LM head + final norm + embedding row)
+KV_BYTES_PER_POS = 114_688        # 28 layers x (K + V) x 1024 bf16 per cached position
+CONFIG = {
+    "workload": "Qwen3-0.6B batch-1 greedy decode at 1K context: 1024-token seeded prompt, decode positions 1024-1279 "
+                "(rewound every 256 tokens), random-init bf16 weights (seed 0)",
+    "model": "Qwen3-0.6B architecture (28 layers, hidden 1024, 16/8 heads, vocab 151936)",
+    "batch": 1,
+    "prompt_tokens": PROMPT_LEN,
+    "decode_positions": [PROMPT_LEN, PROMPT_LEN + WINDOW - 1],
+    "l2": "inputs larger than L2: 1.19 GB of weights stream from HBM every step (L2 126 MB)",
+}
+
+
+def load_qb():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("qwen_b200", os.path.join(REPO, "qwen600-rocm-inference_b200", "qwen_b200.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+def measured_peak():
+    try:
+        d = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram read+write bytes per decode launch from the committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "decode_kernel_ncu.md")
+    try:
+        for line in open(p):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":")[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples (100 ms) of one GPU while the timed region runs."""
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device):
+        self.device = device
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.p is None:
+            return
+        time.sleep(0.15)
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) == 7:
+                self.rows.append(f)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower() == "active"})
+        pw = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows), "power_w_max": max(pw) if pw else None}
+
+
+def cpu_oracle_rate(ck, mode, budget_s, max_tokens, threads):
+    """Tokens/s of the oracle decoding at context 1024 on the host cores."""
+    import oracle_py as O
+    O.set_threads(threads)
+    o = O.Oracle(ck, mode, PROMPT_LEN + WINDOW + 1)
+    o.fill_kv(PROMPT_LEN)
+    ref_samp = O.ref_sampler()
+    rng = np.random.default_rng(11)
+    tok = int(rng.integers(0, 151936))
+    o.forward(tok, PROMPT_LEN)          # warm-up
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens and (n == 0 or time.perf_counter() - t0 < budget_s):
+        lg = o.forward(tok, PROMPT_LEN + 1 + (n % (WINDOW - 1)))
+        if ref_samp is not None:        # the reference's own sampler.h, argmax path
+            import ctypes
+            r = ctypes.c_ulonglong(1)
+            tok = ref_samp.ref_sample(lg.ctypes.data, 0.0, 0.95, 20, ctypes.byref(r))
+        else:
+            tok = O.sample(lg, 0.0, 0.95, 20, 1)[0]
+        n += 1
+    dt = time.perf_counter() - t0
+    o.close()
+    return n / dt, n, dt
+
+
+def ref_cuda_rate(ck, n_prompt=768, n_timed=200):
+    """The reference's own CUDA forward (cuBLAS, compiled for sm_100a) on this
+    GPU: forward + its host argmax sampler per token, positions below 1024 only
+    (its attention is valid there).  Informational."""
+    import ctypes
+    import oracle_py as O
+    L, S = O.ref_model(), O.ref_sampler()
+    if L is None or S is None:
+        return None
+    if L.ref_build(ck.encode()) != 0:
+        return None
+    lg = np.zeros(151936, dtype=np.float32)
+    toks = np.random.default_rng(5).integers(0, 151936, n_prompt).tolist()
+    for pos, t in enumerate(toks):
+        L.ref_forward(t, pos, lg.ctypes.data)
+    r = ctypes.c_ulonglong(1)
+    tok = S.ref_sample(lg.ctypes.data, 0.0, 0.95, 20, ctypes.byref(r))
+    t0 = time.perf_counter()
+    for i in range(n_timed):
+        L.ref_forward(tok, n_prompt + i, lg.ctypes.data)
+        tok = S.ref_sample(lg.ctypes.data, 0.0, 0.95, 20, ctypes.byref(r))
+    dt = time.perf_counter() - t0
+    L.ref_free()
+    return {"value": n_timed / dt, "unit": "tok/s", "positions": [n_prompt, n_prompt + n_timed - 1],
+            "note": "reference qwen_model.cuh + sampler.h built for sm_100a with cuBLAS, on this GPU; context below 1024 "
+                    "because its attention is wrong beyond 1024 positions"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    qb = load_qb()
+    ck = qb.default_checkpoint(0)
+    import oracle_py as O
+    threads = os.cpu_count() or 1
+    budget = min(240.0, max(20.0, 0.05 * args.steps))
+    rate, n, dt = cpu_oracle_rate(ck, O.BF16, budget, args.steps, threads)
+    sample = f"{n} decode tokens at context 1024-{1024 + min(n, WINDOW - 1)} ({dt:.1f} s), oracle bf16-faithful forward + reference sampler.h"
+    line = {"metric": METRIC, "value": rate, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus, "steps": n,
+            "warmup": 1, "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": CONFIG,
+            "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_mine(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    qb = load_qb()
+    ck = qb.default_checkpoint(0)
+    eng = qb.Engine(ck, local)
+    prompt = np.random.default_rng(1000 + rank).integers(0, 151936, PROMPT_LEN).tolist()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            t = torch.zeros(1, device="cuda")
+            dist.all_reduce(t)
+            torch.cuda.synchronize()
+
+    t0 = time.perf_counter()
+    eng.prefill(prompt, 0)
+    prefill_s = time.perf_counter() - t0
+    tok = prompt[-1]
+    # warm-up
+    w = max(args.warmup, 3)
+    toks, _, _ = eng.generate_timed(tok, PROMPT_LEN - 1, min(w, WINDOW))
+    tok = toks[-1]
+    # timed region: K chained steps in windows of 256 positions
+    barrier()
+    dev_ms, done, ctx_sum = 0.0, 0, 0.0
+    with Clocks(local) as clk:
+        wall0 = time.perf_counter()
+        while done < args.steps:
+            n = min(WINDOW, args.steps - done)
+            toks, _, ms = eng.generate_timed(tok, PROMPT_LEN, n)
+            dev_ms += ms
+            ctx_sum += n * (PROMPT_LEN + 1 + (n - 1) / 2.0)
+            tok = toks[-1]
+            done += n
+        barrier()
+        wall = time.perf_counter() - wall0
+    t = torch.tensor([dev_ms], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    # e2e: one qwen_decode_step per token, token in / token out through pinned host memory
+    n_e2e = min(args.steps, 512)
+    barrier()
+    e0 = time.perf_counter()
+    for i in range(n_e2e):
+        tok, _ = eng.decode_step(tok, PROMPT_LEN + (i % WINDOW))
+    barrier()
+    e2e_s = time.perf_counter() - e0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        ms_step = max_ms / args.steps
+        ctx = ctx_sum / args.steps
+        bytes_step = WEIGHT_BYTES + KV_BYTES_PER_POS * ctx
+        achieved = bytes_step / (ms_step * 1e-3) / 1e9
+        line = {"metric": METRIC, "value": world * args.steps / (max_ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": w, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": dict(CONFIG, parallelism=f"{world} independent replicas" if world > 1 else "single GPU"),
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                             "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                             "traffic": profiled_traffic(), "algorithmic_bytes_per_step": bytes_step,
+                             "kernel": "qb::decode_kernel (one launch per token)"},
+                "e2e": {"value": world * n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 32,
+                        "steps": n_e2e, "call": "qwen_decode_step"},
+                "gpu_launches": args.steps,
+                "clocks": clk.summary(),
+                "wall_s_timed_region": wall,
+                "prefill": {"value": PROMPT_LEN / prefill_s, "unit": "tok/s", "tokens": PROMPT_LEN,
+                            "path": "one decode-kernel launch per prompt position, LM head skipped (qwen_prefill)"}}
+        if world == 1:
+            import oracle_py as O
+            threads = os.cpu_count() or 1
+            rate, n, dt = cpu_oracle_rate(ck, O.FP32, 15.0, 400, threads)
+            line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                                    "sample": f"{n} decode tokens at context 1024 ({dt:.1f} s), fp32 oracle, {threads} threads"}
+            eng.close()
+            torch.cuda.empty_cache()
+            try:
+                line["reference_cuda_b200"] = ref_cuda_rate(ck)
+            except Exception as e:   # informational only
+                line["reference_cuda_b200"] = {"unavailable": str(e)[:200]}
+        print(json.dumps(line), flush=True)
+    else:
+        eng.close()
+    if dist is not None:
+        barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2048)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mine(args)
+
+
+if __name__ == "__main__":
+    main()

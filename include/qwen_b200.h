@@ -123,6 +123,12 @@ int qwen_decode_step(qwen_t* ctx, int token, int pos, const qwen_sampling_t* sp,
 int qwen_generate(qwen_t* ctx, int token, int pos, int n_steps, const qwen_sampling_t* sp,
                   unsigned long long* rng_state, int* tokens_out);
 
+/* qwen_generate with the n_steps launches bracketed by CUDA events on the
+ * handle's stream (synchronised on both sides); *device_ms receives the
+ * elapsed device time.  Used by the benchmark. */
+int qwen_generate_timed(qwen_t* ctx, int token, int pos, int n_steps, const qwen_sampling_t* sp,
+                        unsigned long long* rng_state, int* tokens_out, float* device_ms);
+
 /* Prompt ingestion: positions pos0 .. pos0+n-1 of `tokens` enter the KV cache
  * (no reference counterpart: the reference loops forward() per prompt
  * position, main.cu:141-145).  If logits_host is non-NULL it receives the

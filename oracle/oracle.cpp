@@ -259,6 +259,28 @@ int oracle_get_threads(void) {
 
 // Record the residual stream after every layer into dump[LAYERS][DIM] (NULL = off).
 void oracle_set_dump(void* h, float* dump) { ((Oracle*)h)->dump = dump; }
+// Fill K/V cache positions [0, n) with seeded N(0, 1) values rounded to bf16:
+// lets a timing run decode at context n without computing n prompt positions
+// first (the per-token arithmetic is the same; the cache contents differ).
+int oracle_fill_kv(void* h, int n, unsigned long long seed) {
+    Oracle* o = (Oracle*)h;
+    if (!o || n < 0 || n > o->max_seq) return -1;
+    for (int l = 0; l < LAYERS; l++)
+        for (int t = 0; t < n; t++)
+            for (int j = 0; j < KVD; j++) {
+                unsigned long long z = seed + ((unsigned long long)((l * o->max_seq + t) * KVD + j) << 1);
+                for (int r = 0; r < 2; r++) {
+                    z += 0x9E3779B97F4A7C15ull;
+                    unsigned long long y = z;
+                    y = (y ^ (y >> 30)) * 0xBF58476D1CE4E5B9ull; y = (y ^ (y >> 27)) * 0x94D049BB133111EBull; y ^= y >> 31;
+                    const float u = ((float)(y >> 40) + 0.5f) / 16777216.0f - 0.5f;   // uniform, variance 1/12
+                    const float v = rbf(u * 3.4641016f);
+                    (r == 0 ? o->kc : o->vc)[((size_t)l * o->max_seq + t) * KVD + j] = v;
+                }
+            }
+    return 0;
+}
+
 void oracle_set_dump_qkv(void* h, float* dump) { ((Oracle*)h)->dump_qkv = dump; }
 void oracle_set_float_accum(void* h, int on) { ((Oracle*)h)->float_accum = on; }
 

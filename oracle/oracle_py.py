@@ -29,6 +29,7 @@ def lib():
         L.oracle_set_dump.argtypes = [vp, vp]
         L.oracle_set_dump_qkv.argtypes = [vp, vp]
         L.oracle_set_float_accum.argtypes = [vp, c.c_int]
+        L.oracle_fill_kv.argtypes = [vp, c.c_int, c.c_ulonglong]
         L.oracle_set_threads.argtypes = [c.c_int]
         L.oracle_get_threads.restype = c.c_int
         L.oracle_gemv_bf16.argtypes = [vp, vp, vp, c.c_int, c.c_int]
@@ -62,6 +63,11 @@ class Oracle:
             raise RuntimeError(f"oracle_open failed ({rc})")
         self._h = h
         self.mode = mode
+
+    def fill_kv(self, n, seed=1):
+        """Populate cache positions [0, n) with seeded values (timing runs only)."""
+        if lib().oracle_fill_kv(self._h, int(n), int(seed)) != 0:
+            raise RuntimeError("oracle_fill_kv failed")
 
     def set_float_accum(self, on):
         lib().oracle_set_float_accum(self._h, 1 if on else 0)

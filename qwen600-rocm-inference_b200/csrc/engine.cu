@@ -442,6 +442,45 @@ extern "C" int qwen_generate(qwen_t* c, int token, int pos, int n_steps, const q
     return QWEN_OK;
 }
 
+extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, const qwen_sampling_t* sp,
+                                   unsigned long long* rng_state, int* tokens_out, float* device_ms) {
+    if (!c || !tokens_out || !device_ms) return fail(QWEN_E_ARG, "NULL argument");
+    if (n_steps <= 0) return fail(QWEN_E_ARG, "n_steps must be positive");
+    if (token < 0 || token >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
+    if (pos < 0 || (long long)pos + n_steps > SEQ_LEN) return fail(QWEN_E_ARG, "pos + n_steps exceeds SEQ_LEN");
+    if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
+    int rc = check_sampling(sp);
+    if (rc != QWEN_OK) return rc;
+    CU(cudaSetDevice(c->device));
+    cudaEvent_t e0, e1;
+    CU(cudaEventCreate(&e0));
+    if (cudaEventCreate(&e1) != cudaSuccess) { cudaEventDestroy(e0); return fail(QWEN_E_CUDA, "event creation failed"); }
+    fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, 0);
+    rc = QWEN_OK;
+    if (cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(&c->d_out->n_done, 0, sizeof(int), c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess || cudaEventRecord(e0, c->stream) != cudaSuccess)
+        rc = fail(QWEN_E_CUDA, "timed generate setup failed");
+    for (int i = 0; i < n_steps && rc == QWEN_OK; i++) rc = launch_decode(c);
+    if (rc == QWEN_OK && (cudaEventRecord(e1, c->stream) != cudaSuccess || cudaEventSynchronize(e1) != cudaSuccess))
+        rc = fail(QWEN_E_CUDA, "timed generate failed");
+    if (rc == QWEN_OK) {
+        cudaEventElapsedTime(device_ms, e0, e1);
+        if (cudaMemcpyAsync(c->h_tokens, c->tokens, (size_t)n_steps * sizeof(int), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+            cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+            cudaStreamSynchronize(c->stream) != cudaSuccess)
+            rc = fail(QWEN_E_CUDA, "timed generate readback failed");
+    }
+    cudaEventDestroy(e0); cudaEventDestroy(e1);
+    if (rc != QWEN_OK) return rc;
+    c->last_k = (!sp || sp->temperature == 0.0f || sp->top_k == 1) ? 1 : sp->top_k;
+    if ((rc = check_step(c)) != QWEN_OK) return rc;
+    memcpy(tokens_out, c->h_tokens, (size_t)n_steps * sizeof(int));
+    if (rng_state) *rng_state = c->h_out->rng;
+    c->cached = pos + n_steps;
+    return QWEN_OK;
+}
+
 extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float* logits_host) {
     if (!c || !tokens) return fail(QWEN_E_ARG, "NULL argument");
     if (n <= 0 || pos0 < 0 || (long long)pos0 + n > SEQ_LEN) return fail(QWEN_E_ARG, "prompt does not fit [0, SEQ_LEN)");

@@ -51,6 +51,8 @@ _SIGS = {
     "qwen_read_logits": (_c.c_int, [_P, _P]),
     "qwen_decode_step": (_c.c_int, [_P, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _c.POINTER(_c.c_int)]),
     "qwen_generate": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _P]),
+    "qwen_generate_timed": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _P,
+                                       _c.POINTER(_c.c_float)]),
     "qwen_prefill": (_c.c_int, [_P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_cached_positions": (_c.c_int, [_P]),
     "qwen_set_vocab_shard": (_c.c_int, [_P, _c.c_int, _c.c_int]),
@@ -227,6 +229,15 @@ class Engine:
         r = ctypes.c_ulonglong(rng)
         _check(self._lib.qwen_generate(self._h, int(token), int(pos), int(n_steps), ctypes.byref(sampling), ctypes.byref(r), _ptr(out)))
         return out.tolist(), r.value
+
+    def generate_timed(self, token, pos, n_steps, sampling=GREEDY, rng=0):
+        """generate() plus the device time (ms) of its launches, from CUDA events."""
+        out = np.zeros(n_steps, dtype=np.int32)
+        r = ctypes.c_ulonglong(rng)
+        ms = ctypes.c_float()
+        _check(self._lib.qwen_generate_timed(self._h, int(token), int(pos), int(n_steps), ctypes.byref(sampling), ctypes.byref(r),
+                                             _ptr(out), ctypes.byref(ms)))
+        return out.tolist(), r.value, ms.value
 
     def prefill(self, tokens, pos0=0, want_logits=False):
         tk = np.ascontiguousarray(tokens, dtype=np.int32)
