@@ -140,6 +140,7 @@ struct Oracle {
     Layer layer[LAYERS];
     std::vector<float> kc, vc;        // [layer][max_seq][KVD] (bf16-valued unless mode 2)
     int float_accum = 0;              // perturbation: single float accumulator in matvec
+    int ref_softmax = 0;              // reproduce the reference's softmax reduction (see ref_softmax_rows)
     float* dump = nullptr;            // optional: residual after each layer [LAYERS][DIM]
     float* dump_qkv = nullptr;        // optional: raw q|k|v projections [LAYERS][QD+2*KVD]
 };
@@ -180,6 +181,31 @@ void rmsnorm(const float* x, const uint16_t* w, float* y, int n, int mode) {
         float r = 1.0f / sqrtf(fmaf(ss, 1.0f / (float)n, EPS));
         for (int j = 0; j < n; j++) y[j] = rbf((x[j] * r) * bf2f(w[j]));
     }
+}
+
+// The reference's softmax over len = pos + 1 scores (qwen_model.cuh:486-545):
+// len <= 32 runs one thread per head (softmax_kernel_simple, :452-481); longer
+// rows run softmax_kernel_optimized (:384-449) with block_size = min(1024, len)
+// threads whose shared-memory tree reductions (:412-419, :433-440) halve
+// `s` from block_size / 2 and so drop partial results whenever block_size is
+// not a power of two.  This restates that arithmetic, dropped terms included,
+// so the oracle can be compared with the reference's own output.
+void ref_softmax_row(float* sc, int len) {
+    if (len <= 32) {
+        float m = -INFINITY; for (int i = 0; i < len; i++) m = std::max(m, sc[i]);
+        float sum = 0.f; for (int i = 0; i < len; i++) { sc[i] = expf(sc[i] - m); sum += sc[i]; }
+        const float inv = 1.0f / sum; for (int i = 0; i < len; i++) sc[i] *= inv;
+        return;
+    }
+    const int bs = std::min(1024, len);
+    std::vector<float> part(bs);
+    for (int t = 0; t < bs; t++) { float m = -INFINITY; for (int i = t; i < len; i += bs) if (sc[i] > m) m = sc[i]; part[t] = m; }
+    for (int st = bs / 2; st > 0; st >>= 1) for (int t = 0; t < st; t++) if (part[t + st] > part[t]) part[t] = part[t + st];
+    const float m = part[0];
+    for (int t = 0; t < bs; t++) { float a = 0.f; for (int i = t; i < len; i += bs) { sc[i] = expf(sc[i] - m); a += sc[i]; } part[t] = a; }
+    for (int st = bs / 2; st > 0; st >>= 1) for (int t = 0; t < st; t++) part[t] += part[t + st];
+    const float inv = 1.0f / part[0];
+    for (int i = 0; i < len; i++) sc[i] *= inv;
 }
 
 }  // namespace
@@ -283,6 +309,8 @@ int oracle_fill_kv(void* h, int n, unsigned long long seed) {
 
 void oracle_set_dump_qkv(void* h, float* dump) { ((Oracle*)h)->dump_qkv = dump; }
 void oracle_set_float_accum(void* h, int on) { ((Oracle*)h)->float_accum = on; }
+// bf16 mode only: use the reference's softmax reduction (ref_softmax_row).
+void oracle_set_ref_softmax(void* h, int on) { ((Oracle*)h)->ref_softmax = on; }
 
 // One decode position (qwen_model.cuh:772-851).  Positions must arrive in order
 // 0..pos, as in the reference.  logits: VOCAB floats.  xfinal (optional): the
@@ -359,8 +387,11 @@ int oracle_forward(void* h, int token, int pos, float* logits, float* xfinal) {
                     att[hh * HD + d] = (float)a;
                 }
             } else {
-                float sum = 0; for (int t = 0; t < L; t++) { s[t] = expf(s[t] - m); sum += s[t]; }
-                float inv = 1.0f / sum; for (int t = 0; t < L; t++) s[t] *= inv;
+                if (o->ref_softmax) ref_softmax_row(s.data(), L);
+                else {
+                    float sum = 0; for (int t = 0; t < L; t++) { s[t] = expf(s[t] - m); sum += s[t]; }
+                    float inv = 1.0f / sum; for (int t = 0; t < L; t++) s[t] *= inv;
+                }
                 for (int d = 0; d < HD; d++) {
                     float a = 0; for (int t = 0; t < L; t++) a = fmaf(s[t], Vl[(size_t)t * KVD + g * HD + d], a);
                     att[hh * HD + d] = rbf(a);

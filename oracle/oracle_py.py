@@ -30,6 +30,7 @@ def lib():
         L.oracle_set_dump_qkv.argtypes = [vp, vp]
         L.oracle_set_float_accum.argtypes = [vp, c.c_int]
         L.oracle_fill_kv.argtypes = [vp, c.c_int, c.c_ulonglong]
+        L.oracle_set_ref_softmax.argtypes = [vp, c.c_int]
         L.oracle_set_threads.argtypes = [c.c_int]
         L.oracle_get_threads.restype = c.c_int
         L.oracle_gemv_bf16.argtypes = [vp, vp, vp, c.c_int, c.c_int]
@@ -68,6 +69,10 @@ class Oracle:
         """Populate cache positions [0, n) with seeded values (timing runs only)."""
         if lib().oracle_fill_kv(self._h, int(n), int(seed)) != 0:
             raise RuntimeError("oracle_fill_kv failed")
+
+    def set_ref_softmax(self, on):
+        """bf16 mode: reproduce the reference's softmax reduction, dropped terms included."""
+        lib().oracle_set_ref_softmax(self._h, 1 if on else 0)
 
     def set_float_accum(self, on):
         lib().oracle_set_float_accum(self._h, 1 if on else 0)
