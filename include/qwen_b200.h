@@ -181,6 +181,21 @@ int qwen_debug_read(qwen_t* ctx, float* resid, float* qkv);
  * (qwen_model.cuh:706-757) with alpha = 1, beta = 0. */
 int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* stream);
 
+/* qwen_gemv_bf16 without any device allocation.  No counterpart in the
+ * reference: it is for callers that must not call cudaMalloc, such as code
+ * that runs while a stream is being captured into a CUDA graph, or code inside
+ * a framework whose memory pool already holds the device's memory.  (The
+ * plain entry point allocates its 4-byte device scratch word on its first call
+ * per device.)  The kernel's scratch lives in a 256-byte file-scope device
+ * array that every GPU loading the library holds until exit; this call uses
+ * one word of it and clears it before each launch.  Same shapes and
+ * arguments as qwen_gemv_bf16: k must be a positive multiple of 256 and at
+ * most 4096 (larger k is rejected with QWEN_E_ARG).  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  All calls
+ * share the one array, so calls whose kernels overlap on the GPU race on it. */
+int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

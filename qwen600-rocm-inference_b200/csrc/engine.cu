@@ -12,7 +12,9 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -589,6 +591,53 @@ extern "C" int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int 
     const int grid = n < nsm ? n : nsm;
     gemv_bf16_kernel<<<grid, kThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
                                                                                 err_flag[dev < 64 ? dev : 0]);
+    CU(cudaGetLastError());
+    return QWEN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// isolated GEMV without allocation
+// ---------------------------------------------------------------------------
+// qwen_gemv_bf16 obtains its device scratch (the kernel's error word) with
+// cudaMalloc on its first call on each device.  Some callers cannot allow
+// that: code that runs while a stream is being captured, or inside a framework
+// whose caching allocator already holds the device's memory.  This variant
+// keeps the scratch in a file-scope device array instead.  Host code must not
+// pass the array's name to a kernel (on the host it is only a stand-in for the
+// symbol); the device address comes from cudaGetSymbolAddress, once per
+// device, on the first call made with that device current.
+constexpr int kGemvStaticScratchWords = 64;   // 256 bytes per device; the GEMV uses word 0
+static __device__ __align__(256) uint32_t g_gemv_static_scratch[kGemvStaticScratchWords];
+static std::atomic<uint32_t*> g_gemv_static_ptr[64];
+static std::mutex g_gemv_static_mu;
+
+extern "C" int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, void* stream) {
+    if (!W || !x || !y) return fail(QWEN_E_ARG, "NULL argument");
+    if (n <= 0 || k <= 0 || k % 256 != 0 || k > 4096)
+        return fail(QWEN_E_ARG, "qwen_gemv_bf16_static serves k a positive multiple of 256, at most 4096, and n > 0");
+    if (((uintptr_t)W | (uintptr_t)x) & 15) return fail(QWEN_E_ARG, "W and x must be 16-byte aligned");
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(QWEN_E_ARG, "device index beyond 63");
+    uint32_t* scratch = g_gemv_static_ptr[dev].load();
+    if (!scratch) {   // set-up, once per device, with that device current; allocates nothing
+        std::lock_guard<std::mutex> lk(g_gemv_static_mu);
+        scratch = g_gemv_static_ptr[dev].load();
+        if (!scratch) {
+            void* p = nullptr;
+            CU(cudaGetSymbolAddress(&p, g_gemv_static_scratch));
+            CU(cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmemBytes));
+            scratch = (uint32_t*)p;
+            g_gemv_static_ptr[dev].store(scratch);
+        }
+    }
+    int nsm = 0;
+    CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    // the array keeps the previous call's contents: the error word must start at zero
+    CU(cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream));
+    const int grid = n < nsm ? n : nsm;
+    gemv_bf16_kernel<<<grid, kThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
+                                                                                scratch);
     CU(cudaGetLastError());
     return QWEN_OK;
 }

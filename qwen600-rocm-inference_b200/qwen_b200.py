@@ -63,6 +63,7 @@ _SIGS = {
     "qwen_debug_capture": (_c.c_int, [_P, _c.c_int]),
     "qwen_debug_read": (_c.c_int, [_P, _P, _P]),
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
+    "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
 }
 
 _lib = None
@@ -161,6 +162,12 @@ def gemv_bf16(W_ptr, x_ptr, y_ptr, n, k, stream=0):
     """y = bf16(W x) on device pointers (ints)."""
     _check(load_library().qwen_gemv_bf16(ctypes.c_void_p(W_ptr), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n, k,
                                          ctypes.c_void_p(stream)))
+
+
+def gemv_bf16_static(W_ptr, x_ptr, y_ptr, n, k, stream=0):
+    """y = bf16(W x) on device pointers, without any device allocation."""
+    _check(load_library().qwen_gemv_bf16_static(ctypes.c_void_p(W_ptr), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n, k,
+                                                ctypes.c_void_p(stream)))
 
 
 class Engine:
