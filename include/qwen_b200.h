@@ -167,11 +167,20 @@ int qwen_sample_candidates(const float* values, const int* ids, int n, const qwe
  * Returns the number of CTAs (or a negative status). No reference counterpart. */
 int qwen_debug_chunk_counts(qwen_t* ctx, int* out, int max_ctas);
 
-/* Keep a copy of the residual stream after every layer (enable = 1) for
- * qwen_debug_read; resid: N_LAYERS*DIM floats, qkv: N_LAYERS*4096 floats of raw
- * q|k|v projections of the last launch (either may be NULL). */
+/* Residual stream after every layer (resid: N_LAYERS*DIM floats) and raw
+ * q|k|v projections (qkv: N_LAYERS*4096 floats) of the last launch (either may
+ * be NULL).  qwen_debug_capture is kept for callers that enable capture first;
+ * the values are always retained. */
 int qwen_debug_capture(qwen_t* ctx, int enable);
 int qwen_debug_read(qwen_t* ctx, float* resid, float* qkv);
+
+/* Stage tracing: with tracing enabled every decode launch records %globaltimer
+ * (ns) stamps per CTA at each stage boundary; qwen_trace_read copies
+ * n_ctas * stride stamps of the last launch and returns their count.  The
+ * stride and the meaning of each slot are documented in
+ * csrc/decode_kernel.cuh (kTraceStride). */
+int qwen_trace_enable(qwen_t* ctx, int enable);
+int qwen_trace_read(qwen_t* ctx, unsigned long long* out, int max_entries);
 
 /* ---- isolated kernels ---------------------------------------------------- */
 

@@ -150,14 +150,6 @@ __global__ void pack_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __rest
         wo_g[((size_t)g * DIM + r) * 256 + cc] = wo[i];
     }
 }
-// Wd [DIM][HIDDEN] -> Wd^T [HIDDEN][DIM].
-__global__ void pack_wd_kernel(const uint16_t* __restrict__ wd, uint16_t* __restrict__ wdt) {
-    const size_t n = (size_t)DIM * HIDDEN_DIM;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int j = (int)(i / DIM), r = (int)(i % DIM);
-        wdt[i] = wd[(size_t)r * HIDDEN_DIM + j];
-    }
-}
 
 // RoPE cos/sin of every position, computed the way the reference writes it
 // (qwen_model.cuh:331-334): freq = 1/powf(theta, 2j/128), angle = pos*freq in
@@ -187,8 +179,11 @@ struct qwen_ctx {
     int nsm = 0;
     cudaStream_t stream = nullptr;
     uint8_t* wblock = nullptr;
-    uint16_t *wo_g = nullptr, *wd_t = nullptr, *kc = nullptr, *vc = nullptr;
-    float *rope = nullptr, *qkv = nullptr, *part = nullptr, *ybuf = nullptr, *acc = nullptr, *logits = nullptr;
+    uint16_t *wo_g = nullptr, *kc = nullptr, *vc = nullptr;
+    float *rope = nullptr, *logits = nullptr;
+    uint64_t* xchg = nullptr;      // all exchange words (one allocation)
+    size_t xchg_words = 0;
+    unsigned long long launches = 0;   // since the last reset (bounds the 32-bit sequence tag)
     float *cand_v = nullptr, *top_v = nullptr;
     int *cand_i = nullptr, *top_i = nullptr, *prompt = nullptr, *tokens = nullptr, *chunk_count = nullptr;
     uint32_t* ctr = nullptr;
@@ -207,8 +202,8 @@ static void ctx_free(qwen_t* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    if (c->params.dbg_resid) cudaFree(c->params.dbg_resid);
-    void* dev[] = {c->wblock, c->wo_g, c->wd_t, c->kc, c->vc, c->rope, c->qkv, c->part, c->ybuf, c->acc, c->logits,
+    if (c->params.trace) cudaFree(c->params.trace);
+    void* dev[] = {c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -219,9 +214,10 @@ static void ctx_free(qwen_t* c) {
 
 static int reset_device_state(qwen_t* c) {
     CU(cudaMemsetAsync(c->ctr, 0, (size_t)kNumCtr * kCtrStride * sizeof(uint32_t), c->stream));
-    CU(cudaMemsetAsync(c->acc, 0, (size_t)N_LAYERS * DIM * sizeof(float), c->stream));
+    CU(cudaMemsetAsync(c->xchg, 0, c->xchg_words * sizeof(uint64_t), c->stream));   // tag 0 is never current
+    c->launches = 0;
     StepOut o{};
-    o.epoch = 1;
+    o.seq = 1;
     *c->h_out = o;
     CU(cudaMemcpyAsync(c->d_out, c->h_out, sizeof(StepOut), cudaMemcpyHostToDevice, c->stream));
     CU(cudaStreamSynchronize(c->stream));
@@ -248,7 +244,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     qwen_t* c = new qwen_ctx();
     c->device = device;
     if (cudaDeviceGetAttribute(&c->nsm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "device query failed"); }
-    if (c->nsm < 8 * kMinGS || c->nsm > 8 * kMaxGS || (VOCAB_SIZE + c->nsm - 1) / c->nsm > kMaxLocalRows ||
+    if (c->nsm < kGroups * kMinGS || c->nsm > kGroups * kMaxGS || (VOCAB_SIZE + c->nsm - 1) / c->nsm > kMaxLocalRows ||
         (HIDDEN_DIM + c->nsm - 1) / c->nsm > kMaxMlpRows) {
         ctx_free(c); return fail(QWEN_E_UNSUPPORTED, "unsupported SM count " + std::to_string(c->nsm));
     }
@@ -265,15 +261,15 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     TRY(dalloc(&c->wblock, total));
     TRY(upload_checkpoint(path, m, c->wblock, c->stream));
     TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * DIM * Q_DIM));
-    TRY(dalloc(&c->wd_t, (size_t)N_LAYERS * DIM * HIDDEN_DIM));
     const size_t kv = (size_t)N_LAYERS * N_KV_HEADS * SEQ_LEN * HEAD_DIM;
     TRY(dalloc(&c->kc, kv));
     TRY(dalloc(&c->vc, kv));
     TRY(dalloc(&c->rope, (size_t)SEQ_LEN * HEAD_DIM));
-    TRY(dalloc(&c->qkv, (size_t)N_LAYERS * 4096));
-    TRY(dalloc(&c->part, (size_t)N_LAYERS * kGroups * kMaxGS * kPartStride));
-    TRY(dalloc(&c->ybuf, (size_t)N_LAYERS * kGroups * DIM));
-    TRY(dalloc(&c->acc, (size_t)N_LAYERS * DIM));
+    const size_t n_xw = (size_t)(N_LAYERS + 1) * DIM, n_qkv = (size_t)N_LAYERS * 4096,
+                 n_part = (size_t)N_LAYERS * kGroups * kMaxGS * kPartStride, n_y = (size_t)N_LAYERS * kGroups * DIM,
+                 n_h = (size_t)N_LAYERS * HIDDEN_DIM;
+    c->xchg_words = n_xw + n_qkv + n_part + n_y + n_h;
+    TRY(dalloc(&c->xchg, c->xchg_words));
     TRY(dalloc(&c->logits, (size_t)VOCAB_SIZE));
     TRY(dalloc(&c->cand_v, (size_t)c->nsm * kMaxCand));
     TRY(dalloc(&c->cand_i, (size_t)c->nsm * kMaxCand));
@@ -310,16 +306,22 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         P.in_ln[l] = W(li.in_ln); P.post_ln[l] = W(li.post_ln);
         P.wq[l] = W(li.q_proj); P.wk[l] = W(li.k_proj); P.wv[l] = W(li.v_proj);
         P.qn[l] = W(li.q_norm); P.kn[l] = W(li.k_norm);
-        P.wg[l] = W(li.gate); P.wu[l] = W(li.up);
+        P.wg[l] = W(li.gate); P.wu[l] = W(li.up); P.wd[l] = W(li.down);
         pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * DIM * Q_DIM);
-        pack_wd_kernel<<<1024, 256, 0, c->stream>>>(W(li.down), c->wd_t + (size_t)l * DIM * HIDDEN_DIM);
     }
     if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
-    P.wo_g = c->wo_g; P.wd_t = c->wd_t; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
-    P.qkv = c->qkv; P.part = c->part; P.ybuf = c->ybuf; P.acc = c->acc; P.logits = c->logits;
+    P.wo_g = c->wo_g; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
+    P.xw = c->xchg; P.qkvw = P.xw + n_xw; P.partw = P.qkvw + n_qkv; P.yw = P.partw + n_part; P.hw = P.yw + n_y;
+    P.logits = c->logits;
     P.cand_v = c->cand_v; P.cand_i = c->cand_i; P.top_v = c->top_v; P.top_i = c->top_i; P.ctr = c->ctr;
     P.in = c->d_in; P.out = c->d_out; P.tokens_out = c->tokens; P.tokens_cap = SEQ_LEN;
     P.lm_begin = 0; P.lm_end = VOCAB_SIZE;
+    // tuning knobs (environment, read once per handle): L2 prefetch lead in
+    // chunks, back-off in ns between polls of an exchange word
+    P.prefetch_chunks = 16;
+    P.poll_ns = 0;
+    if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
+    if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -333,6 +335,12 @@ extern "C" const float* qwen_device_logits(qwen_t* c) { return c ? c->logits : n
 extern "C" int qwen_cached_positions(const qwen_t* c) { return c ? c->cached : -1; }
 
 static int launch_decode(qwen_t* c) {
+    if (++c->launches >= 0xFFFFFF00ull) {   // the 32-bit exchange tag is about to wrap: start over
+        CU(cudaStreamSynchronize(c->stream));
+        const int rc = reset_device_state(c);
+        if (rc != QWEN_OK) return rc;
+        c->launches = 1;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c->nsm);
     cfg.blockDim = dim3(kThreads);
@@ -353,7 +361,10 @@ static int check_step(qwen_t* c) {
         const unsigned e = c->h_out->err; const int w = c->h_out->err_where;
         reset_device_state(c);
         c->cached = 0;
-        return fail(QWEN_E_TIMEOUT, "device wait expired (code " + std::to_string(e) + ", slot " + std::to_string(w) +
+        if (e & 24u)   // 8: invalid input token on device, 16: no finite logit to sample
+            return fail(QWEN_E_STATE, "non-finite logits or invalid chained token (code " + std::to_string(e) +
+                                          "); device state reset, KV cache invalidated");
+        return fail(QWEN_E_TIMEOUT, "device wait expired (code " + std::to_string(e) + ", where " + std::to_string(w) +
                                         "); device state reset, KV cache invalidated");
     }
     return QWEN_OK;
@@ -541,22 +552,48 @@ extern "C" int qwen_shard_topk(qwen_t* c, int k, float* values_host, int* ids_ho
 }
 
 extern "C" int qwen_debug_capture(qwen_t* c, int enable) {
-    if (!c) return fail(QWEN_E_ARG, "NULL handle");
-    CU(cudaSetDevice(c->device));
-    if (enable && !c->params.dbg_resid) CU(cudaMalloc(&c->params.dbg_resid, (size_t)N_LAYERS * DIM * sizeof(float)));
-    if (!enable && c->params.dbg_resid) { CU(cudaFree(c->params.dbg_resid)); c->params.dbg_resid = nullptr; }
-    return QWEN_OK;
+    // the residual stream and the projections of the last launch stay in the
+    // exchange buffers; nothing extra to keep
+    (void)enable;
+    return c ? QWEN_OK : fail(QWEN_E_ARG, "NULL handle");
 }
 
 extern "C" int qwen_debug_read(qwen_t* c, float* resid, float* qkv) {
     if (!c) return fail(QWEN_E_ARG, "NULL handle");
     CU(cudaSetDevice(c->device));
-    if (resid) {
-        if (!c->params.dbg_resid) return fail(QWEN_E_STATE, "capture not enabled");
-        CU(cudaMemcpy(resid, c->params.dbg_resid, (size_t)N_LAYERS * DIM * sizeof(float), cudaMemcpyDeviceToHost));
+    CU(cudaStreamSynchronize(c->stream));
+    auto take = [&](const uint64_t* src, size_t n, float* dst) -> int {
+        std::vector<uint64_t> w(n);
+        CU(cudaMemcpy(w.data(), src, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < n; i++) { const uint32_t u = (uint32_t)w[i]; memcpy(&dst[i], &u, 4); }
+        return QWEN_OK;
+    };
+    int rc = QWEN_OK;
+    if (resid) rc = take(c->params.xw + DIM, (size_t)N_LAYERS * DIM, resid);       // residual after layer l = x_{l+1}
+    if (rc == QWEN_OK && qkv) rc = take(c->params.qkvw, (size_t)N_LAYERS * 4096, qkv);
+    return rc;
+}
+
+extern "C" int qwen_trace_enable(qwen_t* c, int enable) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    CU(cudaSetDevice(c->device));
+    const size_t n = (size_t)c->nsm * kTraceStride;
+    if (enable && !c->params.trace) {
+        CU(cudaMalloc(&c->params.trace, n * sizeof(unsigned long long)));
+        CU(cudaMemset(c->params.trace, 0, n * sizeof(unsigned long long)));
     }
-    if (qkv) CU(cudaMemcpy(qkv, c->qkv, (size_t)N_LAYERS * 4096 * sizeof(float), cudaMemcpyDeviceToHost));
+    if (!enable && c->params.trace) { CU(cudaFree(c->params.trace)); c->params.trace = nullptr; }
     return QWEN_OK;
+}
+
+extern "C" int qwen_trace_read(qwen_t* c, unsigned long long* out, int max_entries) {
+    if (!c || !out) return fail(QWEN_E_ARG, "NULL argument");
+    if (!c->params.trace) return fail(QWEN_E_STATE, "tracing not enabled");
+    const int n = c->nsm * kTraceStride;
+    if (max_entries < n) return fail(QWEN_E_ARG, "buffer too small");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpy(out, c->params.trace, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    return n;
 }
 
 extern "C" int qwen_debug_chunk_counts(qwen_t* c, int* out, int max_ctas) {
@@ -589,7 +626,7 @@ extern "C" int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int 
     int nsm = 0;
     CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     const int grid = n < nsm ? n : nsm;
-    gemv_bf16_kernel<<<grid, kThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
+    gemv_bf16_kernel<<<grid, kGemvThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
                                                                                 err_flag[dev < 64 ? dev : 0]);
     CU(cudaGetLastError());
     return QWEN_OK;
@@ -636,7 +673,7 @@ extern "C" int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int 
     // the array keeps the previous call's contents: the error word must start at zero
     CU(cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream));
     const int grid = n < nsm ? n : nsm;
-    gemv_bf16_kernel<<<grid, kThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
+    gemv_bf16_kernel<<<grid, kGemvThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
                                                                                 scratch);
     CU(cudaGetLastError());
     return QWEN_OK;

@@ -17,6 +17,7 @@ struct __align__(16) GemvSmem {
     float part[2][kNCW];
 };
 constexpr size_t kGemvSmemBytes = (size_t)kSlots * kSlotBytes + sizeof(GemvSmem);
+constexpr int kGemvThreads = kNCT + 32;     // 16 consumer warps + one producer warp
 
 __host__ __device__ __forceinline__ int gemv_segs(int K) { return (K + 1023) / 1024; }
 __host__ __device__ __forceinline__ int gemv_rows_per_chunk(int K) {
@@ -24,7 +25,7 @@ __host__ __device__ __forceinline__ int gemv_rows_per_chunk(int K) {
     return a < b ? a : b;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kGemvThreads, 1)
 gemv_bf16_kernel(const uint16_t* __restrict__ W, const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int N, int K,
                  uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t smem[];

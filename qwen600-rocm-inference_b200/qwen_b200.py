@@ -62,6 +62,8 @@ _SIGS = {
     "qwen_debug_chunk_counts": (_c.c_int, [_P, _P, _c.c_int]),
     "qwen_debug_capture": (_c.c_int, [_P, _c.c_int]),
     "qwen_debug_read": (_c.c_int, [_P, _P, _P]),
+    "qwen_trace_enable": (_c.c_int, [_P, _c.c_int]),
+    "qwen_trace_read": (_c.c_int, [_P, _P, _c.c_int]),
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
 }
@@ -268,6 +270,19 @@ class Engine:
         q = np.zeros((N_LAYERS, 4096), dtype=np.float32)
         _check(self._lib.qwen_debug_read(self._h, _ptr(r), _ptr(q)))
         return r, q
+
+    TRACE_STRIDE = 448
+
+    def trace_enable(self, enable=True):
+        _check(self._lib.qwen_trace_enable(self._h, 1 if enable else 0))
+
+    def trace_read(self):
+        """[n_ctas, TRACE_STRIDE] %globaltimer stamps (ns) of the last launch."""
+        out = np.zeros(1024 * self.TRACE_STRIDE, dtype=np.uint64)
+        n = self._lib.qwen_trace_read(self._h, _ptr(out), out.size)
+        if n < 0:
+            _check(n)
+        return out[:n].reshape(-1, self.TRACE_STRIDE)
 
     def set_vocab_shard(self, begin, end):
         _check(self._lib.qwen_set_vocab_shard(self._h, int(begin), int(end)))
