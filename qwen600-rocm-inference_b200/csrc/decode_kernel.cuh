@@ -53,7 +53,7 @@ namespace qb {
 constexpr int kNCW = 16;                    // consumer warps
 constexpr int kNCT = kNCW * 32;             // consumer threads
 constexpr int kThreads = kNCT + 64;         // + one producer warp + one L2-prefetch warp
-constexpr int kSlots = 6;
+constexpr int kSlots = 4;
 constexpr int kSlotBytes = 32768;
 constexpr int kGroups = N_KV_HEADS;         // one CTA group per KV head
 constexpr int kMaxGS = 19;                  // max CTAs per group (grid <= 152)
@@ -141,6 +141,19 @@ struct DecodeParams {
     unsigned long long* trace;   // [G][kTraceStride] %globaltimer stamps, or nullptr
     int prefetch_chunks;     // L2 prefetch lead of the producer, in chunks (0 = none)
     int poll_ns;             // back-off between polls of an exchange word
+    int ring_slots;          // ring slots in use, 2..kSlots (bounds the bulk bytes in flight)
+};
+
+struct Plan {          // this CTA's share of every stage
+    int g, gr, gs;
+    int qa, qb;        // QKV rows of the group's 512
+    int p0, p1, pe;    // attention positions [p0, p1); cached ones [p0, pe)
+    int oa, ob;        // Wo_g rows
+    int ha, hb;        // hidden rows (gate / up)
+    int da, db;        // output rows of Wd
+    int va, vb;        // LM-head rows
+    bool head;
+    size_t kvbase;     // element offset of (layer 0, head g) in the K/V cache
 };
 
 struct __align__(16) DecodeSmem {
@@ -169,6 +182,7 @@ struct __align__(16) DecodeSmem {
     int flag;
     int abort;               // set after a ring wait expired: stop waiting on the ring
     unsigned int copied;     // chunks the producer has issued (read by the prefetch warp)
+    Plan pl;                 // this CTA's share of every stage (one copy, in shared memory)
 };
 constexpr size_t kDecodeSmemBytes = (size_t)kSlots * kSlotBytes + sizeof(DecodeSmem);
 
@@ -217,18 +231,6 @@ constexpr int kRowsK3072 = kSlotBytes / (2 * HIDDEN_DIM); // 5 rows of 3072 bf16
 constexpr int kKVChunk = 64;                               // positions per K|V chunk
 constexpr int kVOff = kKVChunk * 2 * HEAD_DIM;             // V offset in a K|V chunk
 constexpr int kRowsWo = kSlotBytes / (2 * 256);            // 64 rows of 256 bf16
-
-struct Plan {          // this CTA's share of every stage
-    int g, gr, gs;
-    int qa, qb;        // QKV rows of the group's 512
-    int p0, p1, pe;    // attention positions [p0, p1); cached ones [p0, pe)
-    int oa, ob;        // Wo_g rows
-    int ha, hb;        // hidden rows (gate / up)
-    int da, db;        // output rows of Wd
-    int va, vb;        // LM-head rows
-    bool head;
-    size_t kvbase;     // element offset of (layer 0, head g) in the K/V cache
-};
 
 __device__ __forceinline__ Plan make_plan(const DecodeParams& P, int c, int G, int pos, int flags) {
     Plan p;
@@ -372,7 +374,8 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
     for (;;) {
         const int n = it.next(P, pl, seg);
         if (n == 0) break;
-        const uint32_t s = k % kSlots, ph = (k / kSlots) & 1u;
+        const uint32_t ns = (uint32_t)P.ring_slots;
+        const uint32_t s = k % ns, ph = (k / ns) & 1u;
         if (!dead && !mbar_wait(&S->empty[s], ph ^ 1u, 2 * kWaitNs)) {
             atomicOr(&P.out->err, 2u);
             atomicExch(&P.out->err_where, -1 - (int)s);
@@ -427,12 +430,18 @@ struct Consumer {
     bool failed = false;    // this thread stopped waiting after an error
     unsigned long long* tr = nullptr;   // thread 0's trace row while tracing
     int tl = 0;                          // layer being traced (N_LAYERS = head)
+    unsigned long long ring_ns = 0, xw_ns = 0;   // thread 0's waits in layer tl (written by flush)
+    __device__ __forceinline__ void flush() {                    // stores only: no global read on the timed path
+        if (tr) { tr[320 + tl] = ring_ns; tr[352 + tl] = xw_ns; }
+        ring_ns = 0; xw_ns = 0;
+    }
 
-    __device__ const uint8_t* wait_chunk() {
-        const uint32_t s = k % kSlots, ph = (k / kSlots) & 1u;
+    uint32_t ns = kSlots;   // ring slots in use
+    __device__ __forceinline__ const uint8_t* wait_chunk() {
+        const uint32_t s = k % ns, ph = (k / ns) & 1u;
         const uint64_t t0 = tr ? global_ns() : 0;
         const bool ok = *(volatile int*)&S->abort || mbar_wait(&S->full[s], ph, 3 * kWaitNs);
-        if (tr) tr[320 + tl] += global_ns() - t0;
+        if (tr) ring_ns += global_ns() - t0;
         if (!ok) {
             *(volatile int*)&S->abort = 1;
             atomicOr(&P->out->err, 4u);
@@ -440,17 +449,17 @@ struct Consumer {
         }
         return ring + (size_t)s * kSlotBytes;
     }
-    __device__ void release_chunk() {
+    __device__ __forceinline__ void release_chunk() {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S->empty[k % kSlots]);
+        if (lane == 0) mbar_arrive(&S->empty[k % ns]);
         k++;
     }
-    __device__ void bar() { named_bar(1, kNCT); }
+    __device__ __forceinline__ void bar() { named_bar(1, kNCT); }
 
     // Value of exchange word p, whose first load returned w: spin until its tag
     // is this launch's (bounded; on error the value is garbage and no thread of
     // this CTA waits again).
-    __device__ float xw_get(const uint64_t* p, uint64_t w, int where) {
+    __device__ __forceinline__ float xw_get(const uint64_t* p, uint64_t w, int where) {
         if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
         if (failed) return 0.f;
         const uint64_t t0 = global_ns();
@@ -459,7 +468,7 @@ struct Consumer {
             if (P->poll_ns) __nanosleep(P->poll_ns);
             w = xw_load(p);
             if ((uint32_t)(w >> 32) == tag) {
-                if (tr) tr[352 + tl] += global_ns() - t0;
+                if (tr) xw_ns += global_ns() - t0;
                 return __uint_as_float((uint32_t)w);
             }
             if ((++it & 31u) == 0) {
@@ -473,7 +482,7 @@ struct Consumer {
             }
         }
     }
-    __device__ float block_sum(float v) {
+    __device__ __forceinline__ float block_sum(float v) {
         v = warp_sum(v);
         if (lane == 0) S->bred[0][warp] = v;
         bar();
@@ -484,7 +493,7 @@ struct Consumer {
         return t;
     }
     // argmax over the block: largest value, ties to the smallest index
-    __device__ void block_argmax(float& v, int& i) {
+    __device__ __forceinline__ void block_argmax(float& v, int& i) {
         #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
@@ -499,7 +508,7 @@ struct Consumer {
         bar();
     }
     // RMSNorm of S->xres (sum of squares `ss`) with the bf16 gains at `gain` -> S->xs
-    __device__ void norm_into_xs(const uint16_t* gain, float ss) {
+    __device__ __forceinline__ void norm_into_xs(const uint16_t* gain, float ss) {
         const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
         const int j = tid * 2;
         const uint32_t w = *(const uint32_t*)(gain + j);
@@ -507,7 +516,7 @@ struct Consumer {
         S->xs[j + 1] = (S->xres[j + 1] * r) * bf_hi(w);
     }
     // lane's 32 fp32 values of a 1024-wide vector v: v[256 i + 8 lane + e]
-    __device__ void load_regs(const float* v, float* xr) {
+    __device__ __forceinline__ void load_regs(const float* v, float* xr) {
         #pragma unroll
         for (int i = 0; i < 4; i++) {
             const float4 a = *(const float4*)&v[256 * i + 8 * lane];
@@ -517,7 +526,7 @@ struct Consumer {
         }
     }
     // dot of a 1024-wide bf16 row segment in shared memory with xr (full warp)
-    __device__ float row_dot(const uint8_t* row, const float* xr) {
+    __device__ __forceinline__ float row_dot(const uint8_t* row, const float* xr) {
         const uint4* w = (const uint4*)row;
         float a = 0.f;
         #pragma unroll
@@ -526,7 +535,7 @@ struct Consumer {
     }
     // rows [a, b) of 1024 columns, 16 per chunk, one row per warp; f(row, value) on lane 0
     template <typename F>
-    __device__ void rows_1024(int a, int b, const float* xr, F&& f) {
+    __device__ __forceinline__ void rows_1024(int a, int b, const float* xr, F&& f) {
         for (int r = a; r < b; r += kRowsK1024) {
             const int n = min(kRowsK1024, b - r);
             const uint8_t* ch = wait_chunk();
@@ -539,29 +548,31 @@ struct Consumer {
     }
 };
 
-__device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, int G, const Plan& pl,
+__device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, int G, const Plan& pl,
                                              int token, int pos, int flags, uint32_t seq) {
     Consumer C;
     C.P = &P; C.ring = ring; C.S = S;
     C.tid = threadIdx.x; C.warp = C.tid >> 5; C.lane = C.tid & 31;
     C.tag = seq;
+    C.ns = (uint32_t)P.ring_slots;
     const int tid = C.tid, warp = C.warp, lane = C.lane;
     if (P.trace && tid == 0) {
         C.tr = P.trace + (size_t)c * kTraceStride;
-        for (int i = 320; i < kTraceStride; i++) C.tr[i] = 0;
     }
     const int g = pl.g, gs = pl.gs, gr = pl.gr;
     const bool owner = (gr == gs - 1);                 // its position range ends at pos
     const float sqrt_hd = sqrtf((float)HEAD_DIM);
     unsigned long long* tr = (P.trace && tid == 0) ? P.trace + (size_t)c * kTraceStride : nullptr;
 #define QB_TRACE(i) do { if (tr) tr[(i)] = global_ns(); } while (0)
-#define QB_SUB(i) do { if (tr && l == 13) tr[384 + (i)] = global_ns(); } while (0)
+#define QB_SUB(i) do { if (tr && l == 13) tr[384 + (i)] = clock64(); } while (0)   // cycles: exact within a CTA
     QB_TRACE(0);
+    if (tr) tr[384 + 50] = clock64();
 
     if (tid < HEAD_DIM) S->rope[tid] = __ldg(P.rope + (size_t)pos * HEAD_DIM + tid);
 
     for (int l = 0; l < N_LAYERS; l++) {
         const int TB = 1 + 10 * l;
+        C.flush();
         C.tl = l;
         // ---------------- QKV ----------------
         float ss;
@@ -580,6 +591,7 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
             ss = C.block_sum(v.x * v.x + v.y * v.y);
         }
         QB_TRACE(TB + 0);
+        QB_SUB(31);
         {
             const uint8_t* ch = C.wait_chunk();
             QB_SUB(0);
@@ -593,10 +605,13 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
         {
             float xr[32];
             C.load_regs(S->xs, xr);
-            uint64_t* q = P.qkvw + (size_t)l * 4096;
-            C.rows_1024(pl.qa, pl.qb, xr, [&](int r, float v) { xw_store(q + qkv_dst(g, r), v, seq); });
+            C.rows_1024(pl.qa, pl.qb, xr, [&](int r, float v) { S->gv[r - pl.qa] = v; });
         }
+        C.bar();
+        if (tid < pl.qb - pl.qa)   // one exchange store per thread, all in flight together
+            xw_store(P.qkvw + (size_t)l * 4096 + qkv_dst(g, pl.qa + tid), S->gv[tid], seq);
         QB_TRACE(TB + 1);
+        QB_SUB(32);
 
         // ---------------- ATT ----------------
         if (warp < 4) {   // warp w: q head 2g (0), q head 2g+1 (1), k (2), v (3); lane holds dims 4l..4l+3
@@ -641,6 +656,7 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
         QB_SUB(3);
         C.bar();
         QB_TRACE(TB + 2);
+        QB_SUB(33);
         {
             // warps 0-7: q head 2g; warps 8-15: q head 2g+1.  Each warp runs an
             // online softmax over positions hw, hw+8, ... of every K|V chunk.
@@ -719,20 +735,22 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
         }
         C.bar();
         QB_TRACE(TB + 4);
+        if (warp < 2) {   // warp hh: the combine weights of head hh, lane cc = chunk
+            const int hh = warp;
+            const float* b = &S->w.pst[lane * kPartStride + hh * kHeadPart];
+            const bool live = lane < gs && b[1] > 0.f;
+            const float m = live ? b[0] : -INFINITY;
+            const float M = warp_max(m);
+            const float e = live ? expf(m - M) : 0.f;
+            const float den = warp_sum(live ? b[1] * e : 0.f);
+            if (lane < kMaxGS) S->gv[hh * 32 + lane] = e / den;
+        }
+        C.bar();
         if (tid < 2 * HEAD_DIM) {
             const int hh = tid >> 7, d = tid & 127;
-            float M = -INFINITY;
-            for (int cc = 0; cc < gs; cc++) M = fmaxf(M, S->w.pst[cc * kPartStride + hh * kHeadPart]);
-            float den = 0.f, num = 0.f;
-            for (int cc = 0; cc < gs; cc++) {
-                const float* b = &S->w.pst[cc * kPartStride + hh * kHeadPart];
-                if (b[1] > 0.f) {
-                    const float wt = expf(b[0] - M);
-                    den = fmaf(b[1], wt, den);
-                    num = fmaf(b[4 + d], wt, num);
-                }
-            }
-            S->os[tid] = num / den;
+            float num = 0.f;
+            for (int cc = 0; cc < gs; cc++) num = fmaf(S->w.pst[cc * kPartStride + hh * kHeadPart + 4 + d], S->gv[hh * 32 + cc], num);
+            S->os[tid] = num;
         }
         QB_SUB(11);
         C.bar();
@@ -749,11 +767,13 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
                 for (int i = warp; i < cnt; i += kNCW) {
                     const uint4 w = ((const uint4*)(ch + (size_t)i * 512))[lane];
                     const float a = warp_sum(dot8(w, o8, 0.f));
-                    if (lane == 0) xw_store(y + r + i, a, seq);
+                    if (lane == 0) S->w.hs[r - pl.oa + i] = a;
                 }
                 QB_SUB(14);
                 C.release_chunk();
             }
+            C.bar();
+            if (tid < pl.ob - pl.oa) xw_store(y + pl.oa + tid, S->w.hs[tid], seq);
         }
         QB_TRACE(TB + 5);
 
@@ -776,6 +796,7 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
             ss = C.block_sum(x0 * x0 + x1 * x1);
         }
         QB_TRACE(TB + 6);
+        QB_SUB(34);
         {
             const uint8_t* ch = C.wait_chunk();
             C.norm_into_xs((const uint16_t*)ch, ss);
@@ -797,6 +818,7 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
             xw_store(P.hw + (size_t)l * HIDDEN_DIM + pl.ha + tid, (gt / (1.0f + expf(-gt))) * S->uv[tid], seq);
         }
         QB_TRACE(TB + 7);
+        QB_SUB(35);
 
         // ---------------- MLP-B ----------------
         {
@@ -810,23 +832,28 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
         }
         C.bar();
         QB_TRACE(TB + 8);
+        const long long cy0 = clock64();
         {
             // warp -> (row rw of the chunk, 1024-column segment sg); 5 rows x 3 segments
             const int rw = warp / 3, sg = warp % 3;
             float xr[32];
             C.load_regs(S->w.hs + 1024 * sg, xr);
+            if (tr && l == 13) tr[384 + 40] = clock64() - cy0;
             uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
             for (int r = pl.da; r < pl.db; r += kRowsK3072) {
                 const int n = min(kRowsK3072, pl.db - r);
                 const uint8_t* ch = C.wait_chunk();
+                if (tr && l == 13 && r == pl.da) tr[384 + 41] = clock64() - cy0;
                 QB_SUB(28);
                 if (rw < n) {
                     const float v = C.row_dot(ch + (size_t)rw * 2 * HIDDEN_DIM + (size_t)sg * 2 * 1024, xr);
                     if (lane == 0) S->part[warp] = v;
                 }
                 QB_SUB(29);
+                if (tr && l == 13 && r == pl.da) tr[384 + 42] = clock64() - cy0;
                 C.release_chunk();
                 C.bar();
+                if (tr && l == 13 && r == pl.da) tr[384 + 43] = clock64() - cy0;
                 QB_SUB(30);
                 if (tid < n) {
                     const float v = S->xres[r + tid] + ((S->part[3 * tid] + S->part[3 * tid + 1]) + S->part[3 * tid + 2]);
@@ -837,9 +864,11 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
         }
         C.bar();     // S->w.hs and S->xres are reused by the next layer
         QB_TRACE(TB + 9);
+        QB_SUB(36);
     }
 
     // ---------------- HEAD ----------------
+    C.flush();
     C.tl = N_LAYERS;
     const bool head = pl.head;
     const bool greedy = (P.in->temperature == 0.0f || P.in->top_k == 1);
@@ -886,6 +915,8 @@ __device__ __noinline__ void decode_consumer(const DecodeParams& P, uint8_t* rin
         }
     }
     QB_TRACE(kTrHead + 1);
+    if (tr) tr[384 + 51] = clock64();
+    C.flush();
     // last CTA to arrive merges and samples
     C.bar();
     if (tid == 0) {
@@ -1014,7 +1045,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         token = 0;
     }
     const uint32_t seq = P.out->seq;
-    const Plan pl = make_plan(P, c, G, pos, flags);
+    if (tid == 0) S->pl = make_plan(P, c, G, pos, flags);
+    __syncthreads();
+    const Plan& pl = S->pl;
     if ((tid >> 5) == kNCW) {
         if ((tid & 31) == 0) decode_producer(P, ring, S, c, pl);
         return;
