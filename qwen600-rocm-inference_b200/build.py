@@ -52,7 +52,7 @@ def build(force=False, verbose_ptxas=False):
         objs.append(obj)
     for src in HOST_SOURCES:
         obj = os.path.join(objdir, src + ".o")
-        _run([NVCC, *COMMON, "-x", "c++", "-c", os.path.join(CSRC, src), "-o", obj])
+        _run([NVCC, *COMMON, "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", os.path.join(CSRC, src), "-o", obj])
         objs.append(obj)
     tmp = OUT + ".tmp"
     _run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lgomp"])

@@ -74,7 +74,7 @@ constexpr int kNumCtr = 1;                  // the head's arrival counter
 // 288 + l producer issues layer l; 316 producer issues the head;
 // 320 + l ns thread 0 spent waiting for ring chunks in layer l (348: head);
 // 352 + l ns thread 0 spent waiting for exchange words in layer l (380: head)
-constexpr int kTraceStride = 448;   // 384 + i: sub-stage stamps of layer 13
+constexpr int kTraceStride = 576;   // 384 + i: sub-stage stamps of layer 13; 448+: its ring chunks
 constexpr int kTrHead = 1 + 10 * N_LAYERS;
 
 // StepIn.flags
@@ -214,6 +214,10 @@ __device__ __forceinline__ uint64_t xw_load(const uint64_t* p) {
     uint64_t w;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
+}
+// two consecutive words (16-byte aligned); each word is checked on its own
+__device__ __forceinline__ void xw_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -370,6 +374,7 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
     ChunkIter it;
     Seg seg[3];
     uint32_t k = 0;
+    int k13 = -1;
     bool dead = false;
     for (;;) {
         const int n = it.next(P, pl, seg);
@@ -382,6 +387,10 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
             dead = true;   // issue nothing more; consumers stop waiting after their own timeout
         }
         if (tr && it.cur_st == 0) tr[288 + it.cur_l] = global_ns();
+        if (tr && it.cur_l == 13 && it.cur_st <= 7) {   // layer 13's chunks: issue cycle and stage
+            if (k13 < 0) k13 = (int)k;
+            if ((int)k - k13 < 32) { tr[448 + k - k13] = clock64(); tr[544 + k - k13] = it.cur_st; }
+        }
         if (tr && it.cur_st == 8) tr[316] = global_ns();
         if (!dead) {
             uint32_t total = 0;
@@ -430,6 +439,7 @@ struct Consumer {
     bool failed = false;    // this thread stopped waiting after an error
     unsigned long long* tr = nullptr;   // thread 0's trace row while tracing
     int tl = 0;                          // layer being traced (N_LAYERS = head)
+    int k13 = -1;                        // first ring chunk of layer 13 (cycle trace)
     unsigned long long ring_ns = 0, xw_ns = 0;   // thread 0's waits in layer tl (written by flush)
     __device__ __forceinline__ void flush() {                    // stores only: no global read on the timed path
         if (tr) { tr[320 + tl] = ring_ns; tr[352 + tl] = xw_ns; }
@@ -440,8 +450,10 @@ struct Consumer {
     __device__ __forceinline__ const uint8_t* wait_chunk() {
         const uint32_t s = k % ns, ph = (k / ns) & 1u;
         const uint64_t t0 = tr ? global_ns() : 0;
+        if (tr && tl == 13) { if (k13 < 0) k13 = (int)k; if ((int)k - k13 < 32) tr[480 + k - k13] = clock64(); }
         const bool ok = *(volatile int*)&S->abort || mbar_wait(&S->full[s], ph, 3 * kWaitNs);
         if (tr) ring_ns += global_ns() - t0;
+        if (tr && tl == 13 && (int)k - k13 < 32) tr[512 + k - k13] = clock64();
         if (!ok) {
             *(volatile int*)&S->abort = 1;
             atomicOr(&P->out->err, 4u);
@@ -456,31 +468,50 @@ struct Consumer {
     }
     __device__ __forceinline__ void bar() { named_bar(1, kNCT); }
 
-    // Value of exchange word p, whose first load returned w: spin until its tag
-    // is this launch's (bounded; on error the value is garbage and no thread of
-    // this CTA waits again).
-    __device__ __forceinline__ float xw_get(const uint64_t* p, uint64_t w, int where) {
-        if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
-        if (failed) return 0.f;
-        const uint64_t t0 = global_ns();
+    // Gathers up to N word pairs: pair i (16-byte aligned, at addr(i)) for each i
+    // whose bit is set in `mask`, into v[2i], v[2i+1].  A round loads every pair
+    // at once; until all carry this launch's tag the thread spins on the first
+    // stale pair only, then runs another round.  Once the last writer has stored,
+    // the gather costs about one round trip whatever the number of words, and a
+    // waiting CTA polls one pair per thread.
+    template <int N, typename A>
+    __device__ __forceinline__ void gather(A addr, uint32_t mask, float* v, int where) {
+        uint64_t t0 = 0;
         uint32_t it = 0;
-        for (;;) {
-            if (P->poll_ns) __nanosleep(P->poll_ns);
-            w = xw_load(p);
-            if ((uint32_t)(w >> 32) == tag) {
-                if (tr) xw_ns += global_ns() - t0;
-                return __uint_as_float((uint32_t)w);
+        while (!failed) {
+            uint64_t a[N], b[N];
+            #pragma unroll
+            for (int i = 0; i < N; i++) if (mask & (1u << i)) xw_load2(addr(i), a[i], b[i]);
+            int stale = -1;
+            #pragma unroll
+            for (int i = N - 1; i >= 0; i--)
+                if ((mask & (1u << i)) && ((uint32_t)(a[i] >> 32) != tag || (uint32_t)(b[i] >> 32) != tag)) stale = i;
+            if (stale < 0) {
+                #pragma unroll
+                for (int i = 0; i < N; i++) { v[2 * i] = __uint_as_float((uint32_t)a[i]); v[2 * i + 1] = __uint_as_float((uint32_t)b[i]); }
+                if (tr && t0) xw_ns += global_ns() - t0;
+                return;
             }
-            if ((++it & 31u) == 0) {
-                if (ld_volatile(&P->out->err)) { failed = true; return 0.f; }
-                if (global_ns() - t0 > kWaitNs) {
-                    atomicOr(&P->out->err, 1u);
-                    atomicExch(&P->out->err_where, where);
-                    failed = true;
-                    return 0.f;
+            if (t0 == 0) t0 = global_ns();
+            const uint64_t* q = addr(stale);
+            for (;;) {
+                if (P->poll_ns) __nanosleep(P->poll_ns);
+                uint64_t x, y;
+                xw_load2(q, x, y);
+                if ((uint32_t)(x >> 32) == tag && (uint32_t)(y >> 32) == tag) break;
+                if ((++it & 31u) == 0) {
+                    if (ld_volatile(&P->out->err)) { failed = true; break; }
+                    if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(&P->out->err, 1u);
+                        atomicExch(&P->out->err_where, where);
+                        failed = true;
+                        break;
+                    }
                 }
             }
         }
+        #pragma unroll
+        for (int i = 0; i < 2 * N; i++) v[i] = 0.f;   // after an error the values are never used for a result
     }
     __device__ __forceinline__ float block_sum(float v) {
         v = warp_sum(v);
@@ -584,8 +615,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 v = make_float2(bf_lo(w), bf_hi(w));
             } else {
                 const uint64_t* p = P.xw + (size_t)l * DIM + j;
-                const uint64_t w0 = xw_load(p), w1 = xw_load(p + 1);
-                v.x = C.xw_get(p, w0, 10 * l); v.y = C.xw_get(p + 1, w1, 10 * l);
+                float xv[2];
+                C.gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
+                v.x = xv[0]; v.y = xv[1];
             }
             S->xres[j] = v.x; S->xres[j + 1] = v.y;
             ss = C.block_sum(v.x * v.x + v.y * v.y);
@@ -617,12 +649,8 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         if (warp < 4) {   // warp w: q head 2g (0), q head 2g+1 (1), k (2), v (3); lane holds dims 4l..4l+3
             const int off = warp < 2 ? 256 * g + 128 * warp : (warp == 2 ? Q_DIM + 128 * g : Q_DIM + KV_DIM + 128 * g);
             const uint64_t* p = P.qkvw + (size_t)l * 4096 + off + 4 * lane;
-            uint64_t w[4];
-            #pragma unroll
-            for (int e = 0; e < 4; e++) w[e] = xw_load(p + e);
             float x[4];
-            #pragma unroll
-            for (int e = 0; e < 4; e++) x[e] = C.xw_get(p + e, w[e], 10 * l + 2);
+            C.gather<2>([&](int i) { return p + 2 * i; }, 3u, x, 10 * l + 2);
             if (warp < 3) {
                 const float tot = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
                 const float r = 1.0f / sqrtf(tot * (1.0f / HEAD_DIM) + EPS);
@@ -721,15 +749,16 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             // stage the group's gs x 264 partial words in shared memory, spread over all threads
             const uint64_t* gbase = P.partw + (size_t)(l * kGroups + g) * kMaxGS * kPartStride;
             const int nw = gs * kPartStride;
-            constexpr int kPer = (kMaxGS * kPartStride + kNCT - 1) / kNCT;
-            uint64_t w[kPer];
+            constexpr int kPer = (kMaxGS * kPartStride + 2 * kNCT - 1) / (2 * kNCT);
+            uint32_t pend = 0;
             #pragma unroll
-            for (int i = 0; i < kPer; i++) { const int idx = tid + i * kNCT; if (idx < nw) w[i] = xw_load(gbase + idx); }
+            for (int i = 0; i < kPer; i++) if (2 * tid + 2 * kNCT * i < nw) pend |= 1u << i;
+            float v[2 * kPer];
             QB_SUB(8);
+            C.gather<kPer>([&](int i) { return gbase + 2 * tid + 2 * kNCT * i; }, pend, v, 10 * l + 4);
             #pragma unroll
             for (int i = 0; i < kPer; i++) {
-                const int idx = tid + i * kNCT;
-                if (idx < nw) S->w.pst[idx] = C.xw_get(gbase + idx, w[i], 10 * l + 4);
+                if (pend & (1u << i)) *(float2*)&S->w.pst[2 * tid + 2 * kNCT * i] = make_float2(v[2 * i], v[2 * i + 1]);
             }
             QB_SUB(9);
         }
@@ -781,15 +810,13 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         {
             const int j = tid * 2;
             const uint64_t* yb = P.yw + (size_t)l * kGroups * DIM + j;
-            uint64_t w[2 * kGroups];
-            #pragma unroll
-            for (int gg = 0; gg < kGroups; gg++) { w[2 * gg] = xw_load(yb + (size_t)gg * DIM); w[2 * gg + 1] = xw_load(yb + (size_t)gg * DIM + 1); }
             QB_SUB(16);
             float x0 = S->xres[j], x1 = S->xres[j + 1];
-            #pragma unroll
-            for (int gg = 0; gg < kGroups; gg++) {
-                x0 += C.xw_get(yb + (size_t)gg * DIM, w[2 * gg], 10 * l + 6);
-                x1 += C.xw_get(yb + (size_t)gg * DIM + 1, w[2 * gg + 1], 10 * l + 6);
+            {
+                float yv[2 * kGroups];
+                C.gather<kGroups>([&](int gg) { return yb + (size_t)gg * DIM; }, (1u << kGroups) - 1u, yv, 10 * l + 6);
+                #pragma unroll
+                for (int gg = 0; gg < kGroups; gg++) { x0 += yv[2 * gg]; x1 += yv[2 * gg + 1]; }
             }
             QB_SUB(17);
             S->xres[j] = x0; S->xres[j + 1] = x1;
@@ -822,13 +849,13 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 
         // ---------------- MLP-B ----------------
         {
-            const uint64_t* hb = P.hw + (size_t)l * HIDDEN_DIM;
-            uint64_t w[HIDDEN_DIM / kNCT];
-            #pragma unroll
-            for (int i = 0; i < HIDDEN_DIM / kNCT; i++) w[i] = xw_load(hb + tid + i * kNCT);
+            const uint64_t* hb = P.hw + (size_t)l * HIDDEN_DIM + 2 * tid;
+            constexpr int kHP = HIDDEN_DIM / (2 * kNCT);
+            float hv[2 * kHP];
             QB_SUB(25);
+            C.gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
             #pragma unroll
-            for (int i = 0; i < HIDDEN_DIM / kNCT; i++) S->w.hs[tid + i * kNCT] = C.xw_get(hb + tid + i * kNCT, w[i], 10 * l + 8);
+            for (int i = 0; i < kHP; i++) *(float2*)&S->w.hs[2 * tid + 2 * kNCT * i] = make_float2(hv[2 * i], hv[2 * i + 1]);
         }
         C.bar();
         QB_TRACE(TB + 8);
@@ -878,8 +905,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         {
             const int j = tid * 2;
             const uint64_t* p = P.xw + (size_t)N_LAYERS * DIM + j;
-            const uint64_t w0 = xw_load(p), w1 = xw_load(p + 1);
-            const float x0 = C.xw_get(p, w0, 10 * N_LAYERS), x1 = C.xw_get(p + 1, w1, 10 * N_LAYERS);
+            float xv[2];
+            C.gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
+            const float x0 = xv[0], x1 = xv[1];
             S->xres[j] = x0; S->xres[j + 1] = x1;
             ss = C.block_sum(x0 * x0 + x1 * x1);
         }

@@ -271,7 +271,7 @@ class Engine:
         _check(self._lib.qwen_debug_read(self._h, _ptr(r), _ptr(q)))
         return r, q
 
-    TRACE_STRIDE = 448
+    TRACE_STRIDE = 576
 
     def trace_enable(self, enable=True):
         _check(self._lib.qwen_trace_enable(self._h, 1 if enable else 0))
