@@ -11,25 +11,30 @@
 // warp streams the CTA's slices, in consumption order, through a ring of
 // kSlots x 32 KB shared-memory slots with 1-D bulk async copies (TMA engine,
 // mbarrier completion, L2 evict-first); a second cursor issues bulk L2
-// prefetches kPrefetchChunks further ahead, so the 126 MB L2 is the deep
-// buffer and HBM keeps streaming while the ring is full.  The stream never
-// waits on activations.  Sixteen consumer warps compute from the slots.
+// prefetches further ahead.  The stream never waits on activations, so the
+// slots of the next stages are full while a CTA waits on another CTA.
+// Sixteen consumer warps compute from the slots, two chunks at a time, so
+// every warp has two or more independent rows in flight.
 //
 // Activation exchange.  Every value one CTA hands to another is an 8-byte word
 // (fp32 value | 32-bit sequence tag) written with one relaxed 64-bit store;
-// the consumer polls the words it needs until their tag equals this launch's
-// sequence number.  No fences, no counters: a hop costs about one L2 round
-// trip.  Per layer l (the 8 KV heads define 8 CTA groups of ~G/8 CTAs):
+// a reader loads the words it needs in 16-byte pairs, all at once, and polls
+// until every tag equals this launch's sequence number.  No fences, no
+// counters: a hop costs about one L2 round trip after the last writer.  Per
+// layer l (the 8 KV heads define 8 CTA groups of ~G/8 CTAs):
 //
-//   QKV   group g: x_l -> RMSNorm (input_layernorm) -> its rows of the
-//         group's 512 projection rows (q heads 2g, 2g+1; k, v head g)  -> qkv
+//   QKV   group g: x_l -> RMSNorm (input_layernorm, folded into each lane's
+//         registers) -> its rows of the group's 512 projection rows (q heads
+//         2g, 2g+1; k, v head g)                                     -> qkv
 //   ATT   group g: QK-norm + RoPE of q/k; the CTA whose positions end at pos
-//         appends bf16 K/V; split-K attention over its share of positions
-//         with a per-warp online softmax                          -> partials
+//         appends bf16 K/V; split-K attention over its share of positions:
+//         four lanes per (head, position) score, one online softmax per warp
+//                                                                -> partials
 //   OPROJ group g: combine the group's partials -> o (256 values) -> its rows
 //         of Wo[:, 256g:256g+256] (packed contiguous)             -> y[g]
 //   MLP-A all: x_mid = x_l + sum_g y[g] (fixed order); RMSNorm
-//         (post_attention_layernorm) -> its gate and up rows -> SwiGLU -> h
+//         (post_attention_layernorm) -> its gate/up rows (one warp per
+//         hidden unit) -> SwiGLU                                   -> h
 //   MLP-B all: its rows r of Wd: x_{l+1}[r] = x_mid[r] + Wd[r] . h  -> x_{l+1}
 //   HEAD  all: final RMSNorm -> its LM-head rows -> fp32 logits and a local
 //         top-K; the last CTA to finish (one atomic) merges the candidates
@@ -141,7 +146,6 @@ struct DecodeParams {
     unsigned long long* trace;   // [G][kTraceStride] %globaltimer stamps, or nullptr
     int prefetch_chunks;     // L2 prefetch lead of the producer, in chunks (0 = none)
     int poll_ns;             // back-off between polls of an exchange word
-    int ring_slots;          // ring slots in use, 2..kSlots (bounds the bulk bytes in flight)
 };
 
 struct Plan {          // this CTA's share of every stage
@@ -160,25 +164,25 @@ struct __align__(16) DecodeSmem {
     uint64_t full[kSlots];
     uint64_t empty[kSlots];
     float xres[DIM];         // layer input x_l, then x_mid
-    float xs[DIM];           // normed activation
     union {                  // one stage at a time (a barrier separates users)
         float hs[HIDDEN_DIM];                 // MLP-B: h; head merge: probabilities
         float comb[kNCW * HEAD_DIM];          // ATT: per-warp accumulators
         float pst[kMaxGS * kPartStride];      // OPROJ: the group's partials
         float lg[kMaxLocalRows];              // HEAD: local logits
     } w;
-    float qs[2 * HEAD_DIM];
-    float kn[HEAD_DIM];
+    float qs[2 * HEAD_DIM];  // the group's two q heads (normed, rotated)
+    float kn[HEAD_DIM];      // the new position's k and v (bf16-rounded)
     float vn[HEAD_DIM];
-    float gq[HEAD_DIM];
-    float gk[HEAD_DIM];
-    float rope[HEAD_DIM];
-    float os[2 * HEAD_DIM];
-    float gv[kMaxMlpRows];
-    float uv[kMaxMlpRows];
-    float part[kNCW];
-    float bred[2][kNCW];
-    int bidx[kNCW];
+    float rope[HEAD_DIM];    // cos | sin of this position
+    uint16_t gain[DIM];      // the RMSNorm gains in use (bf16)
+    float os[2 * HEAD_DIM];  // the group's attention output
+    float part[8][4];        // MLP-B: row x column-quarter partial dots
+    float bsum[2][kNCW];     // block sums, two buffers used alternately
+    float am[kNCW], al[kNCW];   // ATT: per-warp running max and sum
+    float av[kNCW];          // block argmax
+    int ai[kNCW];
+    float tv[kMaxCand];      // merged top-K (head)
+    int ti[kMaxCand];
     int flag;
     int abort;               // set after a ring wait expired: stop waiting on the ring
     unsigned int copied;     // chunks the producer has issued (read by the prefetch warp)
@@ -222,16 +226,20 @@ __device__ __forceinline__ void xw_load2(const uint64_t* p, uint64_t& a, uint64_
 
 // ---------------------------------------------------------------------------
 // The chunk sequence.  One CTA's weight / KV stream, in consumption order:
-//   per layer: [gains: input_ln | q_norm | k_norm] [QKV rows, 16/chunk]
+//   per layer: [QKV rows, 16/chunk]
 //              [K | V of cached positions, 64/chunk: K at 0, V at 16 KB]
-//              [Wo_g rows, 64/chunk] [post_ln] [gate rows, 16/chunk]
-//              [up rows, 16/chunk] [Wd rows (3072 wide), 5/chunk]
-//   then (unless kFlagNoHead): [final_ln] [LM-head rows, 16/chunk]
-// The producer walks it twice (an L2-prefetch cursor ahead of the copy
-// cursor); the consumers' code visits the same chunks in the same order.
+//              [Wo_g rows, 64/chunk]
+//              [gate|up units, 8/chunk: gate rows at 0, up rows at 16 KB]
+//              [Wd rows (3072 wide), 4/chunk]
+//   then (unless kFlagNoHead): [LM-head rows, 16/chunk]
+// RMSNorm gains are not streamed: every lane loads the few it needs from L2.
+// The producer walks the sequence twice (an L2-prefetch cursor ahead of the
+// copy cursor); the consumers' code visits the same chunks in the same order.
 // ---------------------------------------------------------------------------
 constexpr int kRowsK1024 = kSlotBytes / (2 * DIM);        // 16 rows of 1024 bf16
-constexpr int kRowsK3072 = kSlotBytes / (2 * HIDDEN_DIM); // 5 rows of 3072 bf16
+constexpr int kUnitsGU = kSlotBytes / (4 * DIM);          // 8 gate|up units per chunk
+constexpr int kUpOff = kUnitsGU * 2 * DIM;                // up rows at 16 KB
+constexpr int kRowsWd = 4;                                // Wd rows (3072 bf16) per chunk
 constexpr int kKVChunk = 64;                               // positions per K|V chunk
 constexpr int kVOff = kKVChunk * 2 * HEAD_DIM;             // V offset in a K|V chunk
 constexpr int kRowsWo = kSlotBytes / (2 * 256);            // 64 rows of 256 bf16
@@ -264,19 +272,12 @@ struct ChunkIter {
     int cur_st = 0, cur_l = 0;   // stage and layer of the chunk last returned
     // Fills seg[] with the next chunk's copies; returns their count (0 at the end).
     __device__ int next(const DecodeParams& P, const Plan& pl, Seg* seg) {
-        const int n = step(P, pl, seg);
-        return n;
-    }
-    __device__ int step(const DecodeParams& P, const Plan& pl, Seg* seg) {
         for (;;) {
             cur_st = st; cur_l = l;
             switch (st) {
             case 0:
-                seg[0] = {(const uint8_t*)P.in_ln[l], 2 * DIM, 0};
-                seg[1] = {(const uint8_t*)P.qn[l], 2 * HEAD_DIM, 2 * DIM};
-                seg[2] = {(const uint8_t*)P.kn[l], 2 * HEAD_DIM, 2 * DIM + 2 * HEAD_DIM};
                 st = 1; r = pl.qa;
-                return 3;
+                break;
             case 1:
                 if (r < pl.qb) {
                     const int n = min(kRowsK1024, pl.qb - r);
@@ -314,38 +315,28 @@ struct ChunkIter {
                     r += n;
                     return 1;
                 }
-                st = 4;
-                break;
-            case 4:
-                seg[0] = {(const uint8_t*)P.post_ln[l], 2 * DIM, 0};
                 st = 5; r = pl.ha;
-                return 1;
+                break;
             case 5:
-            case 6:
                 if (r < pl.hb) {
-                    const int n = min(kRowsK1024, pl.hb - r);
-                    const uint16_t* base = st == 5 ? P.wg[l] : P.wu[l];
-                    seg[0] = {(const uint8_t*)(base + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0};
+                    const int n = min(kUnitsGU, pl.hb - r);
+                    seg[0] = {(const uint8_t*)(P.wg[l] + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0};
+                    seg[1] = {(const uint8_t*)(P.wu[l] + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), (uint32_t)kUpOff};
                     r += n;
-                    return 1;
+                    return 2;
                 }
-                if (st == 5) { st = 6; r = pl.ha; break; }
                 st = 7; r = pl.da;
                 break;
             case 7:
                 if (r < pl.db) {
-                    const int n = min(kRowsK3072, pl.db - r);
+                    const int n = min(kRowsWd, pl.db - r);
                     seg[0] = {(const uint8_t*)(P.wd[l] + (size_t)r * HIDDEN_DIM), (uint32_t)(n * 2 * HIDDEN_DIM), 0};
                     r += n;
                     return 1;
                 }
                 if (++l < N_LAYERS) { st = 0; break; }
-                st = pl.head ? 8 : 10;
+                st = pl.head ? 9 : 10; r = pl.va;
                 break;
-            case 8:
-                seg[0] = {(const uint8_t*)P.final_ln, 2 * DIM, 0};
-                st = 9; r = pl.va;
-                return 1;
             case 9:
                 if (r < pl.vb) {
                     const int n = min(kRowsK1024, pl.vb - r);
@@ -374,24 +365,23 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
     ChunkIter it;
     Seg seg[3];
     uint32_t k = 0;
-    int k13 = -1;
-    bool dead = false;
+    int k13 = -1, last_l = -1;
+    bool dead = false, head_seen = false;
     for (;;) {
         const int n = it.next(P, pl, seg);
         if (n == 0) break;
-        const uint32_t ns = (uint32_t)P.ring_slots;
-        const uint32_t s = k % ns, ph = (k / ns) & 1u;
+        const uint32_t s = k % kSlots, ph = (k / kSlots) & 1u;
         if (!dead && !mbar_wait(&S->empty[s], ph ^ 1u, 2 * kWaitNs)) {
             atomicOr(&P.out->err, 2u);
             atomicExch(&P.out->err_where, -1 - (int)s);
             dead = true;   // issue nothing more; consumers stop waiting after their own timeout
         }
-        if (tr && it.cur_st == 0) tr[288 + it.cur_l] = global_ns();
+        if (tr && it.cur_st <= 7 && it.cur_l != last_l) { tr[288 + it.cur_l] = global_ns(); last_l = it.cur_l; }
         if (tr && it.cur_l == 13 && it.cur_st <= 7) {   // layer 13's chunks: issue cycle and stage
             if (k13 < 0) k13 = (int)k;
             if ((int)k - k13 < 32) { tr[448 + k - k13] = clock64(); tr[544 + k - k13] = it.cur_st; }
         }
-        if (tr && it.cur_st == 8) tr[316] = global_ns();
+        if (tr && it.cur_st == 9 && !head_seen) { tr[316] = global_ns(); head_seen = true; }
         if (!dead) {
             uint32_t total = 0;
             for (int i = 0; i < n; i++) total += seg[i].bytes;
@@ -434,9 +424,10 @@ struct Consumer {
     uint8_t* ring;
     DecodeSmem* S;
     int tid, warp, lane;
-    uint32_t k = 0;
+    uint32_t k = 0;          // first ring chunk not yet released by this warp
     uint32_t tag = 0;
-    bool failed = false;    // this thread stopped waiting after an error
+    uint32_t bsp = 0;        // block_sum buffer parity
+    bool failed = false;     // this thread stopped waiting after an error
     unsigned long long* tr = nullptr;   // thread 0's trace row while tracing
     int tl = 0;                          // layer being traced (N_LAYERS = head)
     int k13 = -1;                        // first ring chunk of layer 13 (cycle trace)
@@ -446,14 +437,16 @@ struct Consumer {
         ring_ns = 0; xw_ns = 0;
     }
 
-    uint32_t ns = kSlots;   // ring slots in use
-    __device__ __forceinline__ const uint8_t* wait_chunk() {
-        const uint32_t s = k % ns, ph = (k / ns) & 1u;
+    // Ring chunk k + i (i < kSlots), once it has landed.  Every warp takes every
+    // chunk in order and releases it after use; a warp may hold two at once.
+    __device__ __forceinline__ const uint8_t* chunk(uint32_t i) {
+        const uint32_t kk = k + i;
+        const uint32_t s = kk % kSlots, ph = (kk / kSlots) & 1u;
         const uint64_t t0 = tr ? global_ns() : 0;
-        if (tr && tl == 13) { if (k13 < 0) k13 = (int)k; if ((int)k - k13 < 32) tr[480 + k - k13] = clock64(); }
+        if (tr && tl == 13) { if (k13 < 0) k13 = (int)kk; if ((int)kk - k13 < 32) tr[480 + kk - k13] = clock64(); }
         const bool ok = *(volatile int*)&S->abort || mbar_wait(&S->full[s], ph, 3 * kWaitNs);
         if (tr) ring_ns += global_ns() - t0;
-        if (tr && tl == 13 && (int)k - k13 < 32) tr[512 + k - k13] = clock64();
+        if (tr && tl == 13 && (int)kk - k13 < 32) tr[512 + kk - k13] = clock64();
         if (!ok) {
             *(volatile int*)&S->abort = 1;
             atomicOr(&P->out->err, 4u);
@@ -461,19 +454,22 @@ struct Consumer {
         }
         return ring + (size_t)s * kSlotBytes;
     }
-    __device__ __forceinline__ void release_chunk() {
+    __device__ __forceinline__ void release(uint32_t n) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S->empty[k % ns]);
-        k++;
+        if (lane == 0)
+            for (uint32_t i = 0; i < n; i++) mbar_arrive(&S->empty[(k + i) % kSlots]);
+        k += n;
     }
     __device__ __forceinline__ void bar() { named_bar(1, kNCT); }
 
     // Gathers up to N word pairs: pair i (16-byte aligned, at addr(i)) for each i
-    // whose bit is set in `mask`, into v[2i], v[2i+1].  A round loads every pair
-    // at once; until all carry this launch's tag the thread spins on the first
-    // stale pair only, then runs another round.  Once the last writer has stored,
-    // the gather costs about one round trip whatever the number of words, and a
-    // waiting CTA polls one pair per thread.
+    // whose bit is set in `mask`, into v[2i], v[2i+1].  Called by whole warps.
+    // A round loads every pair of every lane at once; until all carry this
+    // launch's tag, ONE lane of the warp spins on its first stale pair and the
+    // others wait, then the warp runs another round.  Once the last writer has
+    // stored, the gather costs about one round trip whatever the number of
+    // words, and a waiting CTA polls one pair per warp, so the L2 lines being
+    // written are not swamped by readers.
     template <int N, typename A>
     __device__ __forceinline__ void gather(A addr, uint32_t mask, float* v, int where) {
         uint64_t t0 = 0;
@@ -486,41 +482,50 @@ struct Consumer {
             #pragma unroll
             for (int i = N - 1; i >= 0; i--)
                 if ((mask & (1u << i)) && ((uint32_t)(a[i] >> 32) != tag || (uint32_t)(b[i] >> 32) != tag)) stale = i;
-            if (stale < 0) {
+            const unsigned waiting = __ballot_sync(0xffffffffu, stale >= 0);
+            if (waiting == 0) {
                 #pragma unroll
                 for (int i = 0; i < N; i++) { v[2 * i] = __uint_as_float((uint32_t)a[i]); v[2 * i + 1] = __uint_as_float((uint32_t)b[i]); }
                 if (tr && t0) xw_ns += global_ns() - t0;
                 return;
             }
             if (t0 == 0) t0 = global_ns();
-            const uint64_t* q = addr(stale);
-            for (;;) {
-                if (P->poll_ns) __nanosleep(P->poll_ns);
-                uint64_t x, y;
-                xw_load2(q, x, y);
-                if ((uint32_t)(x >> 32) == tag && (uint32_t)(y >> 32) == tag) break;
-                if ((++it & 31u) == 0) {
-                    if (ld_volatile(&P->out->err)) { failed = true; break; }
-                    if (global_ns() - t0 > kWaitNs) {
-                        atomicOr(&P->out->err, 1u);
-                        atomicExch(&P->out->err_where, where);
-                        failed = true;
-                        break;
+            const int src = __ffs(waiting) - 1;
+            if (lane == src) {
+                const uint64_t* q = addr(stale);
+                for (;;) {
+                    if (P->poll_ns) __nanosleep(P->poll_ns);
+                    uint64_t x, y;
+                    xw_load2(q, x, y);
+                    if ((uint32_t)(x >> 32) == tag && (uint32_t)(y >> 32) == tag) break;
+                    if ((++it & 31u) == 0) {
+                        if (ld_volatile(&P->out->err)) { failed = true; break; }
+                        if (global_ns() - t0 > kWaitNs) {
+                            atomicOr(&P->out->err, 1u);
+                            atomicExch(&P->out->err_where, where);
+                            failed = true;
+                            break;
+                        }
                     }
                 }
             }
+            failed = __shfl_sync(0xffffffffu, failed, src);
         }
         #pragma unroll
         for (int i = 0; i < 2 * N; i++) v[i] = 0.f;   // after an error the values are never used for a result
     }
+    // Sum over the 512 consumer threads.  One barrier: consecutive calls use
+    // alternate buffers, and a call's buffer is not written again before every
+    // thread has passed the next call's barrier.
     __device__ __forceinline__ float block_sum(float v) {
         v = warp_sum(v);
-        if (lane == 0) S->bred[0][warp] = v;
+        float* b = S->bsum[bsp];
+        bsp ^= 1u;
+        if (lane == 0) b[warp] = v;
         bar();
         float t = 0.f;
         #pragma unroll
-        for (int i = 0; i < kNCW; i++) t += S->bred[0][i];
-        bar();
+        for (int i = 0; i < kNCW; i++) t += b[i];
         return t;
     }
     // argmax over the block: largest value, ties to the smallest index
@@ -531,50 +536,80 @@ struct Consumer {
             const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
             better(v, i, v2, i2);
         }
-        if (lane == 0) { S->bred[0][warp] = v; S->bidx[warp] = i; }
+        if (lane == 0) { S->av[warp] = v; S->ai[warp] = i; }
         bar();
-        v = S->bred[0][0]; i = S->bidx[0];
+        v = S->av[0]; i = S->ai[0];
         #pragma unroll
-        for (int w = 1; w < kNCW; w++) better(v, i, S->bred[0][w], S->bidx[w]);
+        for (int w = 1; w < kNCW; w++) better(v, i, S->av[w], S->ai[w]);
         bar();
     }
-    // RMSNorm of S->xres (sum of squares `ss`) with the bf16 gains at `gain` -> S->xs
-    __device__ __forceinline__ void norm_into_xs(const uint16_t* gain, float ss) {
-        const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
-        const int j = tid * 2;
-        const uint32_t w = *(const uint32_t*)(gain + j);
-        S->xs[j] = (S->xres[j] * r) * bf_lo(w);
-        S->xs[j + 1] = (S->xres[j + 1] * r) * bf_hi(w);
+    // RMSNorm gains: threads 0..127 fetch one 16-byte piece each before a
+    // gather (four registers held across it) and park it in shared memory
+    // after; the block_sum barrier that follows publishes the gains.
+    __device__ __forceinline__ uint4 gain_fetch(const uint16_t* g) {
+        return tid < DIM / 8 ? __ldg((const uint4*)(g + 8 * tid)) : make_uint4(0u, 0u, 0u, 0u);
     }
-    // lane's 32 fp32 values of a 1024-wide vector v: v[256 i + 8 lane + e]
-    __device__ __forceinline__ void load_regs(const float* v, float* xr) {
+    __device__ __forceinline__ void gain_park(uint4 v) {
+        if (tid < DIM / 8) *(uint4*)&S->gain[8 * tid] = v;
+    }
+    // This lane's 32 RMSNorm outputs of the 1024-wide x in shared memory:
+    // xr[4i + e] = (x[j] * r) * gain[j] with j = 128 i + 4 lane + e (each
+    // warp-wide load is 512 contiguous bytes: no bank conflicts).
+    __device__ __forceinline__ void norm_regs(const float* x, float r, float* xr) {
         #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 a = *(const float4*)&v[256 * i + 8 * lane];
-            const float4 b = *(const float4*)&v[256 * i + 8 * lane + 4];
-            xr[8 * i + 0] = a.x; xr[8 * i + 1] = a.y; xr[8 * i + 2] = a.z; xr[8 * i + 3] = a.w;
-            xr[8 * i + 4] = b.x; xr[8 * i + 5] = b.y; xr[8 * i + 6] = b.z; xr[8 * i + 7] = b.w;
+        for (int i = 0; i < 8; i++) {
+            const float4 a = *(const float4*)&x[128 * i + 4 * lane];
+            const uint2 gw = *(const uint2*)&S->gain[128 * i + 4 * lane];
+            xr[4 * i + 0] = (a.x * r) * bf_lo(gw.x); xr[4 * i + 1] = (a.y * r) * bf_hi(gw.x);
+            xr[4 * i + 2] = (a.z * r) * bf_lo(gw.y); xr[4 * i + 3] = (a.w * r) * bf_hi(gw.y);
         }
     }
-    // dot of a 1024-wide bf16 row segment in shared memory with xr (full warp)
-    __device__ __forceinline__ float row_dot(const uint8_t* row, const float* xr) {
-        const uint4* w = (const uint4*)row;
-        float a = 0.f;
+    // This lane's partial dot of a bf16 row segment of 128 * NI columns with
+    // xr (xr[4i + e] <-> column 128 i + 4 lane + e), in C independent chains.
+    template <int NI, int C>
+    __device__ __forceinline__ float row_part(const uint8_t* row, const float* xr) {
+        const uint2* w = (const uint2*)row;
+        float a[C];
         #pragma unroll
-        for (int i = 0; i < 4; i++) a = dot8(w[i * 32 + lane], &xr[8 * i], a);
-        return warp_sum(a);
+        for (int c = 0; c < C; c++) a[c] = 0.f;
+        #pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const uint2 v = w[i * 32 + lane];
+            float& t = a[i % C];
+            t = fmaf(bf_lo(v.x), xr[4 * i + 0], t); t = fmaf(bf_hi(v.x), xr[4 * i + 1], t);
+            t = fmaf(bf_lo(v.y), xr[4 * i + 2], t); t = fmaf(bf_hi(v.y), xr[4 * i + 3], t);
+        }
+        if constexpr (C == 4) {
+            return (a[0] + a[1]) + (a[2] + a[3]);
+        } else {
+            float t = a[0];
+            #pragma unroll
+            for (int c = 1; c < C; c++) t += a[c];
+            return t;
+        }
     }
-    // rows [a, b) of 1024 columns, 16 per chunk, one row per warp; f(row, value) on lane 0
+    // Rows [a, b) of 1024 columns, 16 per chunk, two chunks at a time: warp w
+    // takes rows 2w and 2w + 1 of the 32; f(row, value) runs on lanes 0 and 1,
+    // so a warp's two results leave in one store request.
     template <typename F>
     __device__ __forceinline__ void rows_1024(int a, int b, const float* xr, F&& f) {
-        for (int r = a; r < b; r += kRowsK1024) {
-            const int n = min(kRowsK1024, b - r);
-            const uint8_t* ch = wait_chunk();
-            if (warp < n) {
-                const float v = row_dot(ch + (size_t)warp * 2 * DIM, xr);
-                if (lane == 0) f(r + warp, v);
+        for (int r = a; r < b; r += 2 * kRowsK1024) {
+            const int n = min(2 * kRowsK1024, b - r);
+            const uint32_t nc = n > kRowsK1024 ? 2 : 1;
+            const uint8_t* c0 = chunk(0);
+            const uint8_t* c1 = nc == 2 ? chunk(1) : c0;
+            const uint8_t* ch = (2 * warp < kRowsK1024 ? c0 : c1) + (size_t)((2 * warp) & (kRowsK1024 - 1)) * 2 * DIM;
+            const bool v0 = 2 * warp < n, v1 = 2 * warp + 1 < n;
+            float s0 = 0.f, s1 = 0.f;
+            if (v0) s0 = row_part<8, 4>(ch, xr);
+            if (v1) s1 = row_part<8, 4>(ch + 2 * DIM, xr);
+            #pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
             }
-            release_chunk();
+            if (lane < 2 && 2 * warp + lane < n) f(r + 2 * warp + lane, lane == 0 ? s0 : s1);
+            release(nc);
         }
     }
 };
@@ -585,11 +620,8 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
     C.P = &P; C.ring = ring; C.S = S;
     C.tid = threadIdx.x; C.warp = C.tid >> 5; C.lane = C.tid & 31;
     C.tag = seq;
-    C.ns = (uint32_t)P.ring_slots;
     const int tid = C.tid, warp = C.warp, lane = C.lane;
-    if (P.trace && tid == 0) {
-        C.tr = P.trace + (size_t)c * kTraceStride;
-    }
+    if (P.trace && tid == 0) C.tr = P.trace + (size_t)c * kTraceStride;
     const int g = pl.g, gs = pl.gs, gr = pl.gr;
     const bool owner = (gr == gs - 1);                 // its position range ends at pos
     const float sqrt_hd = sqrtf((float)HEAD_DIM);
@@ -597,7 +629,6 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 #define QB_TRACE(i) do { if (tr) tr[(i)] = global_ns(); } while (0)
 #define QB_SUB(i) do { if (tr && l == 13) tr[384 + (i)] = clock64(); } while (0)   // cycles: exact within a CTA
     QB_TRACE(0);
-    if (tr) tr[384 + 50] = clock64();
 
     if (tid < HEAD_DIM) S->rope[tid] = __ldg(P.rope + (size_t)pos * HEAD_DIM + tid);
 
@@ -606,42 +637,28 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         C.flush();
         C.tl = l;
         // ---------------- QKV ----------------
-        float ss;
         {
+            const uint4 gv = C.gain_fetch(P.in_ln[l]);
             const int j = tid * 2;
-            float2 v;
+            float xv[2];
             if (l == 0) {
                 const uint32_t w = __ldg((const uint32_t*)(P.embed + (size_t)token * DIM + j));
-                v = make_float2(bf_lo(w), bf_hi(w));
+                xv[0] = bf_lo(w); xv[1] = bf_hi(w);
             } else {
                 const uint64_t* p = P.xw + (size_t)l * DIM + j;
-                float xv[2];
                 C.gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
-                v.x = xv[0]; v.y = xv[1];
             }
-            S->xres[j] = v.x; S->xres[j + 1] = v.y;
-            ss = C.block_sum(v.x * v.x + v.y * v.y);
-        }
-        QB_TRACE(TB + 0);
-        QB_SUB(31);
-        {
-            const uint8_t* ch = C.wait_chunk();
-            QB_SUB(0);
-            C.norm_into_xs((const uint16_t*)ch, ss);
-            if (tid < HEAD_DIM) S->gq[tid] = bf2f(((const uint16_t*)(ch + 2 * DIM))[tid]);
-            else if (tid < 2 * HEAD_DIM) S->gk[tid - HEAD_DIM] = bf2f(((const uint16_t*)(ch + 2 * DIM + 2 * HEAD_DIM))[tid - HEAD_DIM]);
-            C.release_chunk();
-        }
-        C.bar();
-        QB_SUB(1);
-        {
+            S->xres[j] = xv[0]; S->xres[j + 1] = xv[1];
+            C.gain_park(gv);
+            const float ss = C.block_sum(xv[0] * xv[0] + xv[1] * xv[1]);
+            QB_SUB(31);
+            QB_TRACE(TB + 0);
+            const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
             float xr[32];
-            C.load_regs(S->xs, xr);
-            C.rows_1024(pl.qa, pl.qb, xr, [&](int r, float v) { S->gv[r - pl.qa] = v; });
+            C.norm_regs(S->xres, r, xr);
+            uint64_t* qkv = P.qkvw + (size_t)l * 4096;
+            C.rows_1024(pl.qa, pl.qb, xr, [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v, seq); });
         }
-        C.bar();
-        if (tid < pl.qb - pl.qa)   // one exchange store per thread, all in flight together
-            xw_store(P.qkvw + (size_t)l * 4096 + qkv_dst(g, pl.qa + tid), S->gv[tid], seq);
         QB_TRACE(TB + 1);
         QB_SUB(32);
 
@@ -649,26 +666,26 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         if (warp < 4) {   // warp w: q head 2g (0), q head 2g+1 (1), k (2), v (3); lane holds dims 4l..4l+3
             const int off = warp < 2 ? 256 * g + 128 * warp : (warp == 2 ? Q_DIM + 128 * g : Q_DIM + KV_DIM + 128 * g);
             const uint64_t* p = P.qkvw + (size_t)l * 4096 + off + 4 * lane;
+            uint2 gn = make_uint2(0u, 0u);
+            if (warp < 3) gn = __ldg((const uint2*)((warp < 2 ? P.qn[l] : P.kn[l]) + 4 * lane));
             float x[4];
             C.gather<2>([&](int i) { return p + 2 * i; }, 3u, x, 10 * l + 2);
             if (warp < 3) {
                 const float tot = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
                 const float r = 1.0f / sqrtf(tot * (1.0f / HEAD_DIM) + EPS);
-                const float* gn = warp < 2 ? S->gq : S->gk;
-                #pragma unroll
-                for (int e = 0; e < 4; e++) x[e] = (x[e] * r) * gn[4 * lane + e];
+                x[0] = (x[0] * r) * bf_lo(gn.x); x[1] = (x[1] * r) * bf_hi(gn.x);
+                x[2] = (x[2] * r) * bf_lo(gn.y); x[3] = (x[3] * r) * bf_hi(gn.y);
                 // NeoX rotation: dim d pairs with d ^ 64, held by lane ^ 16
                 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const float pv = __shfl_xor_sync(0xffffffffu, x[e], 16);
-                    const int d = 4 * lane + e, j = d & 63;
-                    const float cj = S->rope[j], sj = S->rope[64 + j];
+                    const int d = 4 * lane + e, jj = d & 63;
+                    const float cj = S->rope[jj], sj = S->rope[64 + jj];
                     x[e] = d < 64 ? (x[e] * cj - pv * sj) : (pv * sj + x[e] * cj);
                 }
             }
             if (warp < 2) {
-                #pragma unroll
-                for (int e = 0; e < 4; e++) S->qs[128 * warp + 4 * lane + e] = x[e];
+                *(float4*)&S->qs[128 * warp + 4 * lane] = make_float4(x[0], x[1], x[2], x[3]);
             } else if (owner) {
                 uint16_t b[4];
                 #pragma unroll
@@ -677,62 +694,98 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 uint16_t* dst = (warp == 2 ? P.kc : P.vc) + at;
                 *(uint2*)dst = make_uint2((uint32_t)b[0] | ((uint32_t)b[1] << 16), (uint32_t)b[2] | ((uint32_t)b[3] << 16));
                 float* sm = warp == 2 ? S->kn : S->vn;
-                #pragma unroll
-                for (int e = 0; e < 4; e++) sm[4 * lane + e] = bf2f(b[e]);
+                *(float4*)&sm[4 * lane] = make_float4(bf2f(b[0]), bf2f(b[1]), bf2f(b[2]), bf2f(b[3]));
             }
         }
-        QB_SUB(3);
         C.bar();
         QB_TRACE(TB + 2);
         QB_SUB(33);
         {
-            // warps 0-7: q head 2g; warps 8-15: q head 2g+1.  Each warp runs an
-            // online softmax over positions hw, hw+8, ... of every K|V chunk.
-            const int hh = warp >> 3, hw = warp & 7;
-            float q[4];
+            // Warp w: q head hh = w / 8 and positions 8 (w % 8) .. +7 of every
+            // K|V chunk.  Four lanes score one position: lane quarter qq takes
+            // the 16 bf16 pairs 4 (j ^ x) + qq, j = 0..15, x = position % 16 —
+            // a rotation that spreads the warp's 32 reads over all 32 banks.
+            // Then one online-softmax step per chunk; for P.V lane l holds
+            // dims 4l..4l+3.
+            const int hh = warp >> 3, sub = warp & 7;
+            const int ti = 8 * sub + (lane >> 2), qq = lane & 3, xr4 = (ti & 15) << 2;
+            float2 qv[16];
             #pragma unroll
-            for (int e = 0; e < 4; e++) q[e] = S->qs[128 * hh + 4 * lane + e];
+            for (int j = 0; j < 16; j++) qv[j] = *(const float2*)&S->qs[128 * hh + 2 * (((4 * j) ^ xr4) + qq)];
             float m = -INFINITY, lsum = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            auto visit = [&](float k0, float k1, float k2, float k3, float v0, float v1, float v2, float v3) {
-                float s = q[0] * k0; s = fmaf(q[1], k1, s); s = fmaf(q[2], k2, s); s = fmaf(q[3], k3, s);
-                s = warp_sum(s) / sqrt_hd;
-                const float mn = fmaxf(m, s);
-                const float sc = expf(m - mn), p = expf(s - mn);
-                lsum = fmaf(lsum, sc, p);
-                a0 = fmaf(a0, sc, p * v0); a1 = fmaf(a1, sc, p * v1); a2 = fmaf(a2, sc, p * v2); a3 = fmaf(a3, sc, p * v3);
-                m = mn;
-            };
             for (int t0 = pl.p0; t0 < pl.pe; t0 += kKVChunk) {
                 const int cnt = min(kKVChunk, pl.pe - t0);
-                const uint8_t* ch = C.wait_chunk();
-                for (int i = hw; i < cnt; i += 8) {
-                    const uint2 kw = *(const uint2*)(ch + (size_t)i * 2 * HEAD_DIM + 8 * lane);
-                    const uint2 vw = *(const uint2*)(ch + kVOff + (size_t)i * 2 * HEAD_DIM + 8 * lane);
-                    visit(bf_lo(kw.x), bf_hi(kw.x), bf_lo(kw.y), bf_hi(kw.y), bf_lo(vw.x), bf_hi(vw.x), bf_lo(vw.y), bf_hi(vw.y));
+                const uint8_t* ch = C.chunk(0);
+                const bool valid = ti < cnt;
+                float s = 0.f;
+                if (valid) {
+                    const uint32_t* kr = (const uint32_t*)(ch + (size_t)ti * 2 * HEAD_DIM) + qq;
+                    float c4[4] = {0.f, 0.f, 0.f, 0.f};
+                    #pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const uint32_t w = kr[(4 * j) ^ xr4];
+                        c4[j & 3] = fmaf(bf_lo(w), qv[j].x, c4[j & 3]);
+                        c4[j & 3] = fmaf(bf_hi(w), qv[j].y, c4[j & 3]);
+                    }
+                    s = (c4[0] + c4[1]) + (c4[2] + c4[3]);
                 }
-                C.release_chunk();
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                s = valid ? s / sqrt_hd : -INFINITY;
+                float mc = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 4));
+                mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 8));
+                mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 16));
+                const float mn = fmaxf(m, mc);
+                if (mn != -INFINITY) {   // warp-uniform
+                    const float sc = expf(m - mn);
+                    const float pr = valid ? expf(s - mn) : 0.f;
+                    float ps = pr + __shfl_xor_sync(0xffffffffu, pr, 4);
+                    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                    lsum = fmaf(lsum, sc, ps);
+                    a0 *= sc; a1 *= sc; a2 *= sc; a3 *= sc;
+                    const uint8_t* vb = ch + kVOff + 8 * lane;
+                    #pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const float pi = __shfl_sync(0xffffffffu, pr, 4 * i);
+                        if (8 * sub + i < cnt) {
+                            const uint2 vw = *(const uint2*)(vb + (size_t)(8 * sub + i) * 2 * HEAD_DIM);
+                            a0 = fmaf(pi, bf_lo(vw.x), a0); a1 = fmaf(pi, bf_hi(vw.x), a1);
+                            a2 = fmaf(pi, bf_lo(vw.y), a2); a3 = fmaf(pi, bf_hi(vw.y), a3);
+                        }
+                    }
+                    m = mn;
+                }
+                C.release(1);
             }
             QB_SUB(5);
-            if (owner && hw == ((pos - pl.p0) & 7)) {
+            if (owner && sub == 0) {   // the new position, from shared memory (warps 0 and 8)
                 const float4 kk = *(const float4*)&S->kn[4 * lane], vv = *(const float4*)&S->vn[4 * lane];
-                visit(kk.x, kk.y, kk.z, kk.w, vv.x, vv.y, vv.z, vv.w);
+                const float4 qh = *(const float4*)&S->qs[128 * hh + 4 * lane];
+                float s = qh.x * kk.x; s = fmaf(qh.y, kk.y, s); s = fmaf(qh.z, kk.z, s); s = fmaf(qh.w, kk.w, s);
+                s = warp_sum(s) / sqrt_hd;
+                const float mn = fmaxf(m, s);
+                const float sc = expf(m - mn), pr = expf(s - mn);
+                lsum = fmaf(lsum, sc, pr);
+                a0 = fmaf(a0, sc, pr * vv.x); a1 = fmaf(a1, sc, pr * vv.y); a2 = fmaf(a2, sc, pr * vv.z); a3 = fmaf(a3, sc, pr * vv.w);
+                m = mn;
             }
             // combine the 8 warps of each head
             *(float4*)&S->w.comb[(size_t)warp * HEAD_DIM + 4 * lane] = make_float4(a0, a1, a2, a3);
-            if (lane == 0) { S->bred[0][warp] = m; S->bred[1][warp] = lsum; }
+            if (lane == 0) { S->am[warp] = m; S->al[warp] = lsum; }
             C.bar();
             QB_SUB(6);
             if (tid < 2 * HEAD_DIM) {
                 const int h2 = tid >> 7, d = tid & 127;
                 float M = -INFINITY;
                 #pragma unroll
-                for (int w = 0; w < 8; w++) M = fmaxf(M, S->bred[0][8 * h2 + w]);
+                for (int w = 0; w < 8; w++) M = fmaxf(M, S->am[8 * h2 + w]);
                 float Ls = 0.f, A = 0.f;
                 #pragma unroll
                 for (int w = 0; w < 8; w++) {
-                    const float mw = S->bred[0][8 * h2 + w];
+                    const float mw = S->am[8 * h2 + w];
                     const float sc = mw == -INFINITY ? 0.f : expf(mw - M);
-                    Ls = fmaf(S->bred[1][8 * h2 + w], sc, Ls);
+                    Ls = fmaf(S->al[8 * h2 + w], sc, Ls);
                     A = fmaf(S->w.comb[(size_t)(8 * h2 + w) * HEAD_DIM + d], sc, A);
                 }
                 uint64_t* base = P.partw + ((size_t)(l * kGroups + g) * kMaxGS + gr) * kPartStride + h2 * kHeadPart;
@@ -746,7 +799,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 
         // ---------------- OPROJ ----------------
         {
-            // stage the group's gs x 264 partial words in shared memory, spread over all threads
+            // stage the group's gs x 264 partial words in shared memory, in pairs over all threads
             const uint64_t* gbase = P.partw + (size_t)(l * kGroups + g) * kMaxGS * kPartStride;
             const int nw = gs * kPartStride;
             constexpr int kPer = (kMaxGS * kPartStride + 2 * kNCT - 1) / (2 * kNCT);
@@ -764,50 +817,63 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         }
         C.bar();
         QB_TRACE(TB + 4);
-        if (warp < 2) {   // warp hh: the combine weights of head hh, lane cc = chunk
-            const int hh = warp;
+        {
+            // warp w: head hh = w / 8; lane c computes partial c's weight, then
+            // lanes (d, half) of the warp add the even / odd partials of dim d.
+            const int hh = warp >> 3;
             const float* b = &S->w.pst[lane * kPartStride + hh * kHeadPart];
             const bool live = lane < gs && b[1] > 0.f;
-            const float m = live ? b[0] : -INFINITY;
-            const float M = warp_max(m);
-            const float e = live ? expf(m - M) : 0.f;
+            const float mm = live ? b[0] : -INFINITY;
+            const float M = warp_max(mm);
+            const float e = live ? expf(mm - M) : 0.f;
             const float den = warp_sum(live ? b[1] * e : 0.f);
-            if (lane < kMaxGS) S->gv[hh * 32 + lane] = e / den;
-        }
-        C.bar();
-        if (tid < 2 * HEAD_DIM) {
-            const int hh = tid >> 7, d = tid & 127;
+            const float wgt = e / den;
+            const int d = 16 * (warp & 7) + (lane & 15), half = lane >> 4;
             float num = 0.f;
-            for (int cc = 0; cc < gs; cc++) num = fmaf(S->w.pst[cc * kPartStride + hh * kHeadPart + 4 + d], S->gv[hh * 32 + cc], num);
-            S->os[tid] = num;
+            for (int i = 0; i < (gs + 1) / 2; i++) {
+                const int cc = 2 * i + half;
+                const float wc = __shfl_sync(0xffffffffu, wgt, cc & 31);
+                if (cc < gs) num = fmaf(S->w.pst[cc * kPartStride + hh * kHeadPart + 4 + d], wc, num);
+            }
+            num += __shfl_xor_sync(0xffffffffu, num, 16);
+            if (half == 0) S->os[hh * HEAD_DIM + d] = num;
         }
         QB_SUB(11);
         C.bar();
         QB_SUB(12);
         {
             float o8[8];
-            #pragma unroll
-            for (int e = 0; e < 8; e++) o8[e] = S->os[8 * lane + e];
-            uint64_t* y = P.yw + (size_t)(l * kGroups + g) * DIM;
-            for (int r = pl.oa; r < pl.ob; r += kRowsWo) {
-                const int cnt = min(kRowsWo, pl.ob - r);
-                const uint8_t* ch = C.wait_chunk();
-                QB_SUB(13);
-                for (int i = warp; i < cnt; i += kNCW) {
-                    const uint4 w = ((const uint4*)(ch + (size_t)i * 512))[lane];
-                    const float a = warp_sum(dot8(w, o8, 0.f));
-                    if (lane == 0) S->w.hs[r - pl.oa + i] = a;
-                }
-                QB_SUB(14);
-                C.release_chunk();
+            {
+                const float4 oa = *(const float4*)&S->os[8 * lane], ob = *(const float4*)&S->os[8 * lane + 4];
+                o8[0] = oa.x; o8[1] = oa.y; o8[2] = oa.z; o8[3] = oa.w; o8[4] = ob.x; o8[5] = ob.y; o8[6] = ob.z; o8[7] = ob.w;
             }
-            C.bar();
-            if (tid < pl.ob - pl.oa) xw_store(y + pl.oa + tid, S->w.hs[tid], seq);
+            uint64_t* y = P.yw + (size_t)(l * kGroups + g) * DIM;
+            for (int r = pl.oa; r < pl.ob; r += kRowsWo) {   // warp w: rows 4w .. 4w+3 of the chunk
+                const int cnt = min(kRowsWo, pl.ob - r);
+                const uint8_t* ch = C.chunk(0);
+                QB_SUB(13);
+                float v[4];
+                #pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int i = 4 * warp + q;
+                    v[q] = i < cnt ? dot8(((const uint4*)(ch + (size_t)i * 512))[lane], o8, 0.f) : 0.f;
+                }
+                #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    #pragma unroll
+                    for (int q = 0; q < 4; q++) v[q] += __shfl_xor_sync(0xffffffffu, v[q], o);
+                }
+                if (lane < 4 && 4 * warp + lane < cnt)   // lanes 0..3: one 32-byte store request
+                    xw_store(y + r + 4 * warp + lane, lane == 0 ? v[0] : (lane == 1 ? v[1] : (lane == 2 ? v[2] : v[3])), seq);
+                QB_SUB(14);
+                C.release(1);
+            }
         }
         QB_TRACE(TB + 5);
 
         // ---------------- MLP-A ----------------
         {
+            const uint4 gv = C.gain_fetch(P.post_ln[l]);
             const int j = tid * 2;
             const uint64_t* yb = P.yw + (size_t)l * kGroups * DIM + j;
             QB_SUB(16);
@@ -820,29 +886,34 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             }
             QB_SUB(17);
             S->xres[j] = x0; S->xres[j + 1] = x1;
-            ss = C.block_sum(x0 * x0 + x1 * x1);
-        }
-        QB_TRACE(TB + 6);
-        QB_SUB(34);
-        {
-            const uint8_t* ch = C.wait_chunk();
-            C.norm_into_xs((const uint16_t*)ch, ss);
-            C.release_chunk();
-        }
-        C.bar();
-        {
+            C.gain_park(gv);
+            const float ss = C.block_sum(x0 * x0 + x1 * x1);
+            QB_TRACE(TB + 6);
+            QB_SUB(34);
+            const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
             float xr[32];
-            C.load_regs(S->xs, xr);
+            C.norm_regs(S->xres, r, xr);
             QB_SUB(20);
-            C.rows_1024(pl.ha, pl.hb, xr, [&](int r, float v) { S->gv[r - pl.ha] = v; });
-            QB_SUB(21);
-            C.rows_1024(pl.ha, pl.hb, xr, [&](int r, float v) { S->uv[r - pl.ha] = v; });
+            // gate|up units, 8 per chunk, two chunks at a time: warp w takes unit w
+            uint64_t* hw = P.hw + (size_t)l * HIDDEN_DIM;
+            for (int u = pl.ha; u < pl.hb; u += 2 * kUnitsGU) {
+                const int n = min(2 * kUnitsGU, pl.hb - u);
+                const uint32_t nc = n > kUnitsGU ? 2 : 1;
+                const uint8_t* c0 = C.chunk(0);
+                const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
+                if (warp < n) {
+                    const uint8_t* row = (warp < kUnitsGU ? c0 : c1) + (size_t)(warp & (kUnitsGU - 1)) * 2 * DIM;
+                    float gt = C.row_part<8, 4>(row, xr), up = C.row_part<8, 4>(row + kUpOff, xr);
+                    #pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        gt += __shfl_xor_sync(0xffffffffu, gt, o);
+                        up += __shfl_xor_sync(0xffffffffu, up, o);
+                    }
+                    if (lane == 0) xw_store(hw + u + warp, (gt / (1.0f + expf(-gt))) * up, seq);
+                }
+                C.release(nc);
+            }
             QB_SUB(22);
-        }
-        C.bar();
-        if (tid < pl.hb - pl.ha) {
-            const float gt = S->gv[tid];
-            xw_store(P.hw + (size_t)l * HIDDEN_DIM + pl.ha + tid, (gt / (1.0f + expf(-gt))) * S->uv[tid], seq);
         }
         QB_TRACE(TB + 7);
         QB_SUB(35);
@@ -859,34 +930,40 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         }
         C.bar();
         QB_TRACE(TB + 8);
-        const long long cy0 = clock64();
         {
-            // warp -> (row rw of the chunk, 1024-column segment sg); 5 rows x 3 segments
-            const int rw = warp / 3, sg = warp % 3;
-            float xr[32];
-            C.load_regs(S->w.hs + 1024 * sg, xr);
-            if (tr && l == 13) tr[384 + 40] = clock64() - cy0;
+            // warp w: column quarter sg = w % 4 (768 columns) of rows w / 4 and
+            // w / 4 + 4 of a pair of Wd chunks
+            const int sg = warp & 3, ra = warp >> 2;
+            float xr[24];
+            #pragma unroll
+            for (int i = 0; i < 6; i++) {
+                const float4 a = *(const float4*)&S->w.hs[768 * sg + 128 * i + 4 * lane];
+                xr[4 * i + 0] = a.x; xr[4 * i + 1] = a.y; xr[4 * i + 2] = a.z; xr[4 * i + 3] = a.w;
+            }
             uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
-            for (int r = pl.da; r < pl.db; r += kRowsK3072) {
-                const int n = min(kRowsK3072, pl.db - r);
-                const uint8_t* ch = C.wait_chunk();
-                if (tr && l == 13 && r == pl.da) tr[384 + 41] = clock64() - cy0;
+            for (int r = pl.da; r < pl.db; r += 2 * kRowsWd) {
+                const int n = min(2 * kRowsWd, pl.db - r);
+                const uint32_t nc = n > kRowsWd ? 2 : 1;
+                const uint8_t* c0 = C.chunk(0);
+                const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
                 QB_SUB(28);
-                if (rw < n) {
-                    const float v = C.row_dot(ch + (size_t)rw * 2 * HIDDEN_DIM + (size_t)sg * 2 * 1024, xr);
-                    if (lane == 0) S->part[warp] = v;
+                float v0 = 0.f, v1 = 0.f;
+                if (ra < n) v0 = C.row_part<6, 3>(c0 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
+                if (ra + kRowsWd < n) v1 = C.row_part<6, 3>(c1 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
+                #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    v0 += __shfl_xor_sync(0xffffffffu, v0, o);
+                    v1 += __shfl_xor_sync(0xffffffffu, v1, o);
                 }
-                QB_SUB(29);
-                if (tr && l == 13 && r == pl.da) tr[384 + 42] = clock64() - cy0;
-                C.release_chunk();
+                if (lane == 0) { S->part[ra][sg] = v0; S->part[ra + kRowsWd][sg] = v1; }
+                C.release(nc);
                 C.bar();
-                if (tr && l == 13 && r == pl.da) tr[384 + 43] = clock64() - cy0;
                 QB_SUB(30);
                 if (tid < n) {
-                    const float v = S->xres[r + tid] + ((S->part[3 * tid] + S->part[3 * tid + 1]) + S->part[3 * tid + 2]);
-                    xw_store(xn + r + tid, v, seq);
+                    const float* q = S->part[tid];
+                    xw_store(xn + r + tid, S->xres[r + tid] + ((q[0] + q[1]) + (q[2] + q[3])), seq);
                 }
-                C.bar();
+                if (r + 2 * kRowsWd < pl.db) C.bar();   // S->part is rewritten by the next pair
             }
         }
         C.bar();     // S->w.hs and S->xres are reused by the next layer
@@ -901,31 +978,27 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
     const bool greedy = (P.in->temperature == 0.0f || P.in->top_k == 1);
     const int K = greedy ? 1 : min(P.in->top_k, kMaxCand);
     if (head) {
+        const uint4 gv = C.gain_fetch(P.final_ln);
         float ss;
         {
             const int j = tid * 2;
             const uint64_t* p = P.xw + (size_t)N_LAYERS * DIM + j;
             float xv[2];
             C.gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
-            const float x0 = xv[0], x1 = xv[1];
-            S->xres[j] = x0; S->xres[j + 1] = x1;
-            ss = C.block_sum(x0 * x0 + x1 * x1);
+            S->xres[j] = xv[0]; S->xres[j + 1] = xv[1];
+            C.gain_park(gv);
+            ss = C.block_sum(xv[0] * xv[0] + xv[1] * xv[1]);
         }
         QB_TRACE(kTrHead);
-        {
-            const uint8_t* ch = C.wait_chunk();
-            C.norm_into_xs((const uint16_t*)ch, ss);
-            C.release_chunk();
-        }
-        C.bar();
         const int va = pl.va;
         const bool wl = (flags & kFlagWriteLogits) != 0;
         {
+            const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
             float xr[32];
-            C.load_regs(S->xs, xr);
-            C.rows_1024(pl.va, pl.vb, xr, [&](int r, float v) {
-                S->w.lg[r - va] = v;
-                if (wl) P.logits[r] = v;
+            C.norm_regs(S->xres, r, xr);
+            C.rows_1024(pl.va, pl.vb, xr, [&](int row, float v) {
+                S->w.lg[row - va] = v;
+                if (wl) P.logits[row] = v;
             });
         }
         C.bar();
@@ -943,7 +1016,6 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         }
     }
     QB_TRACE(kTrHead + 1);
-    if (tr) tr[384 + 51] = clock64();
     C.flush();
     // last CTA to arrive merges and samples
     C.bar();
@@ -982,23 +1054,23 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 const int a2 = __shfl_xor_sync(0xffffffffu, at, o);
                 if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; at = a2; }
             }
-            if (lane == 0) { S->bred[0][warp] = v; S->bidx[warp] = i; S->bred[1][warp] = __int_as_float(at); }
+            if (lane == 0) { S->av[warp] = v; S->ai[warp] = i; S->am[warp] = __int_as_float(at); }
             C.bar();
             if (tid == 0) {
-                float bv = S->bred[0][0]; int bi = S->bidx[0]; int ba = __float_as_int(S->bred[1][0]);
+                float bv = S->av[0]; int bi = S->ai[0]; int ba = __float_as_int(S->am[0]);
                 for (int w = 1; w < kNCW; w++) {
-                    const float v2 = S->bred[0][w]; const int i2 = S->bidx[w];
-                    if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; ba = __float_as_int(S->bred[1][w]); }
+                    const float v2 = S->av[w]; const int i2 = S->ai[w];
+                    if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; ba = __float_as_int(S->am[w]); }
                 }
                 P.top_v[kk] = bv; P.top_i[kk] = bi;
-                S->gv[kk] = bv;
-                ((int*)S->uv)[kk] = bi;
+                S->tv[kk] = bv;
+                S->ti[kk] = bi;
                 if (ba >= 0) { cv[ba] = -INFINITY; ci[ba] = 0x7fffffff; }
             }
             C.bar();
         }
         if (tid == 0) {
-            const int* ids = (const int*)S->uv;
+            const int* ids = S->ti;
             float* prob = S->w.hs;
             unsigned long long rng = P.in->rng;
             if (greedy) {
@@ -1007,9 +1079,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 // sampler.h:137-174 over the K candidates, scanned in descending order
                 const float T = P.in->temperature, topp = P.in->topp;
                 int nc = K;
-                const float mx = S->gv[0];
+                const float mx = S->tv[0];
                 float sum = 0.f;
-                for (int i = 0; i < nc; i++) { const float e = expf((S->gv[i] - mx) / T); prob[i] = e; sum += e; }
+                for (int i = 0; i < nc; i++) { const float e = expf((S->tv[i] - mx) / T); prob[i] = e; sum += e; }
                 for (int i = 0; i < nc; i++) prob[i] /= sum;
                 if (topp > 0.0f && topp < 1.0f) {
                     float cum = 0.f; int last = nc - 1;

@@ -322,8 +322,6 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     P.poll_ns = 0;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
-    P.ring_slots = kSlots;
-    if (const char* e = getenv("QWEN_B200_SLOTS")) P.ring_slots = std::max(2, std::min(kSlots, atoi(e)));
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
