@@ -174,7 +174,7 @@ struct __align__(16) DecodeSmem {
     float kn[HEAD_DIM];      // the new position's k and v (bf16-rounded)
     float vn[HEAD_DIM];
     float rope[HEAD_DIM];    // cos | sin of this position
-    uint16_t gain[DIM];      // the RMSNorm gains in use (bf16)
+    float xs[DIM];           // the RMSNorm output in use
     float os[2 * HEAD_DIM];  // the group's attention output
     float part[8][4];        // MLP-B: row x column-quarter partial dots
     float bsum[2][kNCW];     // block sums, two buffers used alternately
@@ -359,9 +359,10 @@ struct ChunkIter {
 // P.prefetch_chunks chunks ahead of the producer; it keeps HBM streaming while
 // the ring is full because consumers wait on another CTA.
 // ---------------------------------------------------------------------------
+template <bool kTr>
 __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, const Plan& pl) {
     const uint64_t pol = policy_evict_first();
-    unsigned long long* tr = P.trace ? P.trace + (size_t)c * kTraceStride : nullptr;
+    unsigned long long* tr = (kTr && P.trace) ? P.trace + (size_t)c * kTraceStride : nullptr;
     ChunkIter it;
     Seg seg[3];
     uint32_t k = 0;
@@ -419,6 +420,7 @@ __device__ __noinline__ void decode_prefetcher(const DecodeParams& P, DecodeSmem
 // ---------------------------------------------------------------------------
 // Consumers
 // ---------------------------------------------------------------------------
+template <bool kTr>
 struct Consumer {
     const DecodeParams* P;
     uint8_t* ring;
@@ -433,7 +435,7 @@ struct Consumer {
     int k13 = -1;                        // first ring chunk of layer 13 (cycle trace)
     unsigned long long ring_ns = 0, xw_ns = 0;   // thread 0's waits in layer tl (written by flush)
     __device__ __forceinline__ void flush() {                    // stores only: no global read on the timed path
-        if (tr) { tr[320 + tl] = ring_ns; tr[352 + tl] = xw_ns; }
+        if (kTr && tr) { tr[320 + tl] = ring_ns; tr[352 + tl] = xw_ns; }
         ring_ns = 0; xw_ns = 0;
     }
 
@@ -442,11 +444,11 @@ struct Consumer {
     __device__ __forceinline__ const uint8_t* chunk(uint32_t i) {
         const uint32_t kk = k + i;
         const uint32_t s = kk % kSlots, ph = (kk / kSlots) & 1u;
-        const uint64_t t0 = tr ? global_ns() : 0;
-        if (tr && tl == 13) { if (k13 < 0) k13 = (int)kk; if ((int)kk - k13 < 32) tr[480 + kk - k13] = clock64(); }
+        const uint64_t t0 = kTr && tr ? global_ns() : 0;
+        if (kTr && tr && tl == 13) { if (k13 < 0) k13 = (int)kk; if ((int)kk - k13 < 32) tr[480 + kk - k13] = clock64(); }
         const bool ok = *(volatile int*)&S->abort || mbar_wait(&S->full[s], ph, 3 * kWaitNs);
-        if (tr) ring_ns += global_ns() - t0;
-        if (tr && tl == 13 && (int)kk - k13 < 32) tr[512 + kk - k13] = clock64();
+        if (kTr && tr) ring_ns += global_ns() - t0;
+        if (kTr && tr && tl == 13 && (int)kk - k13 < 32) tr[512 + kk - k13] = clock64();
         if (!ok) {
             *(volatile int*)&S->abort = 1;
             atomicOr(&P->out->err, 4u);
@@ -486,7 +488,7 @@ struct Consumer {
             if (waiting == 0) {
                 #pragma unroll
                 for (int i = 0; i < N; i++) { v[2 * i] = __uint_as_float((uint32_t)a[i]); v[2 * i + 1] = __uint_as_float((uint32_t)b[i]); }
-                if (tr && t0) xw_ns += global_ns() - t0;
+                if (kTr && tr && t0) xw_ns += global_ns() - t0;
                 return;
             }
             if (t0 == 0) t0 = global_ns();
@@ -543,25 +545,23 @@ struct Consumer {
         for (int w = 1; w < kNCW; w++) better(v, i, S->av[w], S->ai[w]);
         bar();
     }
-    // RMSNorm gains: threads 0..127 fetch one 16-byte piece each before a
-    // gather (four registers held across it) and park it in shared memory
-    // after; the block_sum barrier that follows publishes the gains.
-    __device__ __forceinline__ uint4 gain_fetch(const uint16_t* g) {
-        return tid < DIM / 8 ? __ldg((const uint4*)(g + 8 * tid)) : make_uint4(0u, 0u, 0u, 0u);
+    // RMSNorm of the 1024-wide x whose pair j = 2 tid, 2 tid + 1 this thread
+    // holds (x0, x1; gains g2 = its two bf16 gains, fetched before the gather),
+    // given the block's sum of squares: writes S->xs, then a barrier.
+    __device__ __forceinline__ void norm_xs(float x0, float x1, uint32_t g2, float ss) {
+        const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+        *(float2*)&S->xs[2 * tid] = make_float2((x0 * r) * bf_lo(g2), (x1 * r) * bf_hi(g2));
+        bar();
     }
-    __device__ __forceinline__ void gain_park(uint4 v) {
-        if (tid < DIM / 8) *(uint4*)&S->gain[8 * tid] = v;
-    }
-    // This lane's 32 RMSNorm outputs of the 1024-wide x in shared memory:
-    // xr[4i + e] = (x[j] * r) * gain[j] with j = 128 i + 4 lane + e (each
-    // warp-wide load is 512 contiguous bytes: no bank conflicts).
-    __device__ __forceinline__ void norm_regs(const float* x, float r, float* xr) {
+    __device__ __forceinline__ uint32_t gain_fetch(const uint16_t* g) { return __ldg((const uint32_t*)(g + 2 * tid)); }
+    // This lane's 32 values of a 1024-wide vector in shared memory:
+    // xr[4i + e] = v[128 i + 4 lane + e] (each warp-wide load is 512
+    // contiguous bytes: no bank conflicts).
+    __device__ __forceinline__ void load_regs(const float* v, float* xr) {
         #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const float4 a = *(const float4*)&x[128 * i + 4 * lane];
-            const uint2 gw = *(const uint2*)&S->gain[128 * i + 4 * lane];
-            xr[4 * i + 0] = (a.x * r) * bf_lo(gw.x); xr[4 * i + 1] = (a.y * r) * bf_hi(gw.x);
-            xr[4 * i + 2] = (a.z * r) * bf_lo(gw.y); xr[4 * i + 3] = (a.w * r) * bf_hi(gw.y);
+            const float4 a = *(const float4*)&v[128 * i + 4 * lane];
+            xr[4 * i + 0] = a.x; xr[4 * i + 1] = a.y; xr[4 * i + 2] = a.z; xr[4 * i + 3] = a.w;
         }
     }
     // This lane's partial dot of a bf16 row segment of 128 * NI columns with
@@ -614,20 +614,21 @@ struct Consumer {
     }
 };
 
+template <bool kTr>
 __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, int G, const Plan& pl,
                                              int token, int pos, int flags, uint32_t seq) {
-    Consumer C;
+    Consumer<kTr> C;
     C.P = &P; C.ring = ring; C.S = S;
     C.tid = threadIdx.x; C.warp = C.tid >> 5; C.lane = C.tid & 31;
     C.tag = seq;
     const int tid = C.tid, warp = C.warp, lane = C.lane;
-    if (P.trace && tid == 0) C.tr = P.trace + (size_t)c * kTraceStride;
+    if (kTr && P.trace && tid == 0) C.tr = P.trace + (size_t)c * kTraceStride;
     const int g = pl.g, gs = pl.gs, gr = pl.gr;
     const bool owner = (gr == gs - 1);                 // its position range ends at pos
     const float sqrt_hd = sqrtf((float)HEAD_DIM);
-    unsigned long long* tr = (P.trace && tid == 0) ? P.trace + (size_t)c * kTraceStride : nullptr;
-#define QB_TRACE(i) do { if (tr) tr[(i)] = global_ns(); } while (0)
-#define QB_SUB(i) do { if (tr && l == 13) tr[384 + (i)] = clock64(); } while (0)   // cycles: exact within a CTA
+    unsigned long long* tr = (kTr && P.trace && tid == 0) ? P.trace + (size_t)c * kTraceStride : nullptr;
+#define QB_TRACE(i) do { if (kTr && tr) tr[(i)] = global_ns(); } while (0)
+#define QB_SUB(i) do { if (kTr && tr && l == 13) tr[384 + (i)] = clock64(); } while (0)   // cycles: exact within a CTA
     QB_TRACE(0);
 
     if (tid < HEAD_DIM) S->rope[tid] = __ldg(P.rope + (size_t)pos * HEAD_DIM + tid);
@@ -638,7 +639,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         C.tl = l;
         // ---------------- QKV ----------------
         {
-            const uint4 gv = C.gain_fetch(P.in_ln[l]);
+            const uint32_t g2 = C.gain_fetch(P.in_ln[l]);
             const int j = tid * 2;
             float xv[2];
             if (l == 0) {
@@ -646,16 +647,15 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 xv[0] = bf_lo(w); xv[1] = bf_hi(w);
             } else {
                 const uint64_t* p = P.xw + (size_t)l * DIM + j;
-                C.gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
+                C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
             }
             S->xres[j] = xv[0]; S->xres[j + 1] = xv[1];
-            C.gain_park(gv);
             const float ss = C.block_sum(xv[0] * xv[0] + xv[1] * xv[1]);
             QB_SUB(31);
             QB_TRACE(TB + 0);
-            const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+            C.norm_xs(xv[0], xv[1], g2, ss);
             float xr[32];
-            C.norm_regs(S->xres, r, xr);
+            C.load_regs(S->xs, xr);
             uint64_t* qkv = P.qkvw + (size_t)l * 4096;
             C.rows_1024(pl.qa, pl.qb, xr, [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v, seq); });
         }
@@ -669,7 +669,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             uint2 gn = make_uint2(0u, 0u);
             if (warp < 3) gn = __ldg((const uint2*)((warp < 2 ? P.qn[l] : P.kn[l]) + 4 * lane));
             float x[4];
-            C.gather<2>([&](int i) { return p + 2 * i; }, 3u, x, 10 * l + 2);
+            C.template gather<2>([&](int i) { return p + 2 * i; }, 3u, x, 10 * l + 2);
             if (warp < 3) {
                 const float tot = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
                 const float r = 1.0f / sqrtf(tot * (1.0f / HEAD_DIM) + EPS);
@@ -808,7 +808,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             for (int i = 0; i < kPer; i++) if (2 * tid + 2 * kNCT * i < nw) pend |= 1u << i;
             float v[2 * kPer];
             QB_SUB(8);
-            C.gather<kPer>([&](int i) { return gbase + 2 * tid + 2 * kNCT * i; }, pend, v, 10 * l + 4);
+            C.template gather<kPer>([&](int i) { return gbase + 2 * tid + 2 * kNCT * i; }, pend, v, 10 * l + 4);
             #pragma unroll
             for (int i = 0; i < kPer; i++) {
                 if (pend & (1u << i)) *(float2*)&S->w.pst[2 * tid + 2 * kNCT * i] = make_float2(v[2 * i], v[2 * i + 1]);
@@ -873,26 +873,25 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 
         // ---------------- MLP-A ----------------
         {
-            const uint4 gv = C.gain_fetch(P.post_ln[l]);
+            const uint32_t g2 = C.gain_fetch(P.post_ln[l]);
             const int j = tid * 2;
             const uint64_t* yb = P.yw + (size_t)l * kGroups * DIM + j;
             QB_SUB(16);
             float x0 = S->xres[j], x1 = S->xres[j + 1];
             {
                 float yv[2 * kGroups];
-                C.gather<kGroups>([&](int gg) { return yb + (size_t)gg * DIM; }, (1u << kGroups) - 1u, yv, 10 * l + 6);
+                C.template gather<kGroups>([&](int gg) { return yb + (size_t)gg * DIM; }, (1u << kGroups) - 1u, yv, 10 * l + 6);
                 #pragma unroll
                 for (int gg = 0; gg < kGroups; gg++) { x0 += yv[2 * gg]; x1 += yv[2 * gg + 1]; }
             }
             QB_SUB(17);
             S->xres[j] = x0; S->xres[j + 1] = x1;
-            C.gain_park(gv);
             const float ss = C.block_sum(x0 * x0 + x1 * x1);
             QB_TRACE(TB + 6);
             QB_SUB(34);
-            const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+            C.norm_xs(x0, x1, g2, ss);
             float xr[32];
-            C.norm_regs(S->xres, r, xr);
+            C.load_regs(S->xs, xr);
             QB_SUB(20);
             // gate|up units, 8 per chunk, two chunks at a time: warp w takes unit w
             uint64_t* hw = P.hw + (size_t)l * HIDDEN_DIM;
@@ -903,7 +902,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
                 if (warp < n) {
                     const uint8_t* row = (warp < kUnitsGU ? c0 : c1) + (size_t)(warp & (kUnitsGU - 1)) * 2 * DIM;
-                    float gt = C.row_part<8, 4>(row, xr), up = C.row_part<8, 4>(row + kUpOff, xr);
+                    float gt = C.template row_part<8, 4>(row, xr), up = C.template row_part<8, 4>(row + kUpOff, xr);
                     #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
                         gt += __shfl_xor_sync(0xffffffffu, gt, o);
@@ -924,7 +923,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             constexpr int kHP = HIDDEN_DIM / (2 * kNCT);
             float hv[2 * kHP];
             QB_SUB(25);
-            C.gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
+            C.template gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
             #pragma unroll
             for (int i = 0; i < kHP; i++) *(float2*)&S->w.hs[2 * tid + 2 * kNCT * i] = make_float2(hv[2 * i], hv[2 * i + 1]);
         }
@@ -948,8 +947,8 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
                 QB_SUB(28);
                 float v0 = 0.f, v1 = 0.f;
-                if (ra < n) v0 = C.row_part<6, 3>(c0 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
-                if (ra + kRowsWd < n) v1 = C.row_part<6, 3>(c1 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
+                if (ra < n) v0 = C.template row_part<6, 3>(c0 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
+                if (ra + kRowsWd < n) v1 = C.template row_part<6, 3>(c1 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
                 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     v0 += __shfl_xor_sync(0xffffffffu, v0, o);
@@ -978,24 +977,23 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
     const bool greedy = (P.in->temperature == 0.0f || P.in->top_k == 1);
     const int K = greedy ? 1 : min(P.in->top_k, kMaxCand);
     if (head) {
-        const uint4 gv = C.gain_fetch(P.final_ln);
-        float ss;
+        const uint32_t g2 = C.gain_fetch(P.final_ln);
+        float ss, x0, x1;
         {
             const int j = tid * 2;
             const uint64_t* p = P.xw + (size_t)N_LAYERS * DIM + j;
             float xv[2];
-            C.gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
-            S->xres[j] = xv[0]; S->xres[j + 1] = xv[1];
-            C.gain_park(gv);
-            ss = C.block_sum(xv[0] * xv[0] + xv[1] * xv[1]);
+            C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
+            x0 = xv[0]; x1 = xv[1];
+            ss = C.block_sum(x0 * x0 + x1 * x1);
         }
         QB_TRACE(kTrHead);
         const int va = pl.va;
         const bool wl = (flags & kFlagWriteLogits) != 0;
         {
-            const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+            C.norm_xs(x0, x1, g2, ss);
             float xr[32];
-            C.norm_regs(S->xres, r, xr);
+            C.load_regs(S->xs, xr);
             C.rows_1024(pl.va, pl.vb, xr, [&](int row, float v) {
                 S->w.lg[row - va] = v;
                 if (wl) P.logits[row] = v;
@@ -1124,6 +1122,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 #undef QB_SUB
 }
 
+// kTr: the tracing build (stage time stamps into P.trace); the other build has
+// no trace code at all.
+template <bool kTr>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
@@ -1149,14 +1150,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     __syncthreads();
     const Plan& pl = S->pl;
     if ((tid >> 5) == kNCW) {
-        if ((tid & 31) == 0) decode_producer(P, ring, S, c, pl);
+        if ((tid & 31) == 0) decode_producer<kTr>(P, ring, S, c, pl);
         return;
     }
     if ((tid >> 5) == kNCW + 1) {
         if ((tid & 31) == 0) decode_prefetcher(P, S, pl);
         return;
     }
-    decode_consumer(P, ring, S, c, G, pl, token, pos, flags, seq);
+    decode_consumer<kTr>(P, ring, S, c, G, pl, token, pos, flags, seq);
 }
 
 }  // namespace qb

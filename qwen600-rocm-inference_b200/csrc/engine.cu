@@ -248,12 +248,14 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         (HIDDEN_DIM + c->nsm - 1) / c->nsm > kMaxMlpRows) {
         ctx_free(c); return fail(QWEN_E_UNSUPPORTED, "unsupported SM count " + std::to_string(c->nsm));
     }
-    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemBytes) != cudaSuccess) {
-        ctx_free(c); return fail(QWEN_E_CUDA, "cannot reserve " + std::to_string(kDecodeSmemBytes) + " B of shared memory");
-    }
-    int nb = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_kernel, kThreads, kDecodeSmemBytes) != cudaSuccess || nb < 1) {
-        ctx_free(c); return fail(QWEN_E_CUDA, "decode kernel cannot be resident on every SM");
+    for (auto kern : {decode_kernel<false>, decode_kernel<true>}) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemBytes) != cudaSuccess) {
+            ctx_free(c); return fail(QWEN_E_CUDA, "cannot reserve " + std::to_string(kDecodeSmemBytes) + " B of shared memory");
+        }
+        int nb = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kThreads, kDecodeSmemBytes) != cudaSuccess || nb < 1) {
+            ctx_free(c); return fail(QWEN_E_CUDA, "decode kernel cannot be resident on every SM");
+        }
     }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "stream creation failed"); }
 
@@ -351,7 +353,8 @@ static int launch_decode(qwen_t* c) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    CU(cudaLaunchKernelEx(&cfg, decode_kernel, c->params));
+    if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true>, c->params));
+    else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false>, c->params));
     return QWEN_OK;
 }
 

@@ -43,12 +43,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// As mbar_try_wait, but the thread may be suspended in hardware for up to
+// `hint_ns` while the phase is incomplete (woken when it completes), so a
+// waiting thread takes no issue slots from the warps beside it.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait for the phase with the given parity to complete.  Returns false
-// if `limit_ns` elapsed first.
+// if `limit_ns` elapsed first.  Each poll may suspend the thread for up to 20 us.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
         if (global_ns() - t0 > limit_ns) return false;
     }
     return true;

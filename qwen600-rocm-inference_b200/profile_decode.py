@@ -1,0 +1,46 @@
+"""A small decode case for profilers (ncu) and quick timing.
+
+    python qwen600-rocm-inference_b200/profile_decode.py [--prompt N] [--steps K] [--device D]
+
+Builds an Engine on the seed-0 synthetic checkpoint, prefills N seeded prompt
+tokens (rng 1000, as bench.py does: N launches of the decode kernel), then
+decodes K greedy positions with qwen_decode_step (one launch each) and prints
+the host wall time per step.  ncu counts --launch-skip over the launches that
+match its kernel filter, so
+
+    ncu --set full --clock-control none -k regex:decode_kernel -s <N + 1> -c 1 ...
+
+captures the second decode step: position N + 1, context N + 2.
+"""
+import argparse
+import importlib.util
+import os
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--device", type=int, default=0)
+    a = ap.parse_args()
+    spec = importlib.util.spec_from_file_location("qwen_b200", os.path.join(HERE, "qwen_b200.py"))
+    qb = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(qb)
+    import numpy as np
+    eng = qb.Engine(qb.default_checkpoint(0), a.device)
+    prompt = np.random.default_rng(1000).integers(0, qb.VOCAB_SIZE, a.prompt).tolist()
+    eng.prefill(prompt, 0)
+    tok = prompt[-1]
+    t0 = time.perf_counter()
+    for pos in range(a.prompt, a.prompt + a.steps):
+        tok, _ = eng.decode_step(tok, pos)
+    dt = time.perf_counter() - t0
+    eng.close()
+    print(f"prompt {a.prompt} steps {a.steps}: {dt / max(a.steps, 1) * 1e6:.1f} us per step (host wall time)")
+
+
+if __name__ == "__main__":
+    main()
