@@ -48,6 +48,7 @@
 // StepOut.err, stops waiting on other CTAs, still drains its own copies, and
 // returns; the host then resets the exchange buffers.
 #pragma once
+#include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 #include "ptx.cuh"
@@ -58,7 +59,7 @@ namespace qb {
 constexpr int kNCW = 16;                    // consumer warps
 constexpr int kNCT = kNCW * 32;             // consumer threads
 constexpr int kThreads = kNCT + 64;         // + one producer warp + one L2-prefetch warp
-constexpr int kSlots = 4;
+constexpr int kSlots = 6;
 constexpr int kSlotBytes = 32768;
 constexpr int kGroups = N_KV_HEADS;         // one CTA group per KV head
 constexpr int kMaxGS = 19;                  // max CTAs per group (grid <= 152)
@@ -163,20 +164,20 @@ struct Plan {          // this CTA's share of every stage
 struct __align__(16) DecodeSmem {
     uint64_t full[kSlots];
     uint64_t empty[kSlots];
-    float xres[DIM];         // layer input x_l, then x_mid
-    union {                  // one stage at a time (a barrier separates users)
+    alignas(16) float xres[DIM];         // layer input x_l, then x_mid
+    alignas(16) union {                  // one stage at a time (a barrier separates users)
         float hs[HIDDEN_DIM];                 // MLP-B: h; head merge: probabilities
         float comb[kNCW * HEAD_DIM];          // ATT: per-warp accumulators
         float pst[kMaxGS * kPartStride];      // OPROJ: the group's partials
         float lg[kMaxLocalRows];              // HEAD: local logits
     } w;
-    float qs[2 * HEAD_DIM];  // the group's two q heads (normed, rotated)
-    float kn[HEAD_DIM];      // the new position's k and v (bf16-rounded)
-    float vn[HEAD_DIM];
-    float rope[HEAD_DIM];    // cos | sin of this position
-    float xs[DIM];           // the RMSNorm output in use
-    float os[2 * HEAD_DIM];  // the group's attention output
-    float part[8][4];        // MLP-B: row x column-quarter partial dots
+    alignas(16) float qs[2 * HEAD_DIM];  // the group's two q heads (normed, rotated)
+    alignas(16) float kn[HEAD_DIM];      // the new position's k and v (bf16-rounded)
+    alignas(16) float vn[HEAD_DIM];
+    alignas(16) float rope[HEAD_DIM];    // cos | sin of this position
+    alignas(16) float xs[DIM];           // the RMSNorm output in use
+    alignas(16) float os[2 * HEAD_DIM];  // the group's attention output
+    alignas(16) float part[8][4];        // MLP-B: row x column-quarter partial dots
     float bsum[2][kNCW];     // block sums, two buffers used alternately
     float am[kNCW], al[kNCW];   // ATT: per-warp running max and sum
     float av[kNCW];          // block argmax
@@ -188,6 +189,13 @@ struct __align__(16) DecodeSmem {
     unsigned int copied;     // chunks the producer has issued (read by the prefetch warp)
     Plan pl;                 // this CTA's share of every stage (one copy, in shared memory)
 };
+// every array read or written with 8- or 16-byte vector accesses starts on a 16-byte boundary
+static_assert(offsetof(DecodeSmem, xres) % 16 == 0 && offsetof(DecodeSmem, w) % 16 == 0 &&
+              offsetof(DecodeSmem, qs) % 16 == 0 && offsetof(DecodeSmem, kn) % 16 == 0 &&
+              offsetof(DecodeSmem, vn) % 16 == 0 && offsetof(DecodeSmem, xs) % 16 == 0 &&
+              offsetof(DecodeSmem, os) % 16 == 0 && offsetof(DecodeSmem, part) % 16 == 0,
+              "shared-memory arrays must be 16-byte aligned");
+static_assert((kSlots * kSlotBytes) % 16 == 0, "the ring keeps DecodeSmem 16-byte aligned");
 constexpr size_t kDecodeSmemBytes = (size_t)kSlots * kSlotBytes + sizeof(DecodeSmem);
 
 // [n*i/parts, n*(i+1)/parts)

@@ -320,7 +320,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     P.lm_begin = 0; P.lm_end = VOCAB_SIZE;
     // tuning knobs (environment, read once per handle): L2 prefetch lead in
     // chunks, back-off in ns between polls of an exchange word
-    P.prefetch_chunks = 16;
+    P.prefetch_chunks = 0;
     P.poll_ns = 0;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
