@@ -171,6 +171,65 @@ def ref_cuda_rate(ck, n_prompt=768, n_timed=200):
                     "because its attention is wrong beyond 1024 positions"}
 
 
+GEMV_SHAPES = [(1024, 4096), (2048, 1024), (1024, 6144), (3072, 1024), (1024, 151936)]   # (K, N)
+
+
+def gemv_sweep(qb, peak):
+    """Isolated bf16 GEMV y = bf16(W x) through qwen_gemv_bf16 at the decode
+    chain's shapes: x ~ N(0,1), W ~ N(0,0.02) from a seed, fp32 accumulate, bf16
+    out.  Each timed launch is bracketed alone by CUDA events on the launching
+    stream, with a 256 MB write between launches to flush the 126 MB L2; the
+    reported time is the median of 20."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    out = []
+    for k, n in GEMV_SHAPES:
+        W = (torch.randn(n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        x = torch.randn(k, generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        call = lambda: qb.gemv_bf16(W.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, stream.cuda_stream)
+        for _ in range(3):
+            call()
+        ts = []
+        for _ in range(20):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        us = float(np.median(ts))
+        nbytes = n * k * 2 + k * 2 + n * 2
+        out.append({"k": k, "n": n, "bytes": nbytes, "us": us, "gbs": nbytes / (us * 1e-6) / 1e9,
+                    "frac": nbytes / (us * 1e-6) / 1e9 / peak})
+        del W, x, y
+    del flush
+    torch.cuda.empty_cache()
+    return out
+
+
+def long_context(qb, ck, n_prompt=4096, n_gen=512):
+    """4096 seeded prompt tokens, then 512 sampled tokens (temperature 0.6,
+    top-k 20, top-p 0.95, seeded xorshift64*), KV cache sized 8192: decode
+    tok/s from the device time of the 512 chained launches."""
+    eng = qb.Engine(ck, 0)
+    try:
+        prompt = np.random.default_rng(4096).integers(0, 151936, n_prompt).tolist()
+        t0 = time.perf_counter()
+        eng.prefill(prompt, 0)
+        pre_s = time.perf_counter() - t0
+        sp = qb.Sampling(0.6, 0.95, 20)
+        toks, rng, ms = eng.generate_timed(prompt[-1], n_prompt, n_gen, sp, 0x5EED)
+    finally:
+        eng.close()
+    return {"value": n_gen / (ms / 1e3), "unit": "tok/s", "prompt_tokens": n_prompt, "sampled_tokens": n_gen,
+            "sampling": {"temperature": 0.6, "top_k": 20, "top_p": 0.95}, "ms_per_token": ms / n_gen,
+            "prefill_tok_s": n_prompt / pre_s}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -276,13 +335,16 @@ def run_mine(args):
                 "prefill": {"value": PROMPT_LEN / prefill_s, "unit": "tok/s", "tokens": PROMPT_LEN,
                             "path": "one decode-kernel launch per prompt position, LM head skipped (qwen_prefill)"}}
         if world == 1:
+            eng.close()
+            torch.cuda.empty_cache()
+            line["gemv_sweep"] = {"shapes": gemv_sweep(qb, peak), "peak_gbs": peak,
+                                  "l2": "flushed (256 MB write) between timed launches"}
+            line["long_context"] = long_context(qb, ck)
             import oracle_py as O
             threads = os.cpu_count() or 1
             rate, n, dt = cpu_oracle_rate(ck, O.FP32, 15.0, 400, threads)
             line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
                                     "sample": f"{n} decode tokens at context 1024 ({dt:.1f} s), fp32 oracle, {threads} threads"}
-            eng.close()
-            torch.cuda.empty_cache()
             try:
                 line["reference_cuda_b200"] = ref_cuda_rate(ck)
             except Exception as e:   # informational only

@@ -51,6 +51,10 @@ int qwen_abi_version(void);
 /* Number of tensors in the model's canonical weight layout (static_loader.h:81, NUM_TENSORS = 311). */
 int qwen_num_tensors(void);
 
+/* VOCAB_SIZE of this build (config.h); lets callers size logits buffers without
+ * config.h.  No reference counterpart (the reference uses the constant). */
+int qwen_vocab_size(void);
+
 /* Total bytes of the canonical device weight block (static_loader.h:80, TOTAL_WEIGHTS_BYTES). */
 size_t qwen_total_weight_bytes(void);
 

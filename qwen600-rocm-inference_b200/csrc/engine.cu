@@ -45,6 +45,7 @@ extern "C" int qwen_abi_version(void) { return 10000; }
 // tensor table / checkpoint
 // ---------------------------------------------------------------------------
 extern "C" int qwen_num_tensors(void) { return (int)canonical_table().size(); }
+extern "C" int qwen_vocab_size(void) { return VOCAB_SIZE; }
 extern "C" size_t qwen_total_weight_bytes(void) { return canonical_total_bytes(); }
 extern "C" int qwen_tensor_info(int index, const char** name, size_t* offset, size_t* bytes) {
     const auto& t = canonical_table();

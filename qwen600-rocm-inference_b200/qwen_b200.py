@@ -36,6 +36,7 @@ _SIGS = {
     "qwen_last_error": (_c.c_char_p, []),
     "qwen_abi_version": (_c.c_int, []),
     "qwen_num_tensors": (_c.c_int, []),
+    "qwen_vocab_size": (_c.c_int, []),
     "qwen_total_weight_bytes": (_c.c_size_t, []),
     "qwen_tensor_info": (_c.c_int, [_c.c_int, _c.POINTER(_c.c_char_p), _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)]),
     "qwen_checkpoint_validate": (_c.c_int, [_c.c_char_p]),
