@@ -59,7 +59,7 @@ namespace qb {
 constexpr int kNCW = 16;                    // consumer warps
 constexpr int kNCT = kNCW * 32;             // consumer threads
 constexpr int kThreads = kNCT + 64;         // + one producer warp + one L2-prefetch warp
-constexpr int kSlots = 6;
+constexpr int kSlots = 5;
 constexpr int kSlotBytes = 32768;
 constexpr int kGroups = N_KV_HEADS;         // one CTA group per KV head
 constexpr int kMaxGS = 19;                  // max CTAs per group (grid <= 152)
@@ -121,7 +121,7 @@ struct DecodeParams {
     const uint16_t* wg[N_LAYERS];
     const uint16_t* wu[N_LAYERS];
     const uint16_t* wd[N_LAYERS];
-    const uint16_t* wo_g;    // [L][8][DIM][256]  Wo columns of group g, row-major
+    const uint16_t* wo_g;    // [L][8][DIM][kWoCols]  Wo columns of group g, row-major, padded
     uint16_t* kc;            // [L][8][SEQ][128]
     uint16_t* vc;            // [L][8][SEQ][128]
     const float* rope;       // [SEQ][128] cos[64] | sin[64]
@@ -161,23 +161,28 @@ struct Plan {          // this CTA's share of every stage
     size_t kvbase;     // element offset of (layer 0, head g) in the K/V cache
 };
 
+// B-operand fragments of an activation vector v for mma.m16n8k16: v is split
+// into three bf16 parts (v = hi + mid + lo to fp32 precision) in columns 0, 1
+// and 2; columns 3..7 are zero.  frag[kt][lane][reg] for k-tile kt and lanes
+// 0..11 (the only lanes whose B registers are nonzero).
+constexpr int kFragLanes = 12;
 struct __align__(16) DecodeSmem {
     uint64_t full[kSlots];
     uint64_t empty[kSlots];
     alignas(16) float xres[DIM];         // layer input x_l, then x_mid
     alignas(16) union {                  // one stage at a time (a barrier separates users)
-        float hs[HIDDEN_DIM];                 // MLP-B: h; head merge: probabilities
+        uint32_t bh[HIDDEN_DIM / 16][kFragLanes][2];   // MLP-B: fragments of h
         float comb[kNCW * HEAD_DIM];          // ATT: per-warp accumulators
         float pst[kMaxGS * kPartStride];      // OPROJ: the group's partials
-        float lg[kMaxLocalRows];              // HEAD: local logits
+        float lg[kMaxLocalRows];              // HEAD: local logits; merge: probabilities
     } w;
+    alignas(16) uint32_t bx[DIM / 16][kFragLanes][2];          // fragments of the RMSNorm output in use (HEAD: the fp32 output)
+    alignas(16) uint32_t bo[2 * HEAD_DIM / 16][kFragLanes][2]; // fragments of the group's attention output
+    alignas(16) float red[2][kNCW][32];  // per-warp MMA partial sums (two 16-row tiles), two buffers used alternately
     alignas(16) float qs[2 * HEAD_DIM];  // the group's two q heads (normed, rotated)
     alignas(16) float kn[HEAD_DIM];      // the new position's k and v (bf16-rounded)
     alignas(16) float vn[HEAD_DIM];
     alignas(16) float rope[HEAD_DIM];    // cos | sin of this position
-    alignas(16) float xs[DIM];           // the RMSNorm output in use
-    alignas(16) float os[2 * HEAD_DIM];  // the group's attention output
-    alignas(16) float part[8][4];        // MLP-B: row x column-quarter partial dots
     float bsum[2][kNCW];     // block sums, two buffers used alternately
     float am[kNCW], al[kNCW];   // ATT: per-warp running max and sum
     float av[kNCW];          // block argmax
@@ -190,13 +195,15 @@ struct __align__(16) DecodeSmem {
     Plan pl;                 // this CTA's share of every stage (one copy, in shared memory)
 };
 // every array read or written with 8- or 16-byte vector accesses starts on a 16-byte boundary
+static_assert(sizeof(DecodeSmem::bx) >= DIM * sizeof(float), "the head keeps its fp32 RMSNorm output in bx");
 static_assert(offsetof(DecodeSmem, xres) % 16 == 0 && offsetof(DecodeSmem, w) % 16 == 0 &&
               offsetof(DecodeSmem, qs) % 16 == 0 && offsetof(DecodeSmem, kn) % 16 == 0 &&
-              offsetof(DecodeSmem, vn) % 16 == 0 && offsetof(DecodeSmem, xs) % 16 == 0 &&
-              offsetof(DecodeSmem, os) % 16 == 0 && offsetof(DecodeSmem, part) % 16 == 0,
+              offsetof(DecodeSmem, vn) % 16 == 0 && offsetof(DecodeSmem, bx) % 16 == 0 &&
+              offsetof(DecodeSmem, bo) % 16 == 0 && offsetof(DecodeSmem, red) % 16 == 0,
               "shared-memory arrays must be 16-byte aligned");
 static_assert((kSlots * kSlotBytes) % 16 == 0, "the ring keeps DecodeSmem 16-byte aligned");
 constexpr size_t kDecodeSmemBytes = (size_t)kSlots * kSlotBytes + sizeof(DecodeSmem);
+static_assert(kDecodeSmemBytes <= 227 * 1024, "one CTA per SM: at most 227 KB of shared memory");
 
 // [n*i/parts, n*(i+1)/parts)
 __host__ __device__ __forceinline__ int span_lo(int n, int parts, int i) { return (int)(((long long)n * i) / parts); }
@@ -234,23 +241,35 @@ __device__ __forceinline__ void xw_load2(const uint64_t* p, uint64_t& a, uint64_
 
 // ---------------------------------------------------------------------------
 // The chunk sequence.  One CTA's weight / KV stream, in consumption order:
-//   per layer: [QKV rows, 16/chunk]
+//   per layer: [QKV rows, 15/chunk]
 //              [K | V of cached positions, 64/chunk: K at 0, V at 16 KB]
-//              [Wo_g rows, 64/chunk]
-//              [gate|up units, 8/chunk: gate rows at 0, up rows at 16 KB]
+//              [Wo_g rows (packed, padded), 62/chunk]
+//              [gate|up units, 7/chunk: gate rows 0..6, up rows 7..13]
 //              [Wd rows (3072 wide), 4/chunk]
-//   then (unless kFlagNoHead): [LM-head rows, 16/chunk]
+//   then (unless kFlagNoHead): [LM-head rows, 16/chunk, one bulk copy]
+// Layer weight rows land kPad bytes apart beyond their length (one bulk copy
+// per row), the layout the tensor-core tiles read conflict-free.  The LM head
+// is pure streaming (no hop, 2.1 MB per CTA): its rows stay contiguous and are
+// dotted on the FP32 pipe.
 // RMSNorm gains are not streamed: every lane loads the few it needs from L2.
 // The producer walks the sequence twice (an L2-prefetch cursor ahead of the
 // copy cursor); the consumers' code visits the same chunks in the same order.
 // ---------------------------------------------------------------------------
-constexpr int kRowsK1024 = kSlotBytes / (2 * DIM);        // 16 rows of 1024 bf16
-constexpr int kUnitsGU = kSlotBytes / (4 * DIM);          // 8 gate|up units per chunk
-constexpr int kUpOff = kUnitsGU * 2 * DIM;                // up rows at 16 KB
-constexpr int kRowsWd = 4;                                // Wd rows (3072 bf16) per chunk
+// Weight rows land in a slot 16 bytes apart beyond their length, so the eight
+// rows an ldmatrix reads start in eight different bank groups.
+constexpr int kPad = 16;
+constexpr int kStride1024 = 2 * DIM + kPad;                // 2064 B per 1024-wide row
+constexpr int kRowsK1024 = kSlotBytes / kStride1024;       // 15 rows per chunk
+constexpr int kUnitsGU = 7;                                // gate rows 0..6, up rows 7..13 of a chunk
+constexpr int kStrideWd = 2 * HIDDEN_DIM + kPad;           // 6160 B per Wd row
+constexpr int kRowsWd = 4;                                 // Wd rows per chunk
+constexpr int kWoCols = 256 + kPad / 2;                    // packed Wo row, padded in HBM
+constexpr int kStrideWo = 2 * kWoCols;                     // 528 B
+constexpr int kRowsWo = kSlotBytes / kStrideWo;            // 62 rows per chunk
+constexpr int kRowsLM = kSlotBytes / (2 * DIM);            // 16 LM-head rows per chunk (unpadded: FFMA path)
 constexpr int kKVChunk = 64;                               // positions per K|V chunk
 constexpr int kVOff = kKVChunk * 2 * HEAD_DIM;             // V offset in a K|V chunk
-constexpr int kRowsWo = kSlotBytes / (2 * 256);            // 64 rows of 256 bf16
+static_assert(2 * kUnitsGU * kStride1024 <= kSlotBytes && kRowsWd * kStrideWd <= kSlotBytes, "chunks fit a slot");
 
 __device__ __forceinline__ Plan make_plan(const DecodeParams& P, int c, int G, int pos, int flags) {
     Plan p;
@@ -269,10 +288,13 @@ __device__ __forceinline__ Plan make_plan(const DecodeParams& P, int c, int G, i
     return p;
 }
 
-struct Seg {
+struct Seg {            // `rows` copies of `bytes` each: source rows src_stride apart, slot rows dst_stride apart
     const uint8_t* src;
     uint32_t bytes;
-    uint32_t off;      // destination offset inside the slot
+    uint32_t off;      // destination offset of the first row inside the slot
+    uint32_t rows;
+    uint32_t src_stride;
+    uint32_t dst_stride;
 };
 
 struct ChunkIter {
@@ -297,7 +319,8 @@ struct ChunkIter {
                         else if (rr < 384) { src = P.wk[l] + (size_t)(128 * pl.g + rr - 256) * DIM; lim = 384; }
                         else { src = P.wv[l] + (size_t)(128 * pl.g + rr - 384) * DIM; lim = 512; }
                         const int m = min(n - i, lim - rr);
-                        seg[k++] = {(const uint8_t*)src, (uint32_t)(m * 2 * DIM), (uint32_t)(i * 2 * DIM)};
+                        seg[k++] = {(const uint8_t*)src, (uint32_t)(2 * DIM), (uint32_t)(i * kStride1024), (uint32_t)m,
+                                    (uint32_t)(2 * DIM), (uint32_t)kStride1024};
                         i += m;
                     }
                     r += n;
@@ -309,8 +332,8 @@ struct ChunkIter {
                 if (r < pl.pe) {
                     const int n = min(kKVChunk, pl.pe - r);
                     const size_t e = ((size_t)l * kGroups * SEQ_LEN * HEAD_DIM) + pl.kvbase + (size_t)r * HEAD_DIM;
-                    seg[0] = {(const uint8_t*)(P.kc + e), (uint32_t)(n * 2 * HEAD_DIM), 0};
-                    seg[1] = {(const uint8_t*)(P.vc + e), (uint32_t)(n * 2 * HEAD_DIM), (uint32_t)kVOff};
+                    seg[0] = {(const uint8_t*)(P.kc + e), (uint32_t)(n * 2 * HEAD_DIM), 0, 1, 0, 0};
+                    seg[1] = {(const uint8_t*)(P.vc + e), (uint32_t)(n * 2 * HEAD_DIM), (uint32_t)kVOff, 1, 0, 0};
                     r += n;
                     return 2;
                 }
@@ -319,7 +342,8 @@ struct ChunkIter {
             case 3:
                 if (r < pl.ob) {
                     const int n = min(kRowsWo, pl.ob - r);
-                    seg[0] = {(const uint8_t*)(P.wo_g + ((size_t)(l * kGroups + pl.g) * DIM + r) * 256), (uint32_t)(n * 512), 0};
+                    seg[0] = {(const uint8_t*)(P.wo_g + ((size_t)(l * kGroups + pl.g) * DIM + r) * kWoCols), (uint32_t)(n * kStrideWo), 0,
+                              1, 0, 0};
                     r += n;
                     return 1;
                 }
@@ -328,8 +352,10 @@ struct ChunkIter {
             case 5:
                 if (r < pl.hb) {
                     const int n = min(kUnitsGU, pl.hb - r);
-                    seg[0] = {(const uint8_t*)(P.wg[l] + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0};
-                    seg[1] = {(const uint8_t*)(P.wu[l] + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), (uint32_t)kUpOff};
+                    seg[0] = {(const uint8_t*)(P.wg[l] + (size_t)r * DIM), (uint32_t)(2 * DIM), 0, (uint32_t)n,
+                              (uint32_t)(2 * DIM), (uint32_t)kStride1024};
+                    seg[1] = {(const uint8_t*)(P.wu[l] + (size_t)r * DIM), (uint32_t)(2 * DIM), (uint32_t)(kUnitsGU * kStride1024),
+                              (uint32_t)n, (uint32_t)(2 * DIM), (uint32_t)kStride1024};
                     r += n;
                     return 2;
                 }
@@ -338,7 +364,8 @@ struct ChunkIter {
             case 7:
                 if (r < pl.db) {
                     const int n = min(kRowsWd, pl.db - r);
-                    seg[0] = {(const uint8_t*)(P.wd[l] + (size_t)r * HIDDEN_DIM), (uint32_t)(n * 2 * HIDDEN_DIM), 0};
+                    seg[0] = {(const uint8_t*)(P.wd[l] + (size_t)r * HIDDEN_DIM), (uint32_t)(2 * HIDDEN_DIM), 0, (uint32_t)n,
+                              (uint32_t)(2 * HIDDEN_DIM), (uint32_t)kStrideWd};
                     r += n;
                     return 1;
                 }
@@ -347,8 +374,8 @@ struct ChunkIter {
                 break;
             case 9:
                 if (r < pl.vb) {
-                    const int n = min(kRowsK1024, pl.vb - r);
-                    seg[0] = {(const uint8_t*)(P.lm + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0};
+                    const int n = min(kRowsLM, pl.vb - r);
+                    seg[0] = {(const uint8_t*)(P.lm + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0, 1, 0, 0};
                     r += n;
                     return 1;
                 }
@@ -393,10 +420,13 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
         if (tr && it.cur_st == 9 && !head_seen) { tr[316] = global_ns(); head_seen = true; }
         if (!dead) {
             uint32_t total = 0;
-            for (int i = 0; i < n; i++) total += seg[i].bytes;
+            for (int i = 0; i < n; i++) total += seg[i].bytes * seg[i].rows;
             mbar_arrive_expect_tx(&S->full[s], total);
             uint8_t* d = ring + (size_t)s * kSlotBytes;
-            for (int i = 0; i < n; i++) bulk_g2s(d + seg[i].off, seg[i].src, seg[i].bytes, &S->full[s], pol);
+            for (int i = 0; i < n; i++)
+                for (uint32_t r = 0; r < seg[i].rows; r++)
+                    bulk_g2s(d + seg[i].off + r * seg[i].dst_stride, seg[i].src + (size_t)r * seg[i].src_stride, seg[i].bytes,
+                             &S->full[s], pol);
         }
         k++;
         *(volatile unsigned int*)&S->copied = k;
@@ -420,7 +450,8 @@ __device__ __noinline__ void decode_prefetcher(const DecodeParams& P, DecodeSmem
             __nanosleep(256);
             if (global_ns() - t0 > 4 * kWaitNs) return;
         }
-        for (int i = 0; i < n; i++) bulk_prefetch_l2(seg[i].src, seg[i].bytes);
+        for (int i = 0; i < n; i++)
+            for (uint32_t r = 0; r < seg[i].rows; r++) bulk_prefetch_l2(seg[i].src + (size_t)r * seg[i].src_stride, seg[i].bytes);
         npf++;
     }
 }
@@ -553,18 +584,69 @@ struct Consumer {
         for (int w = 1; w < kNCW; w++) better(v, i, S->av[w], S->ai[w]);
         bar();
     }
-    // RMSNorm of the 1024-wide x whose pair j = 2 tid, 2 tid + 1 this thread
-    // holds (x0, x1; gains g2 = its two bf16 gains, fetched before the gather),
-    // given the block's sum of squares: writes S->xs, then a barrier.
-    __device__ __forceinline__ void norm_xs(float x0, float x1, uint32_t g2, float ss) {
+    __device__ __forceinline__ uint32_t gain_fetch(const uint16_t* g) { return __ldg((const uint32_t*)(g + 2 * tid)); }
+    // Writes the B fragments of elements k, k+1 (k even) of a vector: the
+    // bf16 high parts to lanes 0..3, the next bf16 parts to lanes 4..7 and the
+    // last to lanes 8..11 (each subtraction is exact in fp32).
+    __device__ __forceinline__ void put_pair(uint32_t* frag, int k, float v0, float v1) {
+        const int kt = k >> 4, w = k & 15, q = (w & 7) >> 1, reg = w >> 3;
+        const uint16_t h0 = f2bf(v0), h1 = f2bf(v1);
+        const float r0 = v0 - bf2f(h0), r1 = v1 - bf2f(h1);
+        const uint16_t m0 = f2bf(r0), m1 = f2bf(r1);
+        const uint16_t l0 = f2bf(r0 - bf2f(m0)), l1 = f2bf(r1 - bf2f(m1));
+        uint32_t* f = frag + (kt * kFragLanes + q) * 2 + reg;
+        f[0] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        f[8] = (uint32_t)m0 | ((uint32_t)m1 << 16);    // lane q + 4
+        f[16] = (uint32_t)l0 | ((uint32_t)l1 << 16);   // lane q + 8
+    }
+    // RMSNorm of the 1024-wide x whose pair 2 tid, 2 tid + 1 this thread holds
+    // (x0, x1; g2 = its two bf16 gains), given the block's sum of squares:
+    // writes the fragments S->bx, then a barrier.
+    __device__ __forceinline__ void norm_bx(float x0, float x1, uint32_t g2, float ss) {
         const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
-        *(float2*)&S->xs[2 * tid] = make_float2((x0 * r) * bf_lo(g2), (x1 * r) * bf_hi(g2));
+        put_pair(&S->bx[0][0][0], 2 * tid, (x0 * r) * bf_lo(g2), (x1 * r) * bf_hi(g2));
         bar();
     }
-    __device__ __forceinline__ uint32_t gain_fetch(const uint16_t* g) { return __ldg((const uint32_t*)(g + 2 * tid)); }
-    // This lane's 32 values of a 1024-wide vector in shared memory:
-    // xr[4i + e] = v[128 i + 4 lane + e] (each warp-wide load is 512
-    // contiguous bytes: no bank conflicts).
+    // Row tile x k-tile products on the tensor cores (mma.m16n8k16, bf16 in,
+    // fp32 accumulate): ta[t] = this lane's ldmatrix address (shared space) of
+    // tile t at k-tile 0 — row lane % 16, 16-byte half lane / 16 — and bfr the
+    // fragments.  Accumulates k-tiles [kt0, kt0 + nkt) into d[t].
+    template <int NT>
+    __device__ __forceinline__ void mma_tiles(const uint32_t (&ta)[NT], const uint32_t* bfr, int kt0, int nkt, float (&d)[NT][4]) {
+        #pragma unroll 4
+        for (int kt = kt0; kt < kt0 + nkt; kt++) {
+            uint32_t b0 = 0u, b1 = 0u;
+            if (lane < kFragLanes) { const uint2 b = *(const uint2*)&bfr[(kt * kFragLanes + lane) * 2]; b0 = b.x; b1 = b.y; }
+            #pragma unroll
+            for (int t = 0; t < NT; t++) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(ta[t] + kt * 32, a0, a1, a2, a3);
+                mma_bf16_16816(d[t], a0, a1, a2, a3, b0, b1);
+            }
+        }
+    }
+    // This warp's 16-row partial sums of tile t (d = its accumulator) into
+    // red[warp][16 t ..]: columns 0 + 1 + 2 = the dot with v's three parts;
+    // lane 4g holds columns 0, 1 and lane 4g + 1 column 2 of rows g and g + 8.
+    __device__ __forceinline__ void put_red(float* red, int t, const float (&d)[4]) {
+        const float c2a = __shfl_down_sync(0xffffffffu, d[0], 1), c2b = __shfl_down_sync(0xffffffffu, d[2], 1);
+        if ((lane & 3) == 0) {
+            const int r = lane >> 2;
+            red[warp * 32 + 16 * t + r] = (d[0] + d[1]) + c2a;
+            red[warp * 32 + 16 * t + r + 8] = (d[2] + d[3]) + c2b;
+        }
+    }
+    uint32_t rbp = 0;   // S->red buffer parity
+    __device__ __forceinline__ float* next_red() { float* r = &S->red[rbp][0][0]; rbp ^= 1u; return r; }
+    // ---- LM head (FP32 pipe) ----
+    // RMSNorm output as fp32 into v (a 1024-float shared buffer), then a barrier.
+    __device__ __forceinline__ void norm_f32(float* v, float x0, float x1, uint32_t g2, float ss) {
+        const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+        *(float2*)&v[2 * tid] = make_float2((x0 * r) * bf_lo(g2), (x1 * r) * bf_hi(g2));
+        bar();
+    }
+    // This lane's 32 values of a 1024-wide vector: xr[4i + e] = v[128 i + 4 lane + e]
+    // (each warp-wide load is 512 contiguous bytes: no bank conflicts).
     __device__ __forceinline__ void load_regs(const float* v, float* xr) {
         #pragma unroll
         for (int i = 0; i < 8; i++) {
@@ -572,45 +654,33 @@ struct Consumer {
             xr[4 * i + 0] = a.x; xr[4 * i + 1] = a.y; xr[4 * i + 2] = a.z; xr[4 * i + 3] = a.w;
         }
     }
-    // This lane's partial dot of a bf16 row segment of 128 * NI columns with
-    // xr (xr[4i + e] <-> column 128 i + 4 lane + e), in C independent chains.
-    template <int NI, int C>
-    __device__ __forceinline__ float row_part(const uint8_t* row, const float* xr) {
+    // This lane's partial dot of a 1024-wide bf16 row with xr, four chains.
+    __device__ __forceinline__ float row_part_f32(const uint8_t* row, const float* xr) {
         const uint2* w = (const uint2*)row;
-        float a[C];
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
         #pragma unroll
-        for (int c = 0; c < C; c++) a[c] = 0.f;
-        #pragma unroll
-        for (int i = 0; i < NI; i++) {
+        for (int i = 0; i < 8; i++) {
             const uint2 v = w[i * 32 + lane];
-            float& t = a[i % C];
+            float& t = a[i & 3];
             t = fmaf(bf_lo(v.x), xr[4 * i + 0], t); t = fmaf(bf_hi(v.x), xr[4 * i + 1], t);
             t = fmaf(bf_lo(v.y), xr[4 * i + 2], t); t = fmaf(bf_hi(v.y), xr[4 * i + 3], t);
         }
-        if constexpr (C == 4) {
-            return (a[0] + a[1]) + (a[2] + a[3]);
-        } else {
-            float t = a[0];
-            #pragma unroll
-            for (int c = 1; c < C; c++) t += a[c];
-            return t;
-        }
+        return (a[0] + a[1]) + (a[2] + a[3]);
     }
-    // Rows [a, b) of 1024 columns, 16 per chunk, two chunks at a time: warp w
-    // takes rows 2w and 2w + 1 of the 32; f(row, value) runs on lanes 0 and 1,
-    // so a warp's two results leave in one store request.
+    // LM-head rows [a, b), 16 per chunk, two chunks at a time: warp w takes
+    // rows 2w and 2w + 1 of the 32; f(row, value) runs on lanes 0 and 1.
     template <typename F>
-    __device__ __forceinline__ void rows_1024(int a, int b, const float* xr, F&& f) {
-        for (int r = a; r < b; r += 2 * kRowsK1024) {
-            const int n = min(2 * kRowsK1024, b - r);
-            const uint32_t nc = n > kRowsK1024 ? 2 : 1;
+    __device__ __forceinline__ void rows_lm(int a, int b, const float* xr, F&& f) {
+        for (int r = a; r < b; r += 2 * kRowsLM) {
+            const int n = min(2 * kRowsLM, b - r);
+            const uint32_t nc = n > kRowsLM ? 2 : 1;
             const uint8_t* c0 = chunk(0);
             const uint8_t* c1 = nc == 2 ? chunk(1) : c0;
-            const uint8_t* ch = (2 * warp < kRowsK1024 ? c0 : c1) + (size_t)((2 * warp) & (kRowsK1024 - 1)) * 2 * DIM;
+            const uint8_t* ch = (2 * warp < kRowsLM ? c0 : c1) + (size_t)((2 * warp) & (kRowsLM - 1)) * 2 * DIM;
             const bool v0 = 2 * warp < n, v1 = 2 * warp + 1 < n;
             float s0 = 0.f, s1 = 0.f;
-            if (v0) s0 = row_part<8, 4>(ch, xr);
-            if (v1) s1 = row_part<8, 4>(ch + 2 * DIM, xr);
+            if (v0) s0 = row_part_f32(ch, xr);
+            if (v1) s1 = row_part_f32(ch + 2 * DIM, xr);
             #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
                 s0 += __shfl_xor_sync(0xffffffffu, s0, o);
@@ -618,6 +688,38 @@ struct Consumer {
             }
             if (lane < 2 && 2 * warp + lane < n) f(r + 2 * warp + lane, lane == 0 ? s0 : s1);
             release(nc);
+        }
+    }
+    // Rows [a, b) of 1024 columns (15 per chunk), two chunks per round: tile t
+    // = the rows of chunk t; warp w takes k-tiles 4w .. 4w+3 of both tiles; the
+    // sixteen partial sums of a row are added in warp order by thread i after
+    // one barrier, which calls f(row, value).
+    template <typename F>
+    __device__ __forceinline__ void rows_1024(int a, int b, const uint32_t* bfr, F&& f) {
+        const int lr = lane & 15;
+        for (int r = a; r < b; r += 2 * kRowsK1024) {
+            const int n = min(2 * kRowsK1024, b - r);
+            const uint32_t nc = n > kRowsK1024 ? 2 : 1;
+            const int n0 = min(n, kRowsK1024), n1 = n - n0;
+            const uint8_t* c0 = chunk(0);
+            const uint8_t* c1 = nc == 2 ? chunk(1) : c0;
+            uint32_t ta[2];
+            ta[0] = smem_addr(c0 + (size_t)(lr < n0 ? lr : 0) * kStride1024) + (lane >> 4) * 16;
+            ta[1] = smem_addr(c1 + (size_t)(lr < n1 ? lr : 0) * kStride1024) + (lane >> 4) * 16;
+            float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            mma_tiles<2>(ta, bfr, 4 * warp, 4, d);
+            float* red = next_red();
+            put_red(red, 0, d[0]);
+            put_red(red, 1, d[1]);
+            release(nc);
+            bar();
+            if (tid < n) {
+                const int i = tid < kRowsK1024 ? tid : 16 + tid - kRowsK1024;
+                float v = 0.f;
+                #pragma unroll
+                for (int w = 0; w < kNCW; w++) v += red[w * 32 + i];
+                f(r + tid, v);
+            }
         }
     }
 };
@@ -661,11 +763,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             const float ss = C.block_sum(xv[0] * xv[0] + xv[1] * xv[1]);
             QB_SUB(31);
             QB_TRACE(TB + 0);
-            C.norm_xs(xv[0], xv[1], g2, ss);
-            float xr[32];
-            C.load_regs(S->xs, xr);
+            C.norm_bx(xv[0], xv[1], g2, ss);
             uint64_t* qkv = P.qkvw + (size_t)l * 4096;
-            C.rows_1024(pl.qa, pl.qb, xr, [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v, seq); });
+            C.rows_1024(pl.qa, pl.qb, &S->bx[0][0][0], [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v, seq); });
         }
         QB_TRACE(TB + 1);
         QB_SUB(32);
@@ -844,37 +944,35 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 if (cc < gs) num = fmaf(S->w.pst[cc * kPartStride + hh * kHeadPart + 4 + d], wc, num);
             }
             num += __shfl_xor_sync(0xffffffffu, num, 16);
-            if (half == 0) S->os[hh * HEAD_DIM + d] = num;
+            const float nx = __shfl_down_sync(0xffffffffu, num, 1);   // dim d + 1
+            if (half == 0 && (d & 1) == 0) C.put_pair(&S->bo[0][0][0], hh * HEAD_DIM + d, num, nx);
         }
         QB_SUB(11);
         C.bar();
         QB_SUB(12);
         {
-            float o8[8];
-            {
-                const float4 oa = *(const float4*)&S->os[8 * lane], ob = *(const float4*)&S->os[8 * lane + 4];
-                o8[0] = oa.x; o8[1] = oa.y; o8[2] = oa.z; o8[3] = oa.w; o8[4] = ob.x; o8[5] = ob.y; o8[6] = ob.z; o8[7] = ob.w;
-            }
+            // tile t = rows 16t .. 16t+15 of the chunk (up to 62 rows); warp w:
+            // tile w % 4, k-tiles 4 (w / 4) .. +3 of the 16; four warps per row
             uint64_t* y = P.yw + (size_t)(l * kGroups + g) * DIM;
-            for (int r = pl.oa; r < pl.ob; r += kRowsWo) {   // warp w: rows 4w .. 4w+3 of the chunk
+            const int t = warp & 3, lr = lane & 15;
+            for (int r = pl.oa; r < pl.ob; r += kRowsWo) {
                 const int cnt = min(kRowsWo, pl.ob - r);
                 const uint8_t* ch = C.chunk(0);
                 QB_SUB(13);
-                float v[4];
-                #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int i = 4 * warp + q;
-                    v[q] = i < cnt ? dot8(((const uint4*)(ch + (size_t)i * 512))[lane], o8, 0.f) : 0.f;
-                }
-                #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    #pragma unroll
-                    for (int q = 0; q < 4; q++) v[q] += __shfl_xor_sync(0xffffffffu, v[q], o);
-                }
-                if (lane < 4 && 4 * warp + lane < cnt)   // lanes 0..3: one 32-byte store request
-                    xw_store(y + r + 4 * warp + lane, lane == 0 ? v[0] : (lane == 1 ? v[1] : (lane == 2 ? v[2] : v[3])), seq);
-                QB_SUB(14);
+                const int row = 16 * t + lr;
+                uint32_t ta[1] = {smem_addr(ch + (size_t)(row < cnt ? row : 0) * kStrideWo) + (lane >> 4) * 16};
+                float d[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+                C.template mma_tiles<1>(ta, &S->bo[0][0][0], 4 * (warp >> 2), 4, d);
+                float* red = C.next_red();
+                C.put_red(red, 0, d[0]);          // this warp's tile rows at red[warp][0..15]
                 C.release(1);
+                C.bar();
+                if (tid < cnt) {                  // row tid: tile tt, summed over warps tt, tt+4, tt+8, tt+12
+                    const int tt = tid >> 4, ri = tid & 15;
+                    const float v = ((red[tt * 32 + ri] + red[(tt + 4) * 32 + ri]) + red[(tt + 8) * 32 + ri]) + red[(tt + 12) * 32 + ri];
+                    xw_store(y + r + tid, v, seq);
+                }
+                QB_SUB(14);
             }
         }
         QB_TRACE(TB + 5);
@@ -897,28 +995,35 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             const float ss = C.block_sum(x0 * x0 + x1 * x1);
             QB_TRACE(TB + 6);
             QB_SUB(34);
-            C.norm_xs(x0, x1, g2, ss);
-            float xr[32];
-            C.load_regs(S->xs, xr);
+            C.norm_bx(x0, x1, g2, ss);
             QB_SUB(20);
-            // gate|up units, 8 per chunk, two chunks at a time: warp w takes unit w
+            // gate|up units, 7 per chunk (gate rows 0..6, up rows 7..13), two
+            // chunks per round: tile t = chunk t; warp w takes k-tiles 4w..4w+3
             uint64_t* hw = P.hw + (size_t)l * HIDDEN_DIM;
+            const int lr = lane & 15, lu = lr < kUnitsGU ? lr : lr - kUnitsGU;
             for (int u = pl.ha; u < pl.hb; u += 2 * kUnitsGU) {
                 const int n = min(2 * kUnitsGU, pl.hb - u);
                 const uint32_t nc = n > kUnitsGU ? 2 : 1;
+                const int n0 = min(n, kUnitsGU), n1 = n - n0;
                 const uint8_t* c0 = C.chunk(0);
                 const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
-                if (warp < n) {
-                    const uint8_t* row = (warp < kUnitsGU ? c0 : c1) + (size_t)(warp & (kUnitsGU - 1)) * 2 * DIM;
-                    float gt = C.template row_part<8, 4>(row, xr), up = C.template row_part<8, 4>(row + kUpOff, xr);
-                    #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        gt += __shfl_xor_sync(0xffffffffu, gt, o);
-                        up += __shfl_xor_sync(0xffffffffu, up, o);
-                    }
-                    if (lane == 0) xw_store(hw + u + warp, (gt / (1.0f + expf(-gt))) * up, seq);
-                }
+                uint32_t ta[2];
+                ta[0] = smem_addr(c0 + (size_t)(lr < 2 * kUnitsGU && lu < n0 ? lr : 0) * kStride1024) + (lane >> 4) * 16;
+                ta[1] = smem_addr(c1 + (size_t)(lr < 2 * kUnitsGU && lu < n1 ? lr : 0) * kStride1024) + (lane >> 4) * 16;
+                float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                C.template mma_tiles<2>(ta, &S->bx[0][0][0], 4 * warp, 4, d);
+                float* red = C.next_red();
+                C.put_red(red, 0, d[0]);
+                C.put_red(red, 1, d[1]);
                 C.release(nc);
+                C.bar();
+                if (tid < n) {   // unit tid of the round
+                    const int t = tid < kUnitsGU ? 0 : 1, uu = tid - t * kUnitsGU;
+                    float gt = 0.f, up = 0.f;
+                    #pragma unroll
+                    for (int w = 0; w < kNCW; w++) { gt += red[w * 32 + 16 * t + uu]; up += red[w * 32 + 16 * t + kUnitsGU + uu]; }
+                    xw_store(hw + u + tid, (gt / (1.0f + expf(-gt))) * up, seq);
+                }
             }
             QB_SUB(22);
         }
@@ -933,47 +1038,39 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             QB_SUB(25);
             C.template gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
             #pragma unroll
-            for (int i = 0; i < kHP; i++) *(float2*)&S->w.hs[2 * tid + 2 * kNCT * i] = make_float2(hv[2 * i], hv[2 * i + 1]);
+            for (int i = 0; i < kHP; i++) C.put_pair(&S->w.bh[0][0][0], 2 * tid + 2 * kNCT * i, hv[2 * i], hv[2 * i + 1]);
         }
         C.bar();
         QB_TRACE(TB + 8);
         {
-            // warp w: column quarter sg = w % 4 (768 columns) of rows w / 4 and
-            // w / 4 + 4 of a pair of Wd chunks
-            const int sg = warp & 3, ra = warp >> 2;
-            float xr[24];
-            #pragma unroll
-            for (int i = 0; i < 6; i++) {
-                const float4 a = *(const float4*)&S->w.hs[768 * sg + 128 * i + 4 * lane];
-                xr[4 * i + 0] = a.x; xr[4 * i + 1] = a.y; xr[4 * i + 2] = a.z; xr[4 * i + 3] = a.w;
-            }
+            // rows of Wd, two chunks (8 rows) per round as one tile: tile rows
+            // 0..3 = chunk 0, 4..7 = chunk 1; warp w takes k-tiles 12w..12w+11
             uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
+            const int lr = lane & 15;
             for (int r = pl.da; r < pl.db; r += 2 * kRowsWd) {
                 const int n = min(2 * kRowsWd, pl.db - r);
                 const uint32_t nc = n > kRowsWd ? 2 : 1;
                 const uint8_t* c0 = C.chunk(0);
                 const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
                 QB_SUB(28);
-                float v0 = 0.f, v1 = 0.f;
-                if (ra < n) v0 = C.template row_part<6, 3>(c0 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
-                if (ra + kRowsWd < n) v1 = C.template row_part<6, 3>(c1 + (size_t)ra * 2 * HIDDEN_DIM + (size_t)sg * 2 * 768, xr);
-                #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    v0 += __shfl_xor_sync(0xffffffffu, v0, o);
-                    v1 += __shfl_xor_sync(0xffffffffu, v1, o);
-                }
-                if (lane == 0) { S->part[ra][sg] = v0; S->part[ra + kRowsWd][sg] = v1; }
+                const uint8_t* rp = lr < n ? (lr < kRowsWd ? c0 + (size_t)lr * kStrideWd : c1 + (size_t)(lr - kRowsWd) * kStrideWd) : c0;
+                uint32_t ta[1] = {smem_addr(rp) + (lane >> 4) * 16};
+                float d[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+                C.template mma_tiles<1>(ta, &S->w.bh[0][0][0], 12 * warp, HIDDEN_DIM / 16 / kNCW, d);
+                float* red = C.next_red();
+                C.put_red(red, 0, d[0]);
                 C.release(nc);
                 C.bar();
                 QB_SUB(30);
                 if (tid < n) {
-                    const float* q = S->part[tid];
-                    xw_store(xn + r + tid, S->xres[r + tid] + ((q[0] + q[1]) + (q[2] + q[3])), seq);
+                    float v = 0.f;
+                    #pragma unroll
+                    for (int w = 0; w < kNCW; w++) v += red[w * 32 + tid];
+                    xw_store(xn + r + tid, S->xres[r + tid] + v, seq);
                 }
-                if (r + 2 * kRowsWd < pl.db) C.bar();   // S->part is rewritten by the next pair
             }
         }
-        C.bar();     // S->w.hs and S->xres are reused by the next layer
+        C.bar();     // S->w.bh and S->xres are reused by the next layer
         QB_TRACE(TB + 9);
         QB_SUB(36);
     }
@@ -999,10 +1096,11 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         const int va = pl.va;
         const bool wl = (flags & kFlagWriteLogits) != 0;
         {
-            C.norm_xs(x0, x1, g2, ss);
+            float* xs = reinterpret_cast<float*>(&S->bx[0][0][0]);   // 4 KB of the 6 KB fragment buffer
+            C.norm_f32(xs, x0, x1, g2, ss);
             float xr[32];
-            C.load_regs(S->xs, xr);
-            C.rows_1024(pl.va, pl.vb, xr, [&](int row, float v) {
+            C.load_regs(xs, xr);
+            C.rows_lm(pl.va, pl.vb, xr, [&](int row, float v) {
                 S->w.lg[row - va] = v;
                 if (wl) P.logits[row] = v;
             });
@@ -1077,7 +1175,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         }
         if (tid == 0) {
             const int* ids = S->ti;
-            float* prob = S->w.hs;
+            float* prob = S->w.lg;
             unsigned long long rng = P.in->rng;
             if (greedy) {
                 tok = ids[0];

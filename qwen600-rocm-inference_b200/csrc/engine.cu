@@ -144,11 +144,14 @@ extern "C" int qwen_weights_free(void* dev_block) {
 // load-time repacking
 // ---------------------------------------------------------------------------
 // Wo [DIM][Q_DIM] -> [8][DIM][256]: group g's 256 input columns contiguous per row.
+// One layer's Wo [1024][2048] -> [8 groups][1024 rows][kWoCols]: group g's 256
+// input columns of every row contiguous, then kWoCols - 256 zero pad columns.
 __global__ void pack_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __restrict__ wo_g) {
-    const size_t n = (size_t)DIM * Q_DIM;
+    const size_t n = (size_t)kGroups * DIM * kWoCols;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const int r = (int)(i / Q_DIM), col = (int)(i % Q_DIM), g = col / 256, cc = col % 256;
-        wo_g[((size_t)g * DIM + r) * 256 + cc] = wo[i];
+        const int g = (int)(i / ((size_t)DIM * kWoCols)), rem = (int)(i % ((size_t)DIM * kWoCols));
+        const int r = rem / kWoCols, cc = rem % kWoCols;
+        wo_g[i] = cc < 256 ? wo[(size_t)r * Q_DIM + 256 * g + cc] : (uint16_t)0;
     }
 }
 
@@ -263,7 +266,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     const size_t total = canonical_total_bytes();
     TRY(dalloc(&c->wblock, total));
     TRY(upload_checkpoint(path, m, c->wblock, c->stream));
-    TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * DIM * Q_DIM));
+    TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * kGroups * DIM * kWoCols));
     const size_t kv = (size_t)N_LAYERS * N_KV_HEADS * SEQ_LEN * HEAD_DIM;
     TRY(dalloc(&c->kc, kv));
     TRY(dalloc(&c->vc, kv));
@@ -310,7 +313,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         P.wq[l] = W(li.q_proj); P.wk[l] = W(li.k_proj); P.wv[l] = W(li.v_proj);
         P.qn[l] = W(li.q_norm); P.kn[l] = W(li.k_norm);
         P.wg[l] = W(li.gate); P.wu[l] = W(li.up); P.wd[l] = W(li.down);
-        pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * DIM * Q_DIM);
+        pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * kGroups * DIM * kWoCols);
     }
     if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
     P.wo_g = c->wo_g; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
