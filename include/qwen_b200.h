@@ -209,6 +209,15 @@ int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* st
  * share the one array, so calls whose kernels overlap on the GPU race on it. */
 int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, void* stream);
 
+/* C[M][N] = A[M][K] . B[N][K]^T on the tensor cores (tcgen05.mma, bf16 in, fp32
+ * accumulate in TMEM; 128 x 256 or 128 x 128 tiles, TMA-fed).  A and B bf16
+ * row-major (K contiguous: activations x weights in nn.Linear layout); C fp32
+ * (c_fp32 != 0) or bf16, row-major.  M a multiple of 128, N of 128, K of 64;
+ * all pointers device, 16-byte aligned.  The dense contraction of prefill (no
+ * reference counterpart: the reference runs the decode chain per prompt token,
+ * main.cu:141-145). */
+int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,6 +7,8 @@
 //   qwen_forward       forward (qwen_model.cuh:772-851)
 //   qwen_decode_step   forward + sample (main.cu:144-145, sampler.h:120-175)
 //   qwen_destroy       free_transformer (qwen_model.cuh:94-111)
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <unistd.h>
@@ -23,6 +25,7 @@
 #include "../../include/qwen_b200.h"
 #include "decode_kernel.cuh"
 #include "gemv_kernel.cuh"
+#include "gemm_tc.cuh"
 #include "model_format.h"
 
 using namespace qb;
@@ -637,6 +640,77 @@ extern "C" int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int 
                                                                                 err_flag[dev < 64 ? dev : 0]);
     CU(cudaGetLastError());
     return QWEN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// tensor-core GEMM (tcgen05)
+// ---------------------------------------------------------------------------
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+// 2-D K-major bf16 tensor map: `rows` x `cols` (cols contiguous), boxes of
+// box_rows x 64 elements with the 128-byte swizzle the tcgen05 descriptors expect.
+bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    std::call_once(g_encode_once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    if (!g_encode) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)qb::tc::kBK, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+uint32_t* g_gemm_err[64] = {nullptr};
+
+template <int BN, bool F32>
+int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N, int K, int kb_b, cudaStream_t st, uint32_t* err) {
+    static thread_local int attr_dev = -1;
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (attr_dev != dev) {
+        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_kernel<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<BN>::kSmem));
+        attr_dev = dev;
+    }
+    qb::tc::gemm_bf16_tc_kernel<BN, F32><<<dim3(N / BN, M / qb::tc::kBM), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
+        ma, mb, C, N, K, kb_b, err);
+    CU(cudaGetLastError());
+    return QWEN_OK;
+}
+}  // namespace
+
+// C[M][N] = A[M][K] . (B[N][Kb][:] repeated K / Kb times along K)^T.
+static int gemm_tc(const void* A, const void* B, void* C, int M, int N, int K, int Kb, bool c_fp32, cudaStream_t st) {
+    if (!A || !B || !C) return fail(QWEN_E_ARG, "NULL argument");
+    if (M <= 0 || N <= 0 || K <= 0 || Kb <= 0 || M % qb::tc::kBM || N % 128 || K % qb::tc::kBK || Kb % qb::tc::kBK || K % Kb)
+        return fail(QWEN_E_ARG, "M must be a multiple of 128, N of 128, K of 64");
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return fail(QWEN_E_ARG, "A, B and C must be 16-byte aligned");
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
+    if (!g_gemm_err[dev]) {
+        CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
+        CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
+    }
+    const int bn = N % 256 == 0 ? 256 : 128;
+    CUtensorMap ma, mb;
+    if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, qb::tc::kBM) || !kmajor_map(&mb, B, (uint64_t)N, (uint64_t)Kb, (uint32_t)bn))
+        return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    const int kb_b = Kb / qb::tc::kBK;
+    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev])
+                                 : gemm_launch<256, false>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev]);
+    return c_fp32 ? gemm_launch<128, true>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev])
+                  : gemm_launch<128, false>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev]);
+}
+
+extern "C" int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream) {
+    return gemm_tc(A, B, C, M, N, K, K, c_fp32 != 0, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------

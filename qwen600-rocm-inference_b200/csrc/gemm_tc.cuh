@@ -1,0 +1,204 @@
+// gemm_tc.cuh — C[M][N] = A[M][K] . B[N][K]^T on the sm_100a tensor cores
+// (tcgen05.mma, kind::f16, bf16 in, fp32 accumulate in TMEM).
+//
+// The dense contractions of prefill (the reference has none: it runs the
+// decode chain once per prompt token, main.cu:141-145): the projections of M
+// prompt rows against a weight matrix stored row-major [N][K] (nn.Linear
+// layout, K contiguous), so both operands are K-major.
+//
+// One CTA per 128 x BN output tile, 192 threads:
+//   warp 0, one thread: TMA producer — 2-D tiled bulk tensor loads of a
+//           128 x 64 A box and a BN x 64 B box per K step, 128-byte swizzle,
+//           into a kStages-deep ring (mbarrier complete_tx); no multicast;
+//   warp 1: allocates BN TMEM columns (the fp32 accumulator, 128 lanes = the
+//           tile's rows); one thread issues four 128 x BN x 16 MMAs per K step
+//           from shared-memory descriptors and commits each stage back to the
+//           producer (tcgen05.commit -> mbarrier);
+//   warps 2-5: epilogue — wait for the last commit, read their 32 TMEM lanes
+//           (tcgen05.ld 32x32b) and store fp32 or bf16 rows.
+// Every wait is bounded; on expiry the thread sets *err and stops waiting; the
+// TMEM allocation is always released.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "ptx.cuh"
+
+namespace qb {
+namespace tc {
+
+constexpr int kBM = 128;            // tile rows (TMEM lanes)
+constexpr int kBK = 64;             // K per stage: one 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kUmmaK = 16;          // K of one tcgen05.mma for 16-bit inputs
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+template <int BN>
+struct Layout {
+    static constexpr int kABytes = kBM * kBK * 2;          // 16 KB
+    static constexpr int kBBytes = BN * kBK * 2;           // 32 KB at BN = 256
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOff = kStages * kStageBytes;  // full[kStages], empty[kStages], done, tmem slot
+    static constexpr int kSmem = kBarOff + (2 * kStages + 1) * 8 + 16 + 1024;   // + alignment slack
+};
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
+// layout that TMA writes: rows of 128 B, 8-row groups 1024 B apart (SBO),
+// descriptor version 1 (sm_100), layout type 2 = SWIZZLE_128B.  Advancing the
+// start address by 32 B selects the next 16-element K slice inside the row.
+__device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B bf16
+// (bits 7-9, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17,
+// M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes (one row per lane).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    #pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Epilogue of one row segment: `v` = 32 fp32 results of columns [n, n + 32) of
+// row m.  kOutF32: C fp32; else C bf16 (round to nearest even).
+template <bool kOutF32>
+__device__ __forceinline__ void store32(void* C, int ldc, int m, int n, const float (&v)[32]) {
+    if constexpr (kOutF32) {
+        float4* d = reinterpret_cast<float4*>(static_cast<float*>(C) + (size_t)m * ldc + n);
+        #pragma unroll
+        for (int i = 0; i < 8; i++) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+        uint4* d = reinterpret_cast<uint4*>(static_cast<uint16_t*>(C) + (size_t)m * ldc + n);
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint32_t w[4];
+            #pragma unroll
+            for (int j = 0; j < 4; j++) w[j] = (uint32_t)f2bf(v[8 * i + 2 * j]) | ((uint32_t)f2bf(v[8 * i + 2 * j + 1]) << 16);
+            d[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
+// grid (N / BN, M / 128); K a multiple of 64; ldc in elements.  B's K extent
+// may be a divisor kb_b * 64 of K: K step kb reads B columns (kb mod kb_b) * 64,
+// so A = [a_1 | a_2 | a_3] (each K/3 wide) against B gives sum_i a_i . B^T —
+// the three-part bf16 split of fp32 activations in one accumulation.
+template <int BN, bool kOutF32>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void* C, int ldc, int K,
+                    int kb_b, uint32_t* err) {
+    using L = Layout<BN>;
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+    uint64_t* empty = full + kStages;
+    uint64_t* done = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int nkb = K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(done, 1);
+        fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_b) : "memory");
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); break; }
+                uint8_t* st = smem + s * L::kStageBytes;
+                mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                tma_load_2d(st, &map_a, kb * kBK, m0, &full[s]);
+                tma_load_2d(st + L::kABytes, &map_b, (kb % kb_b) * kBK, n0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t id = idesc_bf16_f32(kBM, BN);
+            bool ok = true;
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % kStages;
+                if (!mbar_wait(&full[s], (kb / kStages) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
+                tc_fence_after();
+                const uint32_t a = smem_addr(smem + s * L::kStageBytes), b = a + L::kABytes;
+                #pragma unroll
+                for (int kk = 0; kk < kBK / kUmmaK; kk++)
+                    mma_bf16(tmem, kmajor_sw128_desc(a + kk * 32), kmajor_sw128_desc(b + kk * 32), id, (kb | kk) != 0 ? 1u : 0u);
+                mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+            }
+            (void)ok;                    // on error the epilogue stores garbage; *err is set
+            mma_commit(done);            // arrives once every MMA issued above has completed
+        }
+    } else {
+        const int q = warp & 3;          // the TMEM lane quarter warp w may read is w % 4
+        if (!mbar_wait(done, 0, 2 * kWaitNs)) atomicOr(err, 4u);
+        tc_fence_after();
+        const int m = m0 + 32 * q + lane;
+        #pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+            store32<kOutF32>(C, ldc, m, n0 + c, v);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, BN);
+}
+
+}  // namespace tc
+}  // namespace qb

@@ -67,6 +67,7 @@ _SIGS = {
     "qwen_trace_read": (_c.c_int, [_P, _P, _c.c_int]),
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
+    "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
 }
 
 _lib = None
@@ -165,6 +166,12 @@ def gemv_bf16(W_ptr, x_ptr, y_ptr, n, k, stream=0):
     """y = bf16(W x) on device pointers (ints)."""
     _check(load_library().qwen_gemv_bf16(ctypes.c_void_p(W_ptr), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n, k,
                                          ctypes.c_void_p(stream)))
+
+
+def gemm_bf16(A_ptr, B_ptr, C_ptr, M, N, K, c_fp32=True, stream=0):
+    """C = A B^T on device pointers (ints): A [M][K] bf16, B [N][K] bf16, C [M][N] fp32 or bf16."""
+    _check(load_library().qwen_gemm_bf16(ctypes.c_void_p(A_ptr), ctypes.c_void_p(B_ptr), ctypes.c_void_p(C_ptr), M, N, K,
+                                         1 if c_fp32 else 0, ctypes.c_void_p(stream)))
 
 
 def gemv_bf16_static(W_ptr, x_ptr, y_ptr, n, k, stream=0):
