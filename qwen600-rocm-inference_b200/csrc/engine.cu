@@ -26,6 +26,7 @@
 #include "decode_kernel.cuh"
 #include "gemv_kernel.cuh"
 #include "gemm_tc.cuh"
+#include "prefill_kernels.cuh"
 #include "model_format.h"
 
 using namespace qb;
@@ -201,7 +202,12 @@ struct qwen_ctx {
     float* h_logits = nullptr;
     int* h_tokens = nullptr;
     DecodeParams params{};
+    // prompt pass on the tensor cores (allocated on first use)
+    const uint16_t* wo_raw[N_LAYERS] = {};   // o_proj in the canonical block
+    float *pf_x = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_o = nullptr;
+    uint16_t* pf_as = nullptr;
     int cached = 0;
+    bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int last_k = 0;
 };
 
@@ -210,7 +216,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_o, c->pf_as, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -317,6 +323,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         P.qn[l] = W(li.q_norm); P.kn[l] = W(li.k_norm);
         P.wg[l] = W(li.gate); P.wu[l] = W(li.up); P.wd[l] = W(li.down);
         pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * kGroups * DIM * kWoCols);
+        c->wo_raw[l] = W(li.o_proj);
     }
     if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
     P.wo_g = c->wo_g; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
@@ -504,6 +511,56 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
     return QWEN_OK;
 }
 
+static int gemm_tc(const void* A, int lda, const void* B, int ldb, void* C, int ldc, int M, int N, int K, int Kb, bool c_fp32,
+                   cudaStream_t st);
+
+// Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
+// layer's projections as tcgen05 GEMMs over all rows, attention over the KV
+// cache; fills the cache, computes no logits.  Tokens are in c->prompt.
+static int prefill_pass(qwen_t* c, int pos0, int m) {
+    using namespace qb::pf;
+    constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM, kLdQKV = Q_DIM + 2 * KV_DIM;
+    if (!c->pf_x) {
+        TRY(dalloc(&c->pf_x, (size_t)kMaxRows * DIM));
+        TRY(dalloc(&c->pf_y, (size_t)kMaxRows * kLdY));
+        TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
+        TRY(dalloc(&c->pf_o, (size_t)kMaxRows * Q_DIM));
+        TRY(dalloc(&c->pf_as, (size_t)kMaxRows * kLdAs));
+        CU(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttSmem)));
+    }
+    const DecodeParams& P = c->params;
+    cudaStream_t st = c->stream;
+    const int rows = (m + tc::kBM - 1) / tc::kBM * tc::kBM;
+    embed_kernel<<<rows, 256, 0, st>>>(P.embed, c->prompt + pos0, m, rows, c->pf_x);
+    int rc;
+    for (int l = 0; l < N_LAYERS; l++) {
+        uint16_t* kc_l = c->kc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
+        uint16_t* vc_l = c->vc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
+        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, P.in_ln[l], c->pf_as, kLdAs, rows);
+        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wq[l], DIM, c->pf_y, kLdQKV, rows, Q_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK) return rc;
+        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wk[l], DIM, c->pf_y + Q_DIM, kLdQKV, rows, KV_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK) return rc;
+        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wv[l], DIM, c->pf_y + Q_DIM + KV_DIM, kLdQKV, rows, KV_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK)
+            return rc;
+        qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l);
+        attention_kernel<<<dim3(rows / kAttBlock, N_HEADS), kAttThreads, sizeof(AttSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
+        split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
+        if ((rc = gemm_tc(c->pf_as, kLdAs, c->wo_raw[l], Q_DIM, c->pf_y, kLdY, rows, DIM, 3 * Q_DIM, Q_DIM, true, st)) != QWEN_OK) return rc;
+        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, P.post_ln[l], c->pf_as, kLdAs, rows);
+        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wg[l], DIM, c->pf_y, kLdY, rows, HIDDEN_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK) return rc;
+        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wu[l], DIM, c->pf_y + HIDDEN_DIM, kLdY, rows, HIDDEN_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK)
+            return rc;
+        swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, kLdY, c->pf_as, kLdAs, rows);
+        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wd[l], HIDDEN_DIM, c->pf_y, kLdY, rows, DIM, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st)) != QWEN_OK)
+            return rc;
+    }
+    CU(cudaGetLastError());
+    return QWEN_OK;
+}
+
+// Prompts whose first n - 1 positions number at least this go through
+// prefill_pass; shorter ones through one decode launch per position.
+constexpr int kGemmPrefillMin = 64;
+
 extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float* logits_host) {
     if (!c || !tokens) return fail(QWEN_E_ARG, "NULL argument");
     if (n <= 0 || pos0 < 0 || (long long)pos0 + n > SEQ_LEN) return fail(QWEN_E_ARG, "prompt does not fit [0, SEQ_LEN)");
@@ -513,7 +570,10 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(c->prompt + pos0, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     int rc;
-    if (n > 1) {
+    if (n - 1 >= kGemmPrefillMin && c->gemm_prefill) {
+        for (int s = 0; s < n - 1; s += qb::pf::kMaxRows)
+            if ((rc = prefill_pass(c, pos0 + s, std::min(qb::pf::kMaxRows, n - 1 - s))) != QWEN_OK) return rc;
+    } else if (n > 1) {
         fill_in(c, 0, pos0, nullptr, 0, kFlagPromptToken | kFlagNoHead);
         CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
         for (int i = 0; i < n - 1; i++)
@@ -530,6 +590,12 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     c->last_k = 1;
     if ((rc = check_step(c)) != QWEN_OK) return rc;
     c->cached = pos0 + n;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_set_prefill_mode(qwen_t* c, int gemm) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    c->gemm_prefill = gemm != 0;
     return QWEN_OK;
 }
 
@@ -649,9 +715,10 @@ namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
-// 2-D K-major bf16 tensor map: `rows` x `cols` (cols contiguous), boxes of
-// box_rows x 64 elements with the 128-byte swizzle the tcgen05 descriptors expect.
-bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// 2-D K-major bf16 tensor map: `rows` x `cols` (cols contiguous, rows ld
+// elements apart), boxes of box_rows x 64 elements with the 128-byte swizzle
+// the tcgen05 descriptors expect.
+bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
     std::call_once(g_encode_once, [] {
         void* f = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -660,7 +727,7 @@ bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
     });
     if (!g_encode) return false;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint64_t strides[1] = {ld * 2};
     const cuuint32_t box[2] = {(cuuint32_t)qb::tc::kBK, box_rows};
     const cuuint32_t es[2] = {1, 1};
     return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -670,7 +737,7 @@ bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 uint32_t* g_gemm_err[64] = {nullptr};
 
 template <int BN, bool F32>
-int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, int N, int K, int kb_b, cudaStream_t st, uint32_t* err) {
+int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int ldc, int M, int N, int K, int kb_b, cudaStream_t st, uint32_t* err) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -679,18 +746,21 @@ int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int M, in
         attr_dev = dev;
     }
     qb::tc::gemm_bf16_tc_kernel<BN, F32><<<dim3(N / BN, M / qb::tc::kBM), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
-        ma, mb, C, N, K, kb_b, err);
+        ma, mb, C, ldc, K, kb_b, err);
     CU(cudaGetLastError());
     return QWEN_OK;
 }
 }  // namespace
 
-// C[M][N] = A[M][K] . (B[N][Kb][:] repeated K / Kb times along K)^T.
-static int gemm_tc(const void* A, const void* B, void* C, int M, int N, int K, int Kb, bool c_fp32, cudaStream_t st) {
+// C[M][N] (rows ldc apart) = A[M][K] (rows lda apart) . (B[N][Kb] (rows ldb
+// apart) repeated K / Kb times along K)^T.
+static int gemm_tc(const void* A, int lda, const void* B, int ldb, void* C, int ldc, int M, int N, int K, int Kb, bool c_fp32,
+                   cudaStream_t st) {
     if (!A || !B || !C) return fail(QWEN_E_ARG, "NULL argument");
     if (M <= 0 || N <= 0 || K <= 0 || Kb <= 0 || M % qb::tc::kBM || N % 128 || K % qb::tc::kBK || Kb % qb::tc::kBK || K % Kb)
         return fail(QWEN_E_ARG, "M must be a multiple of 128, N of 128, K of 64");
     if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return fail(QWEN_E_ARG, "A, B and C must be 16-byte aligned");
+    if (lda < K || ldb < Kb || ldc < N || lda % 8 || ldb % 8 || ldc % 8) return fail(QWEN_E_ARG, "bad leading dimension");
     int dev = 0;
     CU(cudaGetDevice(&dev));
     if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
@@ -700,17 +770,18 @@ static int gemm_tc(const void* A, const void* B, void* C, int M, int N, int K, i
     }
     const int bn = N % 256 == 0 ? 256 : 128;
     CUtensorMap ma, mb;
-    if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, qb::tc::kBM) || !kmajor_map(&mb, B, (uint64_t)N, (uint64_t)Kb, (uint32_t)bn))
+    if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM) ||
+        !kmajor_map(&mb, B, (uint64_t)N, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)bn))
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     const int kb_b = Kb / qb::tc::kBK;
-    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev])
-                                 : gemm_launch<256, false>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev]);
-    return c_fp32 ? gemm_launch<128, true>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev])
-                  : gemm_launch<128, false>(ma, mb, C, M, N, K, kb_b, st, g_gemm_err[dev]);
+    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev])
+                                 : gemm_launch<256, false>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev]);
+    return c_fp32 ? gemm_launch<128, true>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev])
+                  : gemm_launch<128, false>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev]);
 }
 
 extern "C" int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream) {
-    return gemm_tc(A, B, C, M, N, K, K, c_fp32 != 0, (cudaStream_t)stream);
+    return gemm_tc(A, K, B, K, C, N, M, N, K, K, c_fp32 != 0, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------

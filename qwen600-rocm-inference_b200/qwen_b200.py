@@ -68,6 +68,7 @@ _SIGS = {
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
+    "qwen_set_prefill_mode": (_c.c_int, [_P, _c.c_int]),
 }
 
 _lib = None
@@ -255,6 +256,10 @@ class Engine:
         _check(self._lib.qwen_generate_timed(self._h, int(token), int(pos), int(n_steps), ctypes.byref(sampling), ctypes.byref(r),
                                              _ptr(out), ctypes.byref(ms)))
         return out.tolist(), r.value, ms.value
+
+    def set_prefill_mode(self, gemm=True):
+        """Long prompts on the tensor cores (True, default) or one decode launch per token."""
+        _check(self._lib.qwen_set_prefill_mode(self._h, 1 if gemm else 0))
 
     def prefill(self, tokens, pos0=0, want_logits=False):
         tk = np.ascontiguousarray(tokens, dtype=np.int32)

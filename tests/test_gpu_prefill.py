@@ -1,0 +1,59 @@
+"""qwen_prefill on the tensor cores (whole-prompt passes: tcgen05 GEMMs with the
+activations split into three bf16 parts, fp32 attention over the KV cache)
+against the one-launch-per-token path and the fp32 oracle.  Tolerances as in
+test_gpu_decode: max-abs <= 2e-2 and relative RMS <= 2.5e-3 on the logits."""
+import numpy as np
+import pytest
+
+from conftest import rel_rms
+
+pytestmark = pytest.mark.gpu
+
+VOCAB = 151936
+
+
+def _prompt(n, seed):
+    return np.random.default_rng(seed).integers(0, VOCAB, n).tolist()
+
+
+def _both(qb, checkpoint, chunks):
+    """Prefill the chunks (list of token lists, consecutive) on a GEMM-path and
+    a per-token-path handle; returns both final logits and both handles."""
+    a, b = qb.Engine(checkpoint, 0), qb.Engine(checkpoint, 0)
+    b.set_prefill_mode(False)
+    pos = 0
+    for ch in chunks:
+        la = a.prefill(ch, pos, want_logits=True)
+        lb = b.prefill(ch, pos, want_logits=True)
+        pos += len(ch)
+    return la, lb, a, b, pos
+
+
+def test_prefill_300_matches_per_token_path_and_oracle(qb, O, checkpoint):
+    toks = _prompt(300, 11)
+    la, lb, a, b, pos = _both(qb, checkpoint, [toks])
+    try:
+        assert np.abs(la - lb).max() <= 2e-2 and rel_rms(la, lb) <= 2.5e-3
+        assert int(np.argmax(la)) == int(np.argmax(lb))
+        of = O.Oracle(checkpoint, O.FP32, 320)
+        for p, t in enumerate(toks[:-1]):
+            of.forward(t, p, want_logits=False)
+        lo = of.forward(toks[-1], len(toks) - 1)
+        assert np.abs(la - lo).max() <= 2e-2 and rel_rms(la, lo) <= 2.5e-3, (np.abs(la - lo).max(), rel_rms(la, lo))
+        # decoding continues from the cache the pass wrote
+        ga, _ = a.generate(int(np.argmax(la)), pos, 8)
+        gb, _ = b.generate(int(np.argmax(lb)), pos, 8)
+        assert ga == gb
+    finally:
+        a.close(); b.close()
+
+
+def test_prefill_two_passes_and_continuation(qb, checkpoint):
+    # 2100 tokens: a 2048-row pass plus a 51-row pass; then 200 more at pos0 = 2100
+    la, lb, a, b, pos = _both(qb, checkpoint, [_prompt(2100, 12), _prompt(200, 13)])
+    try:
+        assert pos == 2300 and a.cached == 2300
+        assert np.abs(la - lb).max() <= 2e-2 and rel_rms(la, lb) <= 2.5e-3, (np.abs(la - lb).max(), rel_rms(la, lb))
+        assert int(np.argmax(la)) == int(np.argmax(lb))
+    finally:
+        a.close(); b.close()
