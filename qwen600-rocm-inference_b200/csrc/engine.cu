@@ -526,7 +526,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
         TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
         TRY(dalloc(&c->pf_o, (size_t)kMaxRows * Q_DIM));
         TRY(dalloc(&c->pf_as, (size_t)kMaxRows * kLdAs));
-        CU(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttSmem)));
+        CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
     }
     const DecodeParams& P = c->params;
     cudaStream_t st = c->stream;
@@ -542,7 +542,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
         if ((rc = gemm_tc(c->pf_as, kLdAs, P.wv[l], DIM, c->pf_y + Q_DIM + KV_DIM, kLdQKV, rows, KV_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK)
             return rc;
         qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l);
-        attention_kernel<<<dim3(rows / kAttBlock, N_HEADS), kAttThreads, sizeof(AttSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
+        attention_tc_kernel<<<dim3(rows / kAttBlock, N_HEADS), kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, c->wo_raw[l], Q_DIM, c->pf_y, kLdY, rows, DIM, 3 * Q_DIM, Q_DIM, true, st)) != QWEN_OK) return rc;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, P.post_ln[l], c->pf_as, kLdAs, rows);

@@ -9,7 +9,7 @@
 //   norm_split    X (+= the previous GEMM's output) -> RMSNorm -> As = [hi|mid|lo]
 //   GEMM          As . [Wq; Wk; Wv]^T -> Y (fp32)
 //   qkv_post      QK-norm + RoPE; q -> Q (fp32); k, v -> the bf16 KV cache
-//   attention     causal GQA over the cache -> O (fp32)
+//   attention     causal GQA over the cache on the tensor cores -> O (fp32)
 //   split         O -> As;  GEMM As . Wo^T -> Y
 //   norm_split    X += Y -> RMSNorm (post_attention_layernorm) -> As
 //   GEMM          As . Wg^T, As . Wu^T -> Y;  swiglu_split -> As
@@ -25,7 +25,6 @@ namespace pf {
 
 constexpr int kMaxRows = 2048;          // prompt rows per pass
 constexpr int kAttBlock = 64;           // query rows and key positions per attention tile
-constexpr int kAttThreads = 256;
 
 __device__ __forceinline__ void split3(float v, uint16_t& h, uint16_t& m, uint16_t& l) {
     h = f2bf(v);
@@ -146,118 +145,162 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int m, in
     }
 }
 
-// Causal GQA attention, fp32: one CTA per (64 query rows, q head h); key/value
-// head h / 2 from the cache, positions 0 .. pos0 + r for row r, in tiles of 64
-// with an online softmax (scores / sqrt(128), as qwen_model.cuh:566-585).
-// Scores: thread (ty, tx) takes query rows 4ty..4ty+3 and keys tx + 16c;
-// P.V: the same query rows and dims 8tx..8tx+7.
-struct AttSmem {
-    float q[kAttBlock][HEAD_DIM];
-    float k[kAttBlock][HEAD_DIM + 1];
-    float v[kAttBlock][HEAD_DIM];
-    float p[kAttBlock][kAttBlock + 1];
+// ---------------------------------------------------------------------------
+// Causal GQA attention on the tensor cores (mma.m16n8k16, bf16 in, fp32
+// accumulate).  One CTA per (64 query rows, q head); warp w owns rows 16w..16w+15.
+// S = Q K^T with Q split into three bf16 parts (K is bf16 in the cache: exact),
+// online softmax on the accumulator fragments, O += P V with P split into three
+// bf16 parts (V exact) — fp32-level numerics.  K and V tiles sit in shared
+// memory with 16-byte row pads (conflict-free ldmatrix; V through .trans).
+// ---------------------------------------------------------------------------
+constexpr int kTcRowE = HEAD_DIM + 8;     // padded smem row, elements (272 B)
+constexpr int kTcThreads = 128;
+struct AttTcSmem {
+    uint16_t q[3][kAttBlock][kTcRowE];    // hi, mid, lo parts of the 64 query rows
+    uint16_t k[kAttBlock][kTcRowE];
+    uint16_t v[kAttBlock][kTcRowE];
 };
-__global__ void __launch_bounds__(kAttThreads)
-attention_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l, float* __restrict__ O) {
-    extern __shared__ __align__(16) uint8_t att_smem[];
-    AttSmem& S = *reinterpret_cast<AttSmem*>(att_smem);
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(uint16_t a, uint16_t b) { return (uint32_t)a | ((uint32_t)b << 16); }
+
+__global__ void __launch_bounds__(kTcThreads)
+attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
+                    float* __restrict__ O) {
+    extern __shared__ __align__(16) uint8_t att_tc_smem[];
+    AttTcSmem& S = *reinterpret_cast<AttTcSmem*>(att_tc_smem);
     const int h = blockIdx.y, hk = h >> 1, q0 = blockIdx.x * kAttBlock, tid = threadIdx.x;
-    const int ty = tid >> 4, tx = tid & 15;
+    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
     const float sqrt_hd = sqrtf((float)HEAD_DIM);
-    for (int i = tid; i < kAttBlock * HEAD_DIM / 4; i += kAttThreads) {
+    // the block's query rows, split
+    for (int i = tid; i < kAttBlock * HEAD_DIM / 4; i += kTcThreads) {
         const int r = i / (HEAD_DIM / 4), c = (i % (HEAD_DIM / 4)) * 4;
-        *(float4*)&S.q[r][c] = *(const float4*)(Q + (size_t)(q0 + r) * Q_DIM + 128 * h + c);
+        const float4 v = *(const float4*)(Q + (size_t)(q0 + r) * Q_DIM + 128 * h + c);
+        uint16_t hh[4], mm[4], ll[4];
+        split3(v.x, hh[0], mm[0], ll[0]); split3(v.y, hh[1], mm[1], ll[1]);
+        split3(v.z, hh[2], mm[2], ll[2]); split3(v.w, hh[3], mm[3], ll[3]);
+        *(uint2*)&S.q[0][r][c] = make_uint2(pack_bf16(hh[0], hh[1]), pack_bf16(hh[2], hh[3]));
+        *(uint2*)&S.q[1][r][c] = make_uint2(pack_bf16(mm[0], mm[1]), pack_bf16(mm[2], mm[3]));
+        *(uint2*)&S.q[2][r][c] = make_uint2(pack_bf16(ll[0], ll[1]), pack_bf16(ll[2], ll[3]));
     }
-    float mrow[4], lrow[4], acc[4][8];
+    const int rowA = 16 * warp + (lane & 15);                    // ldmatrix row of this lane for A tiles
+    const uint32_t qa = smem_addr(&S.q[0][rowA][(lane >> 4) * 8]);
+    constexpr uint32_t kQPart = kAttBlock * kTcRowE * 2;         // bytes between q parts
+    // B fragments of K (keys x dims, row-major = col-major B): lanes 0-7 keys 0-7 @ d, 8-15 keys 0-7 @ d+8,
+    // 16-23 keys 8-15 @ d, 24-31 keys 8-15 @ d+8
+    const uint32_t kb_addr = smem_addr(&S.k[(lane & 7) + ((lane >> 4) << 3)][((lane >> 3) & 1) * 8]);
+    // B fragments of V via .trans: lanes 0-7 keys 0-7 @ n, 8-15 keys 8-15 @ n, 16-23 keys 0-7 @ n+8, 24-31 keys 8-15 @ n+8
+    const uint32_t vb_addr = smem_addr(&S.v[(lane & 15)][(lane >> 4) * 8]);
+    float o[16][4];
     #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        mrow[i] = -INFINITY; lrow[i] = 0.f;
-        #pragma unroll
-        for (int d = 0; d < 8; d++) acc[i][d] = 0.f;
-    }
-    const int last = min(pos0 + q0 + kAttBlock - 1, SEQ_LEN - 1);   // the block's last query position
+    for (int i = 0; i < 16; i++) { o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f; }
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    const int qp0 = pos0 + q0 + 16 * warp + g, qp1 = qp0 + 8;     // this lane's two query positions
+    const int last = min(pos0 + q0 + kAttBlock - 1, SEQ_LEN - 1);
     const uint16_t* kb = kc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
     const uint16_t* vb = vc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
     for (int k0 = 0; k0 <= last; k0 += kAttBlock) {
-        __syncthreads();   // the previous tile's k, v and p are consumed
-        for (int i = tid; i < kAttBlock * HEAD_DIM / 8; i += kAttThreads) {
+        __syncthreads();   // q split written / the previous tile consumed
+        for (int i = tid; i < kAttBlock * HEAD_DIM / 8; i += kTcThreads) {
             const int r = i / (HEAD_DIM / 8), c = (i % (HEAD_DIM / 8)) * 8;
             const int kp = min(k0 + r, SEQ_LEN - 1);
-            const uint4 kw = *(const uint4*)(kb + (size_t)kp * HEAD_DIM + c);
-            const uint4 vw = *(const uint4*)(vb + (size_t)kp * HEAD_DIM + c);
-            const uint32_t ka[4] = {kw.x, kw.y, kw.z, kw.w}, va[4] = {vw.x, vw.y, vw.z, vw.w};
-            #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                S.k[r][c + 2 * j] = bf_lo(ka[j]); S.k[r][c + 2 * j + 1] = bf_hi(ka[j]);
-                S.v[r][c + 2 * j] = bf_lo(va[j]); S.v[r][c + 2 * j + 1] = bf_hi(va[j]);
-            }
+            *(uint4*)&S.k[r][c] = *(const uint4*)(kb + (size_t)kp * HEAD_DIM + c);
+            *(uint4*)&S.v[r][c] = *(const uint4*)(vb + (size_t)kp * HEAD_DIM + c);
         }
         __syncthreads();
-        float s[4][4];
+        // S (16 rows x 64 keys) = Q K^T: 8 n-tiles of 8 keys
+        float sc[8][4];
         #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int n = 0; n < 8; n++) { sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f; }
+        #pragma unroll
+        for (int kt = 0; kt < HEAD_DIM / 16; kt++) {
+            uint32_t a[3][4];
             #pragma unroll
-            for (int c = 0; c < 4; c++) s[i][c] = 0.f;
-        #pragma unroll 4
-        for (int d = 0; d < HEAD_DIM; d++) {
-            float qv[4], kv[4];
+            for (int p = 0; p < 3; p++) ldsm_x4(qa + p * kQPart + kt * 32, a[p][0], a[p][1], a[p][2], a[p][3]);
             #pragma unroll
-            for (int i = 0; i < 4; i++) qv[i] = S.q[4 * ty + i][d];
-            #pragma unroll
-            for (int c = 0; c < 4; c++) kv[c] = S.k[tx + 16 * c][d];
-            #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int np = 0; np < 4; np++) {   // keys 16np .. 16np+15: two n-tiles
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kb_addr + np * 16 * kTcRowE * 2 + kt * 32, b0, b1, b2, b3);
                 #pragma unroll
-                for (int c = 0; c < 4; c++) s[i][c] = fmaf(qv[i], kv[c], s[i][c]);
+                for (int p = 0; p < 3; p++) {
+                    mma_bf16_16816(sc[2 * np], a[p][0], a[p][1], a[p][2], a[p][3], b0, b1);
+                    mma_bf16_16816(sc[2 * np + 1], a[p][0], a[p][1], a[p][2], a[p][3], b2, b3);
+                }
+            }
+        }
+        // online softmax over this tile (rows g and g + 8 of the warp)
+        float mx[2] = {-INFINITY, -INFINITY};
+        #pragma unroll
+        for (int n = 0; n < 8; n++) {
+            #pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int kp = k0 + 8 * n + 2 * qd + (e & 1);
+                const int qp = e < 2 ? qp0 : qp1;
+                sc[n][e] = kp <= qp ? sc[n][e] / sqrt_hd : -INFINITY;
+                mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+            }
+        }
+        float scale[2];
+        #pragma unroll
+        for (int r = 0; r < 2; r++) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float mn = fmaxf(mrow[r], mx[r]);   // finite: key 0 precedes every query
+            scale[r] = expf(mrow[r] - mn);
+            mrow[r] = mn;
+        }
+        float ps[2] = {0.f, 0.f};
+        #pragma unroll
+        for (int n = 0; n < 8; n++) {
+            #pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float pr = sc[n][e] == -INFINITY ? 0.f : expf(sc[n][e] - mrow[e >> 1]);
+                sc[n][e] = pr;
+                ps[e >> 1] += pr;
+            }
         }
         #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int qp = pos0 + q0 + 4 * ty + i;
-            float mx = -INFINITY;
-            #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int kp = k0 + tx + 16 * c;
-                s[i][c] = kp <= qp ? s[i][c] / sqrt_hd : -INFINITY;
-                mx = fmaxf(mx, s[i][c]);
-            }
-            #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float mn = fmaxf(mrow[i], mx);   // finite: key 0 <= every query position
-            const float sc = expf(mrow[i] - mn);
-            float ps = 0.f;
-            #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const float pr = s[i][c] == -INFINITY ? 0.f : expf(s[i][c] - mn);
-                S.p[4 * ty + i][tx + 16 * c] = pr;
-                ps += pr;
-            }
-            #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-            lrow[i] = fmaf(lrow[i], sc, ps);
-            #pragma unroll
-            for (int d = 0; d < 8; d++) acc[i][d] *= sc;
-            mrow[i] = mn;
+        for (int r = 0; r < 2; r++) {
+            ps[r] += __shfl_xor_sync(0xffffffffu, ps[r], 1);
+            ps[r] += __shfl_xor_sync(0xffffffffu, ps[r], 2);
+            lrow[r] = fmaf(lrow[r], scale[r], ps[r]);
         }
-        __syncthreads();
-        #pragma unroll 4
-        for (int j = 0; j < kAttBlock; j++) {
-            const float4 v0 = *(const float4*)&S.v[j][8 * tx], v1 = *(const float4*)&S.v[j][8 * tx + 4];
+        #pragma unroll
+        for (int i = 0; i < 16; i++) { o[i][0] *= scale[0]; o[i][1] *= scale[0]; o[i][2] *= scale[1]; o[i][3] *= scale[1]; }
+        // O += P V: 4 k-tiles of 16 keys; P's A fragment comes from S n-tiles 2kt, 2kt + 1
+        #pragma unroll
+        for (int kt = 0; kt < 4; kt++) {
+            uint32_t a[3][4];
             #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float pr = S.p[4 * ty + i][j];
-                acc[i][0] = fmaf(pr, v0.x, acc[i][0]); acc[i][1] = fmaf(pr, v0.y, acc[i][1]);
-                acc[i][2] = fmaf(pr, v0.z, acc[i][2]); acc[i][3] = fmaf(pr, v0.w, acc[i][3]);
-                acc[i][4] = fmaf(pr, v1.x, acc[i][4]); acc[i][5] = fmaf(pr, v1.y, acc[i][5]);
-                acc[i][6] = fmaf(pr, v1.z, acc[i][6]); acc[i][7] = fmaf(pr, v1.w, acc[i][7]);
+            for (int j = 0; j < 4; j++) {   // a0: (g, keys 2qd..) = n-tile 2kt d0,d1; a1: rows g+8 = d2,d3; a2, a3: n-tile 2kt+1
+                const float* src = &sc[2 * kt + (j >> 1)][(j & 1) * 2];
+                uint16_t h0, m0, l0, h1, m1, l1;
+                split3(src[0], h0, m0, l0);
+                split3(src[1], h1, m1, l1);
+                a[0][j] = pack_bf16(h0, h1); a[1][j] = pack_bf16(m0, m1); a[2][j] = pack_bf16(l0, l1);
+            }
+            #pragma unroll
+            for (int np = 0; np < 8; np++) {   // dims 16np .. 16np+15: two n-tiles
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_trans(vb_addr + kt * 16 * kTcRowE * 2 + np * 32, b0, b1, b2, b3);
+                #pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    mma_bf16_16816(o[2 * np], a[p][0], a[p][1], a[p][2], a[p][3], b0, b1);
+                    mma_bf16_16816(o[2 * np + 1], a[p][0], a[p][1], a[p][2], a[p][3], b2, b3);
+                }
             }
         }
     }
+    // O rows g, g + 8 of the warp; dims 8n + 2qd, +1
+    const float inv0 = 1.0f / lrow[0], inv1 = 1.0f / lrow[1];
+    float* o0 = O + (size_t)(q0 + 16 * warp + g) * Q_DIM + 128 * h + 2 * qd;
+    float* o1 = o0 + (size_t)8 * Q_DIM;
     #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        float* o = O + (size_t)(q0 + 4 * ty + i) * Q_DIM + 128 * h + 8 * tx;
-        const float inv = 1.0f / lrow[i];
-        *(float4*)o = make_float4(acc[i][0] * inv, acc[i][1] * inv, acc[i][2] * inv, acc[i][3] * inv);
-        *(float4*)(o + 4) = make_float4(acc[i][4] * inv, acc[i][5] * inv, acc[i][6] * inv, acc[i][7] * inv);
+    for (int n = 0; n < 16; n++) {
+        *(float2*)(o0 + 8 * n) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
+        *(float2*)(o1 + 8 * n) = make_float2(o[n][2] * inv1, o[n][3] * inv1);
     }
 }
 
