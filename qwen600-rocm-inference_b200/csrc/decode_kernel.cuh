@@ -505,6 +505,7 @@ struct Consumer {
 
     // Gathers up to N word pairs: pair i (16-byte aligned, at addr(i)) for each i
     // whose bit is set in `mask`, into v[2i], v[2i+1].  Called by whole warps.
+    // N <= 3: every round reloads every pair until all are current.
     // A round loads every pair of every lane at once; until all carry this
     // launch's tag, ONE lane of the warp spins on its first stale pair and the
     // others wait, then the warp runs another round.  Once the last writer has
@@ -531,6 +532,21 @@ struct Consumer {
                 return;
             }
             if (t0 == 0) t0 = global_ns();
+            if constexpr (N <= 3) {
+                // small gathers: the next round is the poll (reloading every pair
+                // costs little), so the last store is seen one round trip later
+                if (P->poll_ns) __nanosleep(P->poll_ns);
+                if ((++it & 31u) == 0) {
+                    if (ld_volatile(&P->out->err)) failed = true;
+                    else if (global_ns() - t0 > kWaitNs) {
+                        atomicOr(&P->out->err, 1u);
+                        atomicExch(&P->out->err_where, where);
+                        failed = true;
+                    }
+                }
+                failed = __any_sync(0xffffffffu, failed);
+                continue;
+            }
             const int src = __ffs(waiting) - 1;
             if (lane == src) {
                 const uint64_t* q = addr(stale);
