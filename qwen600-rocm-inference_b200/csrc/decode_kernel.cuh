@@ -505,68 +505,40 @@ struct Consumer {
 
     // Gathers up to N word pairs: pair i (16-byte aligned, at addr(i)) for each i
     // whose bit is set in `mask`, into v[2i], v[2i+1].  Called by whole warps.
-    // N <= 3: every round reloads every pair until all are current.
-    // A round loads every pair of every lane at once; until all carry this
-    // launch's tag, ONE lane of the warp spins on its first stale pair and the
-    // others wait, then the warp runs another round.  Once the last writer has
-    // stored, the gather costs about one round trip whatever the number of
-    // words, and a waiting CTA polls one pair per warp, so the L2 lines being
-    // written are not swamped by readers.
+    // A round loads every pair of every lane at once; while any carries an old
+    // tag the warp runs another round, so the last store is seen one round trip
+    // after it lands.  (Every gather here is at most 8 pairs per lane; letting
+    // one lane spin on a stale pair between rounds measured 2.5 % slower.)
     template <int N, typename A>
     __device__ __forceinline__ void gather(A addr, uint32_t mask, float* v, int where) {
+        static_assert(N >= 1 && N <= 8, "gathers poll by full rounds of at most 8 pairs per lane");
         uint64_t t0 = 0;
         uint32_t it = 0;
         while (!failed) {
             uint64_t a[N], b[N];
             #pragma unroll
             for (int i = 0; i < N; i++) if (mask & (1u << i)) xw_load2(addr(i), a[i], b[i]);
-            int stale = -1;
+            int stale = -1;   // (an index, not a flag: the flag form costs spills at 96 registers)
             #pragma unroll
             for (int i = N - 1; i >= 0; i--)
                 if ((mask & (1u << i)) && ((uint32_t)(a[i] >> 32) != tag || (uint32_t)(b[i] >> 32) != tag)) stale = i;
-            const unsigned waiting = __ballot_sync(0xffffffffu, stale >= 0);
-            if (waiting == 0) {
+            if (__ballot_sync(0xffffffffu, stale >= 0) == 0u) {
                 #pragma unroll
                 for (int i = 0; i < N; i++) { v[2 * i] = __uint_as_float((uint32_t)a[i]); v[2 * i + 1] = __uint_as_float((uint32_t)b[i]); }
                 if (kTr && tr && t0) xw_ns += global_ns() - t0;
                 return;
             }
             if (t0 == 0) t0 = global_ns();
-            if constexpr (N <= 3) {
-                // small gathers: the next round is the poll (reloading every pair
-                // costs little), so the last store is seen one round trip later
-                if (P->poll_ns) __nanosleep(P->poll_ns);
-                if ((++it & 31u) == 0) {
-                    if (ld_volatile(&P->out->err)) failed = true;
-                    else if (global_ns() - t0 > kWaitNs) {
-                        atomicOr(&P->out->err, 1u);
-                        atomicExch(&P->out->err_where, where);
-                        failed = true;
-                    }
-                }
-                failed = __any_sync(0xffffffffu, failed);
-                continue;
-            }
-            const int src = __ffs(waiting) - 1;
-            if (lane == src) {
-                const uint64_t* q = addr(stale);
-                for (;;) {
-                    if (P->poll_ns) __nanosleep(P->poll_ns);
-                    uint64_t x, y;
-                    xw_load2(q, x, y);
-                    if ((uint32_t)(x >> 32) == tag && (uint32_t)(y >> 32) == tag) break;
-                    if ((++it & 31u) == 0) {
-                        if (ld_volatile(&P->out->err)) { failed = true; break; }
-                        if (global_ns() - t0 > kWaitNs) {
-                            atomicOr(&P->out->err, 1u);
-                            atomicExch(&P->out->err_where, where);
-                            failed = true;
-                            break;
-                        }
-                    }
+            if (P->poll_ns) __nanosleep(P->poll_ns);
+            if ((++it & 31u) == 0) {
+                if (ld_volatile(&P->out->err)) failed = true;
+                else if (global_ns() - t0 > kWaitNs) {
+                    atomicOr(&P->out->err, 1u);
+                    atomicExch(&P->out->err_where, where);
+                    failed = true;
                 }
             }
-            failed = __shfl_sync(0xffffffffu, failed, src);
+            failed = __any_sync(0xffffffffu, failed);
         }
         #pragma unroll
         for (int i = 0; i < 2 * N; i++) v[i] = 0.f;   // after an error the values are never used for a result
@@ -615,13 +587,16 @@ struct Consumer {
         f[8] = (uint32_t)m0 | ((uint32_t)m1 << 16);    // lane q + 4
         f[16] = (uint32_t)l0 | ((uint32_t)l1 << 16);   // lane q + 8
     }
-    // RMSNorm of the 1024-wide x whose pair 2 tid, 2 tid + 1 this thread holds
-    // (x0, x1; g2 = its two bf16 gains), given the block's sum of squares:
-    // writes the fragments S->bx, then a barrier.
-    __device__ __forceinline__ void norm_bx(float x0, float x1, uint32_t g2, float ss) {
-        const float r = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
-        put_pair(&S->bx[0][0][0], 2 * tid, (x0 * r) * bf_lo(g2), (x1 * r) * bf_hi(g2));
-        bar();
+    // RMSNorm input of a projection, for the 1024-wide x whose pair 2 tid,
+    // 2 tid + 1 this thread holds (x0, x1; g2 = its two bf16 gains): writes the
+    // fragments S->bx of g * x and returns 1 / rms(x) once the block's sum of
+    // squares is in — one barrier for both.  The projections are linear, so
+    // their row results are scaled by the returned factor instead of the
+    // input: W (g * x / rms) = (W (g * x)) / rms.
+    __device__ __forceinline__ float gain_bx(float x0, float x1, uint32_t g2) {
+        put_pair(&S->bx[0][0][0], 2 * tid, x0 * bf_lo(g2), x1 * bf_hi(g2));
+        const float ss = block_sum(x0 * x0 + x1 * x1);
+        return 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
     }
     // Row tile x k-tile products on the tensor cores (mma.m16n8k16, bf16 in,
     // fp32 accumulate): ta[t] = this lane's ldmatrix address (shared space) of
@@ -776,12 +751,11 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
             }
             S->xres[j] = xv[0]; S->xres[j + 1] = xv[1];
-            const float ss = C.block_sum(xv[0] * xv[0] + xv[1] * xv[1]);
+            const float rn = C.gain_bx(xv[0], xv[1], g2);
             QB_SUB(31);
             QB_TRACE(TB + 0);
-            C.norm_bx(xv[0], xv[1], g2, ss);
             uint64_t* qkv = P.qkvw + (size_t)l * 4096;
-            C.rows_1024(pl.qa, pl.qb, &S->bx[0][0][0], [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v, seq); });
+            C.rows_1024(pl.qa, pl.qb, &S->bx[0][0][0], [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v * rn, seq); });
         }
         QB_TRACE(TB + 1);
         QB_SUB(32);
@@ -1008,10 +982,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             }
             QB_SUB(17);
             S->xres[j] = x0; S->xres[j + 1] = x1;
-            const float ss = C.block_sum(x0 * x0 + x1 * x1);
+            const float rn = C.gain_bx(x0, x1, g2);
             QB_TRACE(TB + 6);
             QB_SUB(34);
-            C.norm_bx(x0, x1, g2, ss);
             QB_SUB(20);
             // gate|up units, 7 per chunk (gate rows 0..6, up rows 7..13), two
             // chunks per round: tile t = chunk t; warp w takes k-tiles 4w..4w+3
@@ -1038,6 +1011,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                     float gt = 0.f, up = 0.f;
                     #pragma unroll
                     for (int w = 0; w < kNCW; w++) { gt += red[w * 32 + 16 * t + uu]; up += red[w * 32 + 16 * t + kUnitsGU + uu]; }
+                    gt *= rn; up *= rn;
                     xw_store(hw + u + tid, (gt / (1.0f + expf(-gt))) * up, seq);
                 }
             }

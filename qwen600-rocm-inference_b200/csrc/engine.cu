@@ -19,6 +19,7 @@
 #include <mutex>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 #include <vector>
 
@@ -511,7 +512,8 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
     return QWEN_OK;
 }
 
-static int gemm_tc(const void* A, int lda, const void* B, int ldb, void* C, int ldc, int M, int N, int K, int Kb, bool c_fp32,
+struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
+static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
                    cudaStream_t st);
 
 // Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
@@ -537,20 +539,20 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
         uint16_t* kc_l = c->kc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = c->vc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, P.in_ln[l], c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wq[l], DIM, c->pf_y, kLdQKV, rows, Q_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK) return rc;
-        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wk[l], DIM, c->pf_y + Q_DIM, kLdQKV, rows, KV_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK) return rc;
-        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wv[l], DIM, c->pf_y + Q_DIM + KV_DIM, kLdQKV, rows, KV_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK)
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, kLdQKV, rows, 3 * DIM, DIM,
+                          true, st)) != QWEN_OK)
             return rc;
         qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l);
         attention_tc_kernel<<<dim3(rows / kAttBlock, N_HEADS), kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, c->wo_raw[l], Q_DIM, c->pf_y, kLdY, rows, DIM, 3 * Q_DIM, Q_DIM, true, st)) != QWEN_OK) return rc;
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st)) != QWEN_OK) return rc;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, P.post_ln[l], c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wg[l], DIM, c->pf_y, kLdY, rows, HIDDEN_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK) return rc;
-        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wu[l], DIM, c->pf_y + HIDDEN_DIM, kLdY, rows, HIDDEN_DIM, 3 * DIM, DIM, true, st)) != QWEN_OK)
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, kLdY, rows, 3 * DIM, DIM, true, st)) !=
+            QWEN_OK)
             return rc;
         swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, kLdY, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, P.wd[l], HIDDEN_DIM, c->pf_y, kLdY, rows, DIM, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st)) != QWEN_OK)
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, kLdY, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st)) !=
+            QWEN_OK)
             return rc;
     }
     CU(cudaGetLastError());
@@ -737,51 +739,72 @@ bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 uint32_t* g_gemm_err[64] = {nullptr};
 
 template <int BN, bool F32>
-int gemm_launch(const CUtensorMap& ma, const CUtensorMap& mb, void* C, int ldc, int M, int N, int K, int kb_b, cudaStream_t st, uint32_t* err) {
+int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int nsm, cudaStream_t st,
+                uint32_t* err) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
     if (attr_dev != dev) {
-        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_kernel<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<BN>::kSmem));
+        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<BN>::kSmem));
         attr_dev = dev;
     }
-    qb::tc::gemm_bf16_tc_kernel<BN, F32><<<dim3(N / BN, M / qb::tc::kBM), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
-        ma, mb, C, ldc, K, kb_b, err);
+    const int tiles = bm.end[2] * (M / qb::tc::kBM);
+    qb::tc::gemm_bf16_tc_persistent<BN, F32><<<std::min(tiles, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
+        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, err);
     CU(cudaGetLastError());
     return QWEN_OK;
 }
 }  // namespace
 
-// C[M][N] (rows ldc apart) = A[M][K] (rows lda apart) . (B[N][Kb] (rows ldb
-// apart) repeated K / Kb times along K)^T.
-static int gemm_tc(const void* A, int lda, const void* B, int ldb, void* C, int ldc, int M, int N, int K, int Kb, bool c_fp32,
+// C[M][N] (rows ldc apart) = A[M][K] (rows lda apart) . (B[N][Kb] repeated
+// K / Kb times along K)^T, where B is the segments stacked along N (each
+// [rows][Kb], rows ldb apart; at most three) and N their total rows.  One
+// persistent launch; 128 x 256 tiles when they fill every SM, else 128 x 128.
+static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
                    cudaStream_t st) {
-    if (!A || !B || !C) return fail(QWEN_E_ARG, "NULL argument");
-    if (M <= 0 || N <= 0 || K <= 0 || Kb <= 0 || M % qb::tc::kBM || N % 128 || K % qb::tc::kBK || Kb % qb::tc::kBK || K % Kb)
+    if (!A || !C || segs.size() < 1 || segs.size() > 3) return fail(QWEN_E_ARG, "NULL argument or bad segment count");
+    int N = 0;
+    bool all256 = true;
+    uintptr_t align = (uintptr_t)A | (uintptr_t)C;
+    for (const BSeg& sg : segs) {
+        if (!sg.B || sg.rows <= 0 || sg.rows % 128) return fail(QWEN_E_ARG, "N must be a multiple of 128");
+        N += sg.rows;
+        all256 = all256 && sg.rows % 256 == 0;
+        align |= (uintptr_t)sg.B;
+    }
+    if (M <= 0 || K <= 0 || Kb <= 0 || M % qb::tc::kBM || K % qb::tc::kBK || Kb % qb::tc::kBK || K % Kb)
         return fail(QWEN_E_ARG, "M must be a multiple of 128, N of 128, K of 64");
-    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15) return fail(QWEN_E_ARG, "A, B and C must be 16-byte aligned");
+    if (align & 15) return fail(QWEN_E_ARG, "A, B and C must be 16-byte aligned");
     if (lda < K || ldb < Kb || ldc < N || lda % 8 || ldb % 8 || ldc % 8) return fail(QWEN_E_ARG, "bad leading dimension");
-    int dev = 0;
+    int dev = 0, nsm = 0;
     CU(cudaGetDevice(&dev));
     if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
+    CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     if (!g_gemm_err[dev]) {
         CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
         CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
     }
-    const int bn = N % 256 == 0 ? 256 : 128;
-    CUtensorMap ma, mb;
-    if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM) ||
-        !kmajor_map(&mb, B, (uint64_t)N, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)bn))
-        return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    const int bn = all256 && (N / 256) * (M / qb::tc::kBM) >= nsm ? 256 : 128;
+    CUtensorMap ma;
+    qb::tc::BMaps bm;
+    if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    int s = 0, end = 0;
+    for (const BSeg& sg : segs) {
+        if (!kmajor_map(&bm.map[s], sg.B, (uint64_t)sg.rows, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)bn))
+            return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+        end += sg.rows / bn;
+        bm.end[s++] = end;
+    }
+    for (; s < 3; s++) { bm.map[s] = bm.map[0]; bm.end[s] = end; }
     const int kb_b = Kb / qb::tc::kBK;
-    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev])
-                                 : gemm_launch<256, false>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev]);
-    return c_fp32 ? gemm_launch<128, true>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev])
-                  : gemm_launch<128, false>(ma, mb, C, ldc, M, N, K, kb_b, st, g_gemm_err[dev]);
+    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev])
+                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev]);
+    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev])
+                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev]);
 }
 
 extern "C" int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream) {
-    return gemm_tc(A, K, B, K, C, N, M, N, K, K, c_fp32 != 0, (cudaStream_t)stream);
+    return gemm_tc(A, K, {{B, N}}, K, C, N, M, K, K, c_fp32 != 0, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------

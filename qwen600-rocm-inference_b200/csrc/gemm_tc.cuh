@@ -6,16 +6,20 @@
 // prompt rows against a weight matrix stored row-major [N][K] (nn.Linear
 // layout, K contiguous), so both operands are K-major.
 //
-// One CTA per 128 x BN output tile, 192 threads:
+// Persistent kernel, one CTA per SM (or per tile when there are fewer tiles),
+// 192 threads; CTA b takes output tiles b, b + grid, ... (128 x BN each):
 //   warp 0, one thread: TMA producer — 2-D tiled bulk tensor loads of a
 //           128 x 64 A box and a BN x 64 B box per K step, 128-byte swizzle,
-//           into a kStages-deep ring (mbarrier complete_tx); no multicast;
-//   warp 1: allocates BN TMEM columns (the fp32 accumulator, 128 lanes = the
-//           tile's rows); one thread issues four 128 x BN x 16 MMAs per K step
-//           from shared-memory descriptors and commits each stage back to the
-//           producer (tcgen05.commit -> mbarrier);
-//   warps 2-5: epilogue — wait for the last commit, read their 32 TMEM lanes
-//           (tcgen05.ld 32x32b) and store fp32 or bf16 rows.
+//           into a kStages-deep ring (mbarrier complete_tx) that runs on
+//           across tile boundaries; no multicast;
+//   warp 1: allocates 2 x BN TMEM columns (two fp32 accumulators, 128 lanes =
+//           the tile's rows); one thread issues four 128 x BN x 16 MMAs per K
+//           step from shared-memory descriptors, commits each stage back to
+//           the producer (tcgen05.commit -> mbarrier) and each finished tile
+//           to the epilogue, alternating accumulators;
+//   warps 2-5: epilogue — wait for a tile's accumulator, read their 32 TMEM
+//           lanes (tcgen05.ld 32x32b), store fp32 or bf16 rows and hand the
+//           accumulator back, while the MMA thread fills the other one.
 // Every wait is bounded; on expiry the thread sets *err and stops waiting; the
 // TMEM allocation is always released.
 #pragma once
@@ -33,15 +37,6 @@ constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kUmmaK = 16;          // K of one tcgen05.mma for 16-bit inputs
 constexpr uint64_t kWaitNs = 2000000000ull;
-
-template <int BN>
-struct Layout {
-    static constexpr int kABytes = kBM * kBK * 2;          // 16 KB
-    static constexpr int kBBytes = BN * kBK * 2;           // 32 KB at BN = 256
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarOff = kStages * kStageBytes;  // full[kStages], empty[kStages], done, tmem slot
-    static constexpr int kSmem = kBarOff + (2 * kStages + 1) * 8 + 16 + 1024;   // + alignment slack
-};
 
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
 // layout that TMA writes: rows of 128 B, 8-row groups 1024 B apart (SBO),
@@ -122,34 +117,60 @@ __device__ __forceinline__ void store32(void* C, int ldc, int m, int n, const fl
     }
 }
 
-// grid (N / BN, M / 128); K a multiple of 64; ldc in elements.  B's K extent
-// may be a divisor kb_b * 64 of K: K step kb reads B columns (kb mod kb_b) * 64,
-// so A = [a_1 | a_2 | a_3] (each K/3 wide) against B gives sum_i a_i . B^T —
-// the three-part bf16 split of fp32 activations in one accumulation.
+// Persistent form: grid = min(tiles, SMs); CTA b takes tiles b, b + grid, ...
+// (tile = (n block, m block), n fastest).  Two TMEM accumulators (2 x BN
+// columns): the MMA thread fills one while the epilogue warps drain the other,
+// so a tile's epilogue overlaps the next tile's mainloop.  The producer runs
+// ahead across tile boundaries through the same stage ring.
+//
+// B may be up to three matrices side by side along N (a grouped GEMM, e.g.
+// the q, k and v projections of one layer, which are not adjacent in memory):
+// n blocks [end[s-1], end[s]) read map[s] from its row 0; C's columns stay
+// contiguous (n block j writes columns j * BN ..).
+//
+// K a multiple of 64; ldc in elements.  B's K extent may be a divisor
+// kb_b * 64 of K: K step kb reads B columns (kb mod kb_b) * 64, so
+// A = [a_1 | a_2 | a_3] (each K/3 wide) against B gives sum_i a_i . B^T — the
+// three-part bf16 split of fp32 activations in one accumulation.
+struct BMaps {
+    CUtensorMap map[3];
+    int end[3];   // cumulative n-block counts; end[2] = total n blocks
+};
+template <int BN>
+struct Layout {
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOff = kStages * kStageBytes;   // full[S], empty[S], acc_full[2], acc_empty[2], tmem slot
+    static constexpr int kSmem = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
+};
 template <int BN, bool kOutF32>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void* C, int ldc, int K,
-                    int kb_b, uint32_t* err) {
+gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
+                        int kb_b, int m_blocks, uint32_t* err) {
     using L = Layout<BN>;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
+    static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
     uint64_t* empty = full + kStages;
-    uint64_t* done = empty + kStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* acc_full = empty + kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
-    const int nkb = K / kBK;
+    const int n_blocks = bm.end[2];
+    const int nkb = K / kBK, ntiles = n_blocks * m_blocks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; b++) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
         fence_barrier_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_b) : "memory");
+        for (int s = 0; s < 3; s++)
+            if (s == 0 || bm.end[s] > bm.end[s - 1]) asm volatile("prefetch.tensormap [%0];" ::"l"(&bm.map[s]) : "memory");
     }
-    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -157,47 +178,70 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int kb = 0; kb < nkb; kb++) {
-                const int s = kb % kStages;
-                if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); break; }
-                uint8_t* st = smem + s * L::kStageBytes;
-                mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-                tma_load_2d(st, &map_a, kb * kBK, m0, &full[s]);
-                tma_load_2d(st + L::kABytes, &map_b, (kb % kb_b) * kBK, n0, &full[s]);
+            uint32_t it = 0;   // stage-ring position across tiles
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int nb = t % n_blocks, m0 = (t / n_blocks) * kBM;
+                const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
+                const CUtensorMap* mb = &bm.map[sg];
+                const int n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN;   // row in matrix sg
+                for (int kb = 0; kb < nkb; kb++, it++) {
+                    const uint32_t s = it % kStages;
+                    if (it >= (uint32_t)kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) {
+                        atomicOr(err, 1u); ok = false; break;
+                    }
+                    uint8_t* st = smem + s * L::kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                    tma_load_2d(st, &map_a, kb * kBK, m0, &full[s]);
+                    tma_load_2d(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t id = idesc_bf16_f32(kBM, BN);
+            uint32_t it = 0, i = 0;
             bool ok = true;
-            for (int kb = 0; kb < nkb; kb++) {
-                const int s = kb % kStages;
-                if (!mbar_wait(&full[s], (kb / kStages) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+                const uint32_t b = i & 1u, use = i >> 1;
+                if (ok && use > 0 && !mbar_wait(&acc_empty[b], (use - 1) & 1u, kWaitNs)) { atomicOr(err, 8u); ok = false; }
                 tc_fence_after();
-                const uint32_t a = smem_addr(smem + s * L::kStageBytes), b = a + L::kABytes;
-                #pragma unroll
-                for (int kk = 0; kk < kBK / kUmmaK; kk++)
-                    mma_bf16(tmem, kmajor_sw128_desc(a + kk * 32), kmajor_sw128_desc(b + kk * 32), id, (kb | kk) != 0 ? 1u : 0u);
-                mma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+                const uint32_t d = tmem + b * BN;
+                for (int kb = 0; kb < nkb && ok; kb++, it++) {
+                    const uint32_t s = it % kStages;
+                    if (!mbar_wait(&full[s], (it / kStages) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_addr(smem + s * L::kStageBytes), bb = a + L::kABytes;
+                    #pragma unroll
+                    for (int kk = 0; kk < kBK / kUmmaK; kk++)
+                        mma_bf16(d, kmajor_sw128_desc(a + kk * 32), kmajor_sw128_desc(bb + kk * 32), id, (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&acc_full[b]);   // the accumulator is complete (or abandoned: *err is set)
             }
-            (void)ok;                    // on error the epilogue stores garbage; *err is set
-            mma_commit(done);            // arrives once every MMA issued above has completed
         }
     } else {
-        const int q = warp & 3;          // the TMEM lane quarter warp w may read is w % 4
-        if (!mbar_wait(done, 0, 2 * kWaitNs)) atomicOr(err, 4u);
-        tc_fence_after();
-        const int m = m0 + 32 * q + lane;
-        #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-            float v[32];
-            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
-            store32<kOutF32>(C, ldc, m, n0 + c, v);
+        const int q = warp & 3;
+        uint32_t i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+            const uint32_t b = i & 1u, use = i >> 1;
+            if (!mbar_wait(&acc_full[b], use & 1u, 2 * kWaitNs)) atomicOr(err, 4u);
+            tc_fence_after();
+            const int n0 = (t % n_blocks) * BN, m = (t / n_blocks) * kBM + 32 * q + lane;
+            #pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                float v[32];
+                tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+                store32<kOutF32>(C, ldc, m, n0 + c, v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);   // this warp has read its lanes of accumulator b
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, BN);
+    if (warp == 1) tmem_dealloc(tmem, 2 * BN);
 }
 
 }  // namespace tc

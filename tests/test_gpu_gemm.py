@@ -1,4 +1,4 @@
-"""qwen_gemm_bf16 (tcgen05 tensor-core GEMM) against float64 products of the same
+"""qwen_gemm_bf16 (persistent tcgen05 tensor-core GEMM) against float64 products of the same
 bf16 inputs: C = A B^T with A [M][K], B [N][K] row-major.  fp32 output within
 1e-5 of sum |a_k b_k| per element (fp32 accumulation of exact bf16 products);
 bf16 output within one bf16 rounding of that."""
@@ -21,7 +21,11 @@ def _case(qb, M, N, K, c_fp32, seed):
     return C.double(), ref, mag
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 384, 512), (384, 512, 1024), (2048, 4096, 1024), (2048, 1024, 3072)])
+# (2048, 4096), (2048, 6144) and (4096, 4096) have more 128 x 256 tiles than SMs:
+# each CTA of the persistent kernel takes two to four tiles and alternates its
+# two TMEM accumulators; the others run one 128 x 128 tile per CTA.
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 384, 512), (384, 512, 1024), (2048, 4096, 1024), (2048, 1024, 3072),
+                                   (2048, 6144, 1024), (4096, 4096, 256)])
 def test_gemm_fp32_out(qb, M, N, K):
     C, ref, mag = _case(qb, M, N, K, True, M + N + K)
     err = ((C - ref).abs() / (mag + 1e-30)).max().item()
