@@ -65,6 +65,15 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def measured_bf16_peak():
+    """Dense bf16 TFLOP/s of a cuBLAS GEMM timed as a burst on this pool's B200s
+    (the kernels below are timed alone), else the 1,590 fallback."""
+    try:
+        return float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def profiled_traffic():
     """dram read+write bytes per decode launch from the committed ncu summary."""
     p = os.path.join(REPO, "profiles", "decode_kernel_ncu.md")
@@ -211,6 +220,48 @@ def gemv_sweep(qb, peak):
     return out
 
 
+# (M, N, K): the prefill projections of a 2048-row pass as the engine runs them
+# (K = 3 x the input width: activations split into three bf16 parts) — q|k|v,
+# gate|up, O, down
+GEMM_SHAPES = [(2048, 4096, 3072), (2048, 6144, 3072), (2048, 1024, 6144), (2048, 1024, 9216)]
+
+
+def gemm_sweep(qb, peak_tflops):
+    """Isolated tcgen05 GEMM C = A B^T (bf16 in, fp32 out) through qwen_gemm_bf16
+    at the prefill shapes: A ~ N(0,1), B ~ N(0,0.05) from a seed.  Each timed
+    launch is bracketed alone by CUDA events with a 256 MB write before it to
+    flush L2; the reported time is the median of 10 after 3 warm-up launches.
+    TFLOP/s counts the executed 2 M N K."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(1)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    out = []
+    for m, n, k in GEMM_SHAPES:
+        A = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+        B = (torch.randn(n, k, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+        C = torch.empty(m, n, dtype=torch.float32, device="cuda")
+        call = lambda: qb.gemm_bf16(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, True, stream.cuda_stream)
+        for _ in range(3):
+            call()
+        ts = []
+        for _ in range(10):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        us = float(np.median(ts))
+        tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+        out.append({"m": m, "n": n, "k": k, "us": us, "tflops": tf, "frac": tf / peak_tflops})
+        del A, B, C
+    del flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def long_context(qb, ck, n_prompt=4096, n_gen=512):
     """4096 seeded prompt tokens, then 512 sampled tokens (temperature 0.6,
     top-k 20, top-p 0.95, seeded xorshift64*), KV cache sized 8192: decode
@@ -256,7 +307,8 @@ def prefill_bench(qb, ck, n_prompt=2048, n_gen=32):
     return {"value": n_prompt / dt, "unit": "tok/s", "prompt_tokens": n_prompt, "ms": dt * 1e3,
             "algorithmic_tflop": alg / 1e12, "achieved_tflops": alg / dt / 1e12,
             "executed_tensor_tflop": 3 * PREFILL_LINEAR_FLOP * n_prompt / 1e12,
-            "path": "28 layers x (6 tcgen05 GEMMs over all prompt rows + fp32 causal attention), decode kernel for the last token",
+            "path": "28 layers x (4 persistent tcgen05 GEMM launches over all prompt rows + causal attention on mma.m16n8k16), "
+                    "decode kernel for the last token",
             "decode_after": {"tokens": n_gen, "tok_s": n_gen / (ms / 1e3)}}
 
 
@@ -368,6 +420,10 @@ def run_mine(args):
             eng.close()
             torch.cuda.empty_cache()
             line["gemv_sweep"] = {"shapes": gemv_sweep(qb, peak), "peak_gbs": peak,
+                                  "l2": "flushed (256 MB write) between timed launches"}
+            bf16_peak = measured_bf16_peak()
+            line["gemm_sweep"] = {"shapes": gemm_sweep(qb, bf16_peak), "peak_tflops": bf16_peak,
+                                  "peak_source": "bf16_tflops (burst, MEASURED_PEAKS.json)",
                                   "l2": "flushed (256 MB write) between timed launches"}
             line["long_context"] = long_context(qb, ck)
             line["prefill"] = prefill_bench(qb, ck)
