@@ -543,7 +543,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
                           true, st)) != QWEN_OK)
             return rc;
         qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l);
-        attention_tc_kernel<<<dim3(rows / kAttBlock, N_HEADS), kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
+        attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st)) != QWEN_OK) return rc;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, P.post_ln[l], c->pf_as, kLdAs, rows);

@@ -147,69 +147,113 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int m, in
 
 // ---------------------------------------------------------------------------
 // Causal GQA attention on the tensor cores (mma.m16n8k16, bf16 in, fp32
-// accumulate).  One CTA per (64 query rows, q head); warp w owns rows 16w..16w+15.
-// S = Q K^T with Q split into three bf16 parts (K is bf16 in the cache: exact),
-// online softmax on the accumulator fragments, O += P V with P split into three
-// bf16 parts (V exact) — fp32-level numerics.  K and V tiles sit in shared
-// memory with 16-byte row pads (conflict-free ldmatrix; V through .trans).
+// accumulate).  One CTA per (64 query rows, KV head): its 8 warps cover both q
+// heads of the group (warp w: head 2 hk + w / 4, rows 16 (w % 4) .. +15), so
+// each K/V tile is loaded once for two heads.  S = Q K^T with Q split into
+// three bf16 parts (K is bf16 in the cache: exact), online softmax on the
+// accumulator fragments in base 2 with the 1/sqrt(d) scale folded into the
+// exponent, O += P V with P split into three bf16 parts (V exact) —
+// fp32-level numerics.  K/V tiles are double-buffered (cp.async, 16-byte
+// row pads: conflict-free ldmatrix, V through .trans); the CTAs with the most
+// causal work are numbered first.
 // ---------------------------------------------------------------------------
 constexpr int kTcRowE = HEAD_DIM + 8;     // padded smem row, elements (272 B)
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 256;
+
 struct AttTcSmem {
-    uint16_t q[3][kAttBlock][kTcRowE];    // hi, mid, lo parts of the 64 query rows
-    uint16_t k[kAttBlock][kTcRowE];
-    uint16_t v[kAttBlock][kTcRowE];
+    uint16_t q[2][3][kAttBlock][kTcRowE];    // per q head: hi, mid, lo parts of the 64 query rows
+    uint16_t k[2][kAttBlock][kTcRowE];       // two K tiles (double buffer)
+    uint16_t v[2][kAttBlock][kTcRowE];
 };
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
 }
 __device__ __forceinline__ uint32_t pack_bf16(uint16_t a, uint16_t b) { return (uint32_t)a | ((uint32_t)b << 16); }
+// bf16 pair (round to nearest even) of lo, hi: lo in bits 0-15
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+// (a, b) -> three bf16 pairs h + m + l = (a, b) to fp32 precision (each
+// subtraction is exact)
+__device__ __forceinline__ void split3x2(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
+    h = cvt_bf16x2(a, b);
+    const float ra = a - __uint_as_float(h << 16), rb = b - __uint_as_float(h & 0xffff0000u);
+    m = cvt_bf16x2(ra, rb);
+    l = cvt_bf16x2(ra - __uint_as_float(m << 16), rb - __uint_as_float(m & 0xffff0000u));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__global__ void __launch_bounds__(kTcThreads)
+// grid: rows / 64 * N_KV_HEADS CTAs (1-D), kTcThreads threads, sizeof(AttTcSmem) bytes.
+__global__ void __launch_bounds__(kTcThreads, 1)
 attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
                     float* __restrict__ O) {
     extern __shared__ __align__(16) uint8_t att_tc_smem[];
     AttTcSmem& S = *reinterpret_cast<AttTcSmem*>(att_tc_smem);
-    const int h = blockIdx.y, hk = h >> 1, q0 = blockIdx.x * kAttBlock, tid = threadIdx.x;
+    const int nqb = gridDim.x / N_KV_HEADS;
+    const int qb = nqb - 1 - (int)blockIdx.x / N_KV_HEADS, hk = (int)blockIdx.x % N_KV_HEADS;
+    const int q0 = qb * kAttBlock, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
-    const float sqrt_hd = sqrtf((float)HEAD_DIM);
-    // the block's query rows, split
-    for (int i = tid; i < kAttBlock * HEAD_DIM / 4; i += kTcThreads) {
-        const int r = i / (HEAD_DIM / 4), c = (i % (HEAD_DIM / 4)) * 4;
-        const float4 v = *(const float4*)(Q + (size_t)(q0 + r) * Q_DIM + 128 * h + c);
-        uint16_t hh[4], mm[4], ll[4];
-        split3(v.x, hh[0], mm[0], ll[0]); split3(v.y, hh[1], mm[1], ll[1]);
-        split3(v.z, hh[2], mm[2], ll[2]); split3(v.w, hh[3], mm[3], ll[3]);
-        *(uint2*)&S.q[0][r][c] = make_uint2(pack_bf16(hh[0], hh[1]), pack_bf16(hh[2], hh[3]));
-        *(uint2*)&S.q[1][r][c] = make_uint2(pack_bf16(mm[0], mm[1]), pack_bf16(mm[2], mm[3]));
-        *(uint2*)&S.q[2][r][c] = make_uint2(pack_bf16(ll[0], ll[1]), pack_bf16(ll[2], ll[3]));
+    const int hl = warp >> 2, wr = warp & 3, h = 2 * hk + hl;     // this warp's q head, and its 16-row slice
+    const int last = min(pos0 + q0 + kAttBlock - 1, SEQ_LEN - 1);
+    const int ntiles = last / kAttBlock + 1;
+    const uint16_t* kb = kc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
+    const uint16_t* vb = vc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
+    // tile t of K and V into buffer t & 1: 64 rows x 16 chunks of 16 bytes each, 8 per thread
+    auto load_tile = [&](int t) {
+        const int k0 = t * kAttBlock, bf = t & 1;
+        #pragma unroll
+        for (int i = 0; i < (kAttBlock * HEAD_DIM / 8) / kTcThreads; i++) {
+            const int e = tid + i * kTcThreads, r = e >> 4, c = (e & 15) * 8;
+            const size_t src = (size_t)min(k0 + r, SEQ_LEN - 1) * HEAD_DIM + c;
+            cp_async16(&S.k[bf][r][c], kb + src);
+            cp_async16(&S.v[bf][r][c], vb + src);
+        }
+        cp_async_commit();
+    };
+    load_tile(0);
+    // the block's query rows of both heads, split
+    for (int i = tid; i < 2 * kAttBlock * HEAD_DIM / 4; i += kTcThreads) {
+        const int hh = i / (kAttBlock * HEAD_DIM / 4), rem = i % (kAttBlock * HEAD_DIM / 4);
+        const int r = rem / (HEAD_DIM / 4), c = (rem % (HEAD_DIM / 4)) * 4;
+        const float4 v = *(const float4*)(Q + (size_t)(q0 + r) * Q_DIM + 128 * (2 * hk + hh) + c);
+        uint32_t h0, m0, l0, h1, m1, l1;
+        split3x2(v.x, v.y, h0, m0, l0);
+        split3x2(v.z, v.w, h1, m1, l1);
+        *(uint2*)&S.q[hh][0][r][c] = make_uint2(h0, h1);
+        *(uint2*)&S.q[hh][1][r][c] = make_uint2(m0, m1);
+        *(uint2*)&S.q[hh][2][r][c] = make_uint2(l0, l1);
     }
-    const int rowA = 16 * warp + (lane & 15);                    // ldmatrix row of this lane for A tiles
-    const uint32_t qa = smem_addr(&S.q[0][rowA][(lane >> 4) * 8]);
+    const int rowA = 16 * wr + (lane & 15);                       // ldmatrix row of this lane for A tiles
+    const uint32_t qa = smem_addr(&S.q[hl][0][rowA][(lane >> 4) * 8]);
     constexpr uint32_t kQPart = kAttBlock * kTcRowE * 2;         // bytes between q parts
+    constexpr uint32_t kKVBuf = kAttBlock * kTcRowE * 2;         // bytes between the two K (or V) buffers
     // B fragments of K (keys x dims, row-major = col-major B): lanes 0-7 keys 0-7 @ d, 8-15 keys 0-7 @ d+8,
     // 16-23 keys 8-15 @ d, 24-31 keys 8-15 @ d+8
-    const uint32_t kb_addr = smem_addr(&S.k[(lane & 7) + ((lane >> 4) << 3)][((lane >> 3) & 1) * 8]);
+    const uint32_t kb_addr = smem_addr(&S.k[0][(lane & 7) + ((lane >> 4) << 3)][((lane >> 3) & 1) * 8]);
     // B fragments of V via .trans: lanes 0-7 keys 0-7 @ n, 8-15 keys 8-15 @ n, 16-23 keys 0-7 @ n+8, 24-31 keys 8-15 @ n+8
-    const uint32_t vb_addr = smem_addr(&S.v[(lane & 15)][(lane >> 4) * 8]);
+    const uint32_t vb_addr = smem_addr(&S.v[0][(lane & 15)][(lane >> 4) * 8]);
+    // scores stay in raw units; p = 2^((s - max) * c), c = log2(e) / sqrt(d)
+    const float c2 = 1.4426950408889634f / sqrtf((float)HEAD_DIM);
     float o[16][4];
     #pragma unroll
     for (int i = 0; i < 16; i++) { o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f; }
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-    const int qp0 = pos0 + q0 + 16 * warp + g, qp1 = qp0 + 8;     // this lane's two query positions
-    const int last = min(pos0 + q0 + kAttBlock - 1, SEQ_LEN - 1);
-    const uint16_t* kb = kc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
-    const uint16_t* vb = vc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
-    for (int k0 = 0; k0 <= last; k0 += kAttBlock) {
-        __syncthreads();   // q split written / the previous tile consumed
-        for (int i = tid; i < kAttBlock * HEAD_DIM / 8; i += kTcThreads) {
-            const int r = i / (HEAD_DIM / 8), c = (i % (HEAD_DIM / 8)) * 8;
-            const int kp = min(k0 + r, SEQ_LEN - 1);
-            *(uint4*)&S.k[r][c] = *(const uint4*)(kb + (size_t)kp * HEAD_DIM + c);
-            *(uint4*)&S.v[r][c] = *(const uint4*)(vb + (size_t)kp * HEAD_DIM + c);
-        }
-        __syncthreads();
+    const int qmin = pos0 + q0 + 16 * wr;                         // the warp's first query position
+    const int qp0 = qmin + g, qp1 = qp0 + 8;                       // this lane's two query positions
+    for (int t = 0; t < ntiles; t++) {
+        if (t + 1 < ntiles) { load_tile(t + 1); cp_async_wait<1>(); }
+        else cp_async_wait<0>();
+        __syncthreads();   // tile t (and, at t = 0, the split q rows) visible to every warp
+        const int k0 = t * kAttBlock;
+        const uint32_t kbuf = kb_addr + (t & 1) * kKVBuf, vbuf = vb_addr + (t & 1) * kKVBuf;
         // S (16 rows x 64 keys) = Q K^T: 8 n-tiles of 8 keys
         float sc[8][4];
         #pragma unroll
@@ -222,7 +266,7 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
             #pragma unroll
             for (int np = 0; np < 4; np++) {   // keys 16np .. 16np+15: two n-tiles
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4(kb_addr + np * 16 * kTcRowE * 2 + kt * 32, b0, b1, b2, b3);
+                ldsm_x4(kbuf + np * 16 * kTcRowE * 2 + kt * 32, b0, b1, b2, b3);
                 #pragma unroll
                 for (int p = 0; p < 3; p++) {
                     mma_bf16_16816(sc[2 * np], a[p][0], a[p][1], a[p][2], a[p][3], b0, b1);
@@ -230,33 +274,40 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
                 }
             }
         }
+        // causal mask, only where the tile reaches past the warp's first query
+        if (k0 + kAttBlock - 1 > qmin) {
+            #pragma unroll
+            for (int n = 0; n < 8; n++) {
+                #pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int kp = k0 + 8 * n + 2 * qd + (e & 1);
+                    if (kp > (e < 2 ? qp0 : qp1)) sc[n][e] = -INFINITY;
+                }
+            }
+        }
         // online softmax over this tile (rows g and g + 8 of the warp)
         float mx[2] = {-INFINITY, -INFINITY};
         #pragma unroll
         for (int n = 0; n < 8; n++) {
-            #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int kp = k0 + 8 * n + 2 * qd + (e & 1);
-                const int qp = e < 2 ? qp0 : qp1;
-                sc[n][e] = kp <= qp ? sc[n][e] / sqrt_hd : -INFINITY;
-                mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
-            }
+            mx[0] = fmaxf(mx[0], fmaxf(sc[n][0], sc[n][1]));
+            mx[1] = fmaxf(mx[1], fmaxf(sc[n][2], sc[n][3]));
         }
-        float scale[2];
+        float scale[2], mc[2];
         #pragma unroll
         for (int r = 0; r < 2; r++) {
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
             mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
             const float mn = fmaxf(mrow[r], mx[r]);   // finite: key 0 precedes every query
-            scale[r] = expf(mrow[r] - mn);
+            scale[r] = exp2f((mrow[r] - mn) * c2);    // 0 on the first tile (mrow = -inf)
             mrow[r] = mn;
+            mc[r] = mn * c2;
         }
         float ps[2] = {0.f, 0.f};
         #pragma unroll
         for (int n = 0; n < 8; n++) {
             #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const float pr = sc[n][e] == -INFINITY ? 0.f : expf(sc[n][e] - mrow[e >> 1]);
+                const float pr = exp2f(fmaf(sc[n][e], c2, -mc[e >> 1]));   // masked: 2^-inf = 0
                 sc[n][e] = pr;
                 ps[e >> 1] += pr;
             }
@@ -276,15 +327,12 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
             #pragma unroll
             for (int j = 0; j < 4; j++) {   // a0: (g, keys 2qd..) = n-tile 2kt d0,d1; a1: rows g+8 = d2,d3; a2, a3: n-tile 2kt+1
                 const float* src = &sc[2 * kt + (j >> 1)][(j & 1) * 2];
-                uint16_t h0, m0, l0, h1, m1, l1;
-                split3(src[0], h0, m0, l0);
-                split3(src[1], h1, m1, l1);
-                a[0][j] = pack_bf16(h0, h1); a[1][j] = pack_bf16(m0, m1); a[2][j] = pack_bf16(l0, l1);
+                split3x2(src[0], src[1], a[0][j], a[1][j], a[2][j]);
             }
             #pragma unroll
             for (int np = 0; np < 8; np++) {   // dims 16np .. 16np+15: two n-tiles
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_trans(vb_addr + kt * 16 * kTcRowE * 2 + np * 32, b0, b1, b2, b3);
+                ldsm_x4_trans(vbuf + kt * 16 * kTcRowE * 2 + np * 32, b0, b1, b2, b3);
                 #pragma unroll
                 for (int p = 0; p < 3; p++) {
                     mma_bf16_16816(o[2 * np], a[p][0], a[p][1], a[p][2], a[p][3], b0, b1);
@@ -292,10 +340,11 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
                 }
             }
         }
+        __syncthreads();   // every warp is done with buffer t & 1 before tile t + 2 is copied into it
     }
     // O rows g, g + 8 of the warp; dims 8n + 2qd, +1
     const float inv0 = 1.0f / lrow[0], inv1 = 1.0f / lrow[1];
-    float* o0 = O + (size_t)(q0 + 16 * warp + g) * Q_DIM + 128 * h + 2 * qd;
+    float* o0 = O + (size_t)(q0 + 16 * wr + g) * Q_DIM + 128 * h + 2 * qd;
     float* o1 = o0 + (size_t)8 * Q_DIM;
     #pragma unroll
     for (int n = 0; n < 16; n++) {
