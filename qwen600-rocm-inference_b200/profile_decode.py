@@ -3,12 +3,14 @@
     python qwen600-rocm-inference_b200/profile_decode.py [--prompt N] [--steps K] [--device D]
 
 Builds an Engine on the seed-0 synthetic checkpoint, prefills N seeded prompt
-tokens (rng 1000, as bench.py does: N launches of the decode kernel), then
-decodes K greedy positions with qwen_decode_step (one launch each) and prints
-the host wall time per step.  ncu counts --launch-skip over the launches that
-match its kernel filter, so
+tokens (rng 1000) with qwen_prefill — for N >= 65 the tensor-core passes over
+positions 0..N-2 and one decode-kernel launch for the last token; below that,
+N decode-kernel launches — then decodes K greedy positions with
+qwen_decode_step (one launch each) and prints the host wall time per step.
+ncu counts --launch-skip over the launches that match its kernel filter, so
+for N >= 65
 
-    ncu --set full --clock-control none -k regex:decode_kernel -s <N + 1> -c 1 ...
+    ncu --set full --clock-control none -k regex:decode_kernel -s 2 -c 1 ...
 
 captures the second decode step: position N + 1, context N + 2.
 """
