@@ -514,7 +514,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
 
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
-                   cudaStream_t st);
+                   cudaStream_t st, int split_cols = 0, int* splits_used = nullptr);
 
 // Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
 // layer's projections as tcgen05 GEMMs over all rows, attention over the KV
@@ -534,25 +534,27 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
     cudaStream_t st = c->stream;
     const int rows = (m + tc::kBM - 1) / tc::kBM * tc::kBM;
     embed_kernel<<<rows, 256, 0, st>>>(P.embed, c->prompt + pos0, m, rows, c->pf_x);
-    int rc;
+    int rc, sp_o = 1, sp_d = 1;   // K splits of the O and down GEMMs: partial sums side by side in pf_y
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = c->kc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = c->vc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
-        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, P.in_ln[l], c->pf_as, kLdAs, rows);
+        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, sp_d, P.in_ln[l], c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, kLdQKV, rows, 3 * DIM, DIM,
                           true, st)) != QWEN_OK)
             return rc;
         qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l);
         attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st)) != QWEN_OK) return rc;
-        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, P.post_ln[l], c->pf_as, kLdAs, rows);
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o)) !=
+            QWEN_OK)
+            return rc;
+        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, sp_o, P.post_ln[l], c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, kLdY, rows, 3 * DIM, DIM, true, st)) !=
             QWEN_OK)
             return rc;
         swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, kLdY, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, kLdY, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st)) !=
-            QWEN_OK)
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, kLdY, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
+                          &sp_d)) != QWEN_OK)
             return rc;
     }
     CU(cudaGetLastError());
@@ -739,8 +741,8 @@ bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 uint32_t* g_gemm_err[64] = {nullptr};
 
 template <int BN, bool F32>
-int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int nsm, cudaStream_t st,
-                uint32_t* err) {
+int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
+                int nsm, cudaStream_t st, uint32_t* err) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -748,9 +750,9 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
         CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<BN>::kSmem));
         attr_dev = dev;
     }
-    const int tiles = bm.end[2] * (M / qb::tc::kBM);
-    qb::tc::gemm_bf16_tc_persistent<BN, F32><<<std::min(tiles, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
-        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, err);
+    const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
+    qb::tc::gemm_bf16_tc_persistent<BN, F32><<<std::min(items, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
+        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, err);
     CU(cudaGetLastError());
     return QWEN_OK;
 }
@@ -760,8 +762,11 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
 // K / Kb times along K)^T, where B is the segments stacked along N (each
 // [rows][Kb], rows ldb apart; at most three) and N their total rows.  One
 // persistent launch; 128 x 256 tiles when they fill every SM, else 128 x 128.
+// With split_cols > 0 the caller accepts K split s ways when 128 x 256 tiles
+// would leave SMs idle: partial sum i lands at columns i * split_cols + [0, N)
+// (within ldc) and *splits_used = s, for the caller to add in order.
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
-                   cudaStream_t st) {
+                   cudaStream_t st, int split_cols, int* splits_used) {
     if (!A || !C || segs.size() < 1 || segs.size() > 3) return fail(QWEN_E_ARG, "NULL argument or bad segment count");
     int N = 0;
     bool all256 = true;
@@ -784,7 +789,14 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
         CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
         CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
     }
-    const int bn = all256 && (N / 256) * (M / qb::tc::kBM) >= nsm ? 256 : 128;
+    const int tiles256 = (N / 256) * (M / qb::tc::kBM);
+    int splits = 1;
+    if (split_cols >= N && all256 && 2 * tiles256 <= nsm)
+        while (splits < 6 && (splits + 1) * tiles256 <= nsm && (K / qb::tc::kBK) % (splits + 1) == 0 &&
+               splits * split_cols + N <= ldc)
+            splits++;
+    if (splits_used) *splits_used = splits;
+    const int bn = all256 && (splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;
     qb::tc::BMaps bm;
     if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
@@ -797,10 +809,11 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     }
     for (; s < 3; s++) { bm.map[s] = bm.map[0]; bm.end[s] = end; }
     const int kb_b = Kb / qb::tc::kBK;
-    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev])
-                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev]);
-    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev])
-                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, nsm, st, g_gemm_err[dev]);
+    const int so = splits > 1 ? split_cols : 0;
+    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev])
+                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev]);
+    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev])
+                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev]);
 }
 
 extern "C" int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream) {

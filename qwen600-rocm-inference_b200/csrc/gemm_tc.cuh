@@ -128,7 +128,11 @@ __device__ __forceinline__ void store32(void* C, int ldc, int m, int n, const fl
 // n blocks [end[s-1], end[s]) read map[s] from its row 0; C's columns stay
 // contiguous (n block j writes columns j * BN ..).
 //
-// K a multiple of 64; ldc in elements.  B's K extent may be a divisor
+// Split K: with splits > 1 every tile is `splits` work items, item s taking
+// K steps [s, s + 1) * K / (64 splits) and writing its partial sum at column
+// offset s * c_split_off of C (the caller adds the partials).
+//
+// K a multiple of 64 * splits; ldc in elements.  B's K extent may be a divisor
 // kb_b * 64 of K: K step kb reads B columns (kb mod kb_b) * 64, so
 // A = [a_1 | a_2 | a_3] (each K/3 wide) against B gives sum_i a_i . B^T — the
 // three-part bf16 split of fp32 activations in one accumulation.
@@ -147,7 +151,7 @@ struct Layout {
 template <int BN, bool kOutF32>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
-                        int kb_b, int m_blocks, uint32_t* err) {
+                        int kb_b, int m_blocks, int splits, int c_split_off, uint32_t* err) {
     using L = Layout<BN>;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
     static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
@@ -160,7 +164,8 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = bm.end[2];
-    const int nkb = K / kBK, ntiles = n_blocks * m_blocks;
+    const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
+    const int nkb = K / kBK / splits;   // K steps per work item
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -180,12 +185,13 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
         if (lane == 0) {
             uint32_t it = 0;   // stage-ring position across tiles
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int w = blockIdx.x; w < nitems && ok; w += gridDim.x) {
+                const int t = w % ntiles, kb0 = (w / ntiles) * nkb;
                 const int nb = t % n_blocks, m0 = (t / n_blocks) * kBM;
                 const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
                 const CUtensorMap* mb = &bm.map[sg];
                 const int n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN;   // row in matrix sg
-                for (int kb = 0; kb < nkb; kb++, it++) {
+                for (int kb = kb0; kb < kb0 + nkb; kb++, it++) {
                     const uint32_t s = it % kStages;
                     if (it >= (uint32_t)kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) {
                         atomicOr(err, 1u); ok = false; break;
@@ -202,7 +208,7 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
             constexpr uint32_t id = idesc_bf16_f32(kBM, BN);
             uint32_t it = 0, i = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+            for (int w = blockIdx.x; w < nitems; w += gridDim.x, i++) {
                 const uint32_t b = i & 1u, use = i >> 1;
                 if (ok && use > 0 && !mbar_wait(&acc_empty[b], (use - 1) & 1u, kWaitNs)) { atomicOr(err, 8u); ok = false; }
                 tc_fence_after();
@@ -223,11 +229,12 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
     } else {
         const int q = warp & 3;
         uint32_t i = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, i++) {
+        for (int w = blockIdx.x; w < nitems; w += gridDim.x, i++) {
             const uint32_t b = i & 1u, use = i >> 1;
             if (!mbar_wait(&acc_full[b], use & 1u, 2 * kWaitNs)) atomicOr(err, 4u);
             tc_fence_after();
-            const int n0 = (t % n_blocks) * BN, m = (t / n_blocks) * kBM + 32 * q + lane;
+            const int t = w % ntiles;
+            const int n0 = (t % n_blocks) * BN + (w / ntiles) * c_split_off, m = (t / n_blocks) * kBM + 32 * q + lane;
             #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 float v[32];

@@ -56,8 +56,10 @@ __global__ void embed_kernel(const uint16_t* __restrict__ embed, const int* __re
 
 // One warp per row: X[r] += add[r] (if add), then RMSNorm with `gain` (the
 // decode chain's formula: (x * (1 / sqrt(mean(x^2) + eps))) * g) into As.
-__global__ void norm_split_kernel(float* __restrict__ X, const float* __restrict__ add, int ld_add, const uint16_t* __restrict__ gain,
-                                  uint16_t* __restrict__ As, int ld_as, int rows) {
+// `add` may hold n_add partial sums side by side (columns s * DIM ..): a GEMM
+// whose K was split; they are added in order s = 0, 1, ... and then to X.
+__global__ void norm_split_kernel(float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
+                                  const uint16_t* __restrict__ gain, uint16_t* __restrict__ As, int ld_as, int rows) {
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= rows) return;
     float* x = X + (size_t)r * DIM;
@@ -68,7 +70,12 @@ __global__ void norm_split_kernel(float* __restrict__ X, const float* __restrict
         const int c = 128 * i + 4 * lane;
         v[i] = *(const float4*)(x + c);
         if (add) {
-            const float4 a = *(const float4*)(add + (size_t)r * ld_add + c);
+            const float* ar = add + (size_t)r * ld_add + c;
+            float4 a = *(const float4*)ar;
+            for (int sp = 1; sp < n_add; sp++) {
+                const float4 b = *(const float4*)(ar + sp * DIM);
+                a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+            }
             v[i].x += a.x; v[i].y += a.y; v[i].z += a.z; v[i].w += a.w;
             *(float4*)(x + c) = v[i];
         }
