@@ -172,6 +172,33 @@ int qwen_sample_host(const float* logits, int n, const qwen_sampling_t* sp,
 int qwen_sample_candidates(const float* values, const int* ids, int n, const qwen_sampling_t* sp,
                            unsigned long long* rng_state, int* token_out);
 
+/* ---- tokenizer (tokenizer.h, export.py) ---------------------------------- */
+
+typedef struct qwen_tokenizer qwen_tokenizer_t;
+
+/* Reads a tokenizer.bin (export.py:168-244 writes it; tokenizer.h:38-70 reads
+ * it): u32 max_token_length, u32 bos, u32 eos, then per token f32 merge score,
+ * u32 byte length, the bytes.  vocab_size entries are read (<= 0: the model's
+ * 151936); entries past the end of the file are empty, as in the reference.
+ * QWEN_E_IO if the file cannot be opened, QWEN_E_FORMAT if it is truncated
+ * inside an entry.  Replaces build_tokenizer's file part (tokenizer.h:38-70;
+ * the prompt templates are text files the caller renders). */
+int qwen_tokenizer_load(const char* path, int vocab_size, qwen_tokenizer_t** out);
+void qwen_tokenizer_free(qwen_tokenizer_t* t);
+int qwen_tokenizer_info(const qwen_tokenizer_t* t, int* vocab_size, int* max_token_length, int* bos, int* eos);
+
+/* encode() (tokenizer.h:104-185): bytes -> one-byte entries ("<...>" special
+ * entries first), then greedy best-score pair merges; the same token ids as the
+ * reference, with hash lookups instead of linear vocabulary scans.  Writes at
+ * most cap ids; *n_tokens is the full count (QWEN_E_ARG if it exceeds cap).
+ * Bytes without a one-byte entry are skipped and counted in *n_unknown (may be
+ * NULL); the reference leaves an unwritten slot for them. */
+int qwen_tokenizer_encode(const qwen_tokenizer_t* t, const char* text, int* tokens, int cap, int* n_tokens, int* n_unknown);
+
+/* decode() (tokenizer.h:80-82): the token's bytes as a NUL-terminated string
+ * owned by the tokenizer. */
+int qwen_tokenizer_decode(const qwen_tokenizer_t* t, int token, const char** piece);
+
 /* ---- diagnostics ---------------------------------------------------------- */
 
 /* Per-CTA ring accounting of the last decode launch: out[2c] = chunks the

@@ -1,7 +1,8 @@
 /* qwen_model_b200.h — the reference's C++ decode API (qwen_model.cuh and
  * sampler.h, Ramshankar07/qwen600-ROCm-inference) on top of libqwen_b200.so.
  *
- * A program written against the reference keeps its calls:
+ * A program written against the reference keeps its calls (and, host-only,
+ * its tokenizer.h calls: Tokenizer, build_tokenizer, encode, decode):
  *
  *     Transformer t;  build_transformer(&t, "model.safetensors");
  *     Sampler s;      build_sampler(&s, 0.6f, 0.95f, 20, seed);
@@ -28,6 +29,8 @@
 #ifndef QWEN_MODEL_B200_H
 #define QWEN_MODEL_B200_H
 
+#include <cstdio>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 
@@ -91,6 +94,63 @@ inline int sample(Sampler* s, float* logits) {
     int tok = -1;
     qwen_model_b200_check(qwen_sample_host(logits, qwen_vocab_size(), &sp, &s->rng_state, &tok), "sample");
     return tok;
+}
+
+/* ---- tokenizer.h -------------------------------------------------------- */
+/* Tokenizer, build_tokenizer, free_tokenizer, decode, encode with the names and
+ * argument meaning of tokenizer.h:14-23, :38, :76, :80, :104.  build_tokenizer
+ * reads <dir_path>/tokenizer.bin and the two template files of the mode
+ * (template_user[_thinking].txt, template_system[_thinking].txt) as the
+ * reference does; encode writes at most strlen(text) ids (one per input byte
+ * is the most the reference's scheme produces) and skips bytes without a
+ * one-byte entry instead of leaving an unwritten slot.  Host-only: no GPU. */
+struct Tokenizer {
+    qwen_tokenizer_t* handle = nullptr;
+    int vocab_size = 0;
+    unsigned int max_token_length = 0;
+    unsigned int bos_token_id = 0;
+    unsigned int eos_token_id = 0;
+    char prompt_template[1024] = {0};
+    char system_prompt_template[1024] = {0};
+};
+
+inline void qwen_model_b200_read_template(char* buf, size_t size, const std::string& path) {
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) throw std::runtime_error("cannot open template file " + path);
+    const size_t n = fread(buf, 1, size - 1, f);
+    buf[n] = 0;
+    fclose(f);
+}
+
+inline void build_tokenizer(Tokenizer* t, const char* dir_path, int enable_thinking) {
+    std::string dir(dir_path);
+    if (!dir.empty() && dir.back() != '/') dir += '/';
+    qwen_model_b200_check(qwen_tokenizer_load((dir + "tokenizer.bin").c_str(), 0, &t->handle), "build_tokenizer");
+    int v = 0, m = 0, b = 0, e = 0;
+    qwen_model_b200_check(qwen_tokenizer_info(t->handle, &v, &m, &b, &e), "build_tokenizer");
+    t->vocab_size = v;
+    t->max_token_length = (unsigned)m;
+    t->bos_token_id = (unsigned)b;
+    t->eos_token_id = (unsigned)e;
+    const char* sfx = enable_thinking ? "_thinking.txt" : ".txt";
+    qwen_model_b200_read_template(t->prompt_template, sizeof(t->prompt_template), dir + "template_user" + sfx);
+    qwen_model_b200_read_template(t->system_prompt_template, sizeof(t->system_prompt_template), dir + "template_system" + sfx);
+}
+
+inline void free_tokenizer(Tokenizer* t) {
+    qwen_tokenizer_free(t->handle);
+    t->handle = nullptr;
+}
+
+inline char* decode(Tokenizer* t, int token) {
+    const char* piece = nullptr;
+    qwen_model_b200_check(qwen_tokenizer_decode(t->handle, token, &piece), "decode");
+    return const_cast<char*>(piece);
+}
+
+inline void encode(Tokenizer* t, char* text, int* tokens, int* n_tokens) {
+    const int cap = (int)strlen(text);
+    qwen_model_b200_check(qwen_tokenizer_encode(t->handle, text, tokens, cap, n_tokens, nullptr), "encode");
 }
 
 #endif /* QWEN_MODEL_B200_H */

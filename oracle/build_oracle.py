@@ -7,6 +7,8 @@ Outputs:
   oracle/liboracle.so            CPU restatement of the reference math (oracle.cpp)
   oracle/_ref/libref_sampler.so  the reference's sampler.h, compiled as is from
                                  the reference tree (CPU)
+  oracle/_ref/libref_tokenizer.so  the reference's tokenizer.h, compiled as is
+                                 from the reference tree (CPU; golden vectors)
   oracle/_ref/libref_model.so    the reference's CUDA forward (qwen_model.cuh,
                                  static_loader.h, config.h) compiled for sm_100a
                                  from the reference tree, linked with cuBLAS
@@ -55,6 +57,11 @@ def build(force=False):
     if force or _stale(samp, [shim, os.path.join(REF, "sampler.h"), __file__]):
         _run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-I", REF, shim, "-o", samp + ".tmp"])
         os.replace(samp + ".tmp", samp)
+    tok = os.path.join(REF_OUT, "libref_tokenizer.so")
+    tshim = os.path.join(HERE, "ref_tokenizer_shim.cpp")
+    if force or _stale(tok, [tshim, os.path.join(REF, "tokenizer.h"), os.path.join(REF, "config.h"), __file__]):
+        _run(["g++", "-O2", "-std=c++17", "-w", "-fPIC", "-shared", "-I", REF, tshim, "-o", tok + ".tmp"])
+        os.replace(tok + ".tmp", tok)
     model = os.path.join(REF_OUT, "libref_model.so")
     harness = os.path.join(HERE, "ref_model_harness.cu")
     deps = [harness, __file__] + [os.path.join(REF, f) for f in ("qwen_model.cuh", "static_loader.h", "config.h")]

@@ -44,6 +44,8 @@ static int fail(int code, const std::string& msg) { g_err = msg; return code; }
     } while (0)
 
 extern "C" const char* qwen_last_error(void) { return g_err.c_str(); }
+// for the library's host-only files (tokenizer.cpp)
+int qwen_internal_fail(int code, const std::string& msg) { return fail(code, msg); }
 extern "C" int qwen_abi_version(void) { return 10000; }
 
 // ---------------------------------------------------------------------------

@@ -69,6 +69,11 @@ _SIGS = {
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
     "qwen_set_prefill_mode": (_c.c_int, [_P, _c.c_int]),
+    "qwen_tokenizer_load": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
+    "qwen_tokenizer_free": (None, [_P]),
+    "qwen_tokenizer_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
+    "qwen_tokenizer_encode": (_c.c_int, [_P, _c.c_char_p, _P, _c.c_int, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
+    "qwen_tokenizer_decode": (_c.c_int, [_P, _c.c_int, _c.POINTER(_c.c_char_p)]),
 }
 
 _lib = None

@@ -1,7 +1,10 @@
 """The reference-named C++ API (include/qwen_model_b200.h: Transformer,
 build_transformer, forward, Sampler, build_sampler, sample — qwen_model.cuh:51-94,
-:772 and sampler.h:11-120) compiled as a plain C++ program against
-libqwen_b200.so, the way a maintainer swaps the reference's headers."""
+:772 and sampler.h:11-120; Tokenizer, build_tokenizer, encode, decode —
+tokenizer.h:14-104) compiled as plain C++ programs against libqwen_b200.so,
+the way a maintainer swaps the reference's headers."""
+import json
+import sys
 import os
 import subprocess
 
@@ -53,3 +56,29 @@ def test_shim_greedy_matches_engine(qb, checkpoint, tmp_path):
     finally:
         eng.close()
     assert got == want
+
+
+def test_shim_tokenizer_matches_reference_ids(qb, tmp_path):
+    """Host-only: the tokenizer calls of tokenizer.h through the C++ names give
+    the reference's own ids (tests/golden/tokenizer_cases.json)."""
+    qb.load_library()
+    sys.path.insert(0, os.path.join(REPO, "tests", "golden"))
+    import make_tokenizer_golden as G
+    d = tmp_path / "model"
+    d.mkdir()
+    G.write_model_dir(str(d))
+    exe = str(tmp_path / "shim_tokenizer")
+    r = subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Werror", "-I", os.path.join(REPO, "include"),
+                        os.path.join(REPO, "tests", "cpp", "shim_tokenizer.cpp"), "-o", exe, "-L", LIB_DIR, "-lqwen_b200",
+                        "-Wl,-rpath," + LIB_DIR], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    cases = json.load(open(os.path.join(REPO, "tests", "golden", "tokenizer_cases.json"), encoding="utf-8"))["cases"]
+    for case in cases:
+        if not case["text"]:
+            continue                      # (an empty argv string is fine too, but keeps the output format simple)
+        out = subprocess.run([exe, str(d), case["text"]], capture_output=True, timeout=60)
+        assert out.returncode == 0, out.stderr
+        lines = out.stdout.split(b"\n")
+        k = lines.index(next(l for l in lines if l.startswith(b"#")))
+        assert [int(x) for x in lines[:k]] == case["ids"]
+        assert b"\n".join(lines[k:])[1:].rstrip(b"\n") == case["text"].encode("utf-8").rstrip(b"\n")
