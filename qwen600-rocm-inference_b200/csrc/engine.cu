@@ -207,7 +207,7 @@ struct qwen_ctx {
     DecodeParams params{};
     // prompt pass on the tensor cores (allocated on first use)
     const uint16_t* wo_raw[N_LAYERS] = {};   // o_proj in the canonical block
-    float *pf_x = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_o = nullptr;
+    float *pf_x = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_o = nullptr, *pf_xn = nullptr;
     uint16_t* pf_as = nullptr;
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
@@ -219,7 +219,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_o, c->pf_as, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_o, c->pf_xn, c->pf_as, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -514,6 +514,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
     return QWEN_OK;
 }
 
+static int gemm_check(qwen_t* c);
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
                    cudaStream_t st, int split_cols = 0, int* splits_used = nullptr);
@@ -521,7 +522,7 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
 // Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
 // layer's projections as tcgen05 GEMMs over all rows, attention over the KV
 // cache; fills the cache, computes no logits.  Tokens are in c->prompt.
-static int prefill_pass(qwen_t* c, int pos0, int m) {
+static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr) {
     using namespace qb::pf;
     constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM, kLdQKV = Q_DIM + 2 * KV_DIM;
     if (!c->pf_x) {
@@ -530,6 +531,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
         TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
         TRY(dalloc(&c->pf_o, (size_t)kMaxRows * Q_DIM));
         TRY(dalloc(&c->pf_as, (size_t)kMaxRows * kLdAs));
+        TRY(dalloc(&c->pf_xn, (size_t)DIM));
         CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
     }
     const DecodeParams& P = c->params;
@@ -560,6 +562,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m) {
             return rc;
     }
     CU(cudaGetLastError());
+    if (down_splits) *down_splits = sp_d;
     return QWEN_OK;
 }
 
@@ -576,7 +579,27 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(c->prompt + pos0, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     int rc;
-    if (n - 1 >= kGemmPrefillMin && c->gemm_prefill) {
+    const bool full_vocab = c->params.lm_begin == 0 && c->params.lm_end == VOCAB_SIZE;
+    if (n - 1 >= kGemmPrefillMin && c->gemm_prefill && full_vocab) {
+        // every position in tensor-core passes; the logits of the last one from
+        // its final residual: RMSNorm + an fp32-input LM-head GEMV
+        int s = 0, m = 0, sp = 1;
+        for (; s < n; s += m) {
+            m = std::min(qb::pf::kMaxRows, n - s);
+            if ((rc = prefill_pass(c, pos0 + s, m, &sp)) != QWEN_OK) return rc;
+        }
+        const int last_row = m - 1;
+        qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, 2 * HIDDEN_DIM, sp, c->params.final_ln, last_row, c->pf_xn);
+        qb::pf::lm_head_f32_kernel<<<c->nsm * 8, 256, 0, c->stream>>>(c->params.lm, c->pf_xn, 0, VOCAB_SIZE, c->logits);
+        CU(cudaGetLastError());
+        if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+        CU(cudaStreamSynchronize(c->stream));
+        if ((rc = gemm_check(c)) != QWEN_OK) return rc;
+        c->last_k = 0;   // no candidate list: the decode kernel did not run
+        c->cached = pos0 + n;
+        return QWEN_OK;
+    }
+    if (n - 1 >= kGemmPrefillMin && c->gemm_prefill) {   // vocabulary shard: the last position through the decode kernel
         for (int s = 0; s < n - 1; s += qb::pf::kMaxRows)
             if ((rc = prefill_pass(c, pos0 + s, std::min(qb::pf::kMaxRows, n - 1 - s))) != QWEN_OK) return rc;
     } else if (n > 1) {
@@ -594,6 +617,7 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
     CU(cudaStreamSynchronize(c->stream));
     c->last_k = 1;
+    if ((rc = gemm_check(c)) != QWEN_OK) return rc;
     if ((rc = check_step(c)) != QWEN_OK) return rc;
     c->cached = pos0 + n;
     return QWEN_OK;
@@ -816,6 +840,20 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
                                  : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev]);
     return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev])
                   : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev]);
+}
+
+// The GEMM kernel's error word for the handle's device (a bounded wait ran out
+// in some launch since the last check): reported as QWEN_E_TIMEOUT, the KV cache
+// invalidated; cleared.  Call after the stream has drained.
+static int gemm_check(qwen_t* c) {
+    uint32_t* e = c->device < 64 ? g_gemm_err[c->device] : nullptr;
+    if (!e) return QWEN_OK;
+    uint32_t h = 0;
+    CU(cudaMemcpy(&h, e, sizeof(h), cudaMemcpyDeviceToHost));
+    if (!h) return QWEN_OK;
+    CU(cudaMemset(e, 0, sizeof(uint32_t)));
+    c->cached = 0;
+    return fail(QWEN_E_TIMEOUT, "tensor-core GEMM wait expired (code " + std::to_string(h) + "); KV cache invalidated");
 }
 
 extern "C" int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream) {

@@ -152,6 +152,72 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int m, in
     }
 }
 
+// The prompt's last row after the last layer: x = X[row] + the down
+// projection's n_add partial sums, then the final RMSNorm (the decode chain's
+// formula, qwen_model.cuh:836-839) into xn (fp32).  One block of 256 threads.
+__global__ void final_norm_row_kernel(const float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
+                                      const uint16_t* __restrict__ gain, int row, float* __restrict__ xn) {
+    __shared__ float part[8];
+    const int t = threadIdx.x, c = 4 * t;
+    float4 v = *(const float4*)(X + (size_t)row * DIM + c);
+    const float* ar = add + (size_t)row * ld_add + c;
+    float4 a = *(const float4*)ar;
+    for (int sp = 1; sp < n_add; sp++) {
+        const float4 b = *(const float4*)(ar + sp * DIM);
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
+    float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    if ((t & 31) == 0) part[t >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+    #pragma unroll
+    for (int w = 0; w < 8; w++) ss += part[w];
+    const float rs = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+    const uint2 g = *(const uint2*)(gain + c);
+    *(float4*)(xn + c) = make_float4((v.x * rs) * bf_lo(g.x), (v.y * rs) * bf_hi(g.x), (v.z * rs) * bf_lo(g.y), (v.w * rs) * bf_hi(g.y));
+}
+
+// logits[r] = LM[r] . xn for r in [r0, r1): fp32 input, bf16 weights, fp32
+// accumulation (the decode chain's head, qwen_model.cuh:841-845).  One warp per
+// row, two rows in flight per warp; lane l holds xn[8 (l + 32 i) .. +7].
+__global__ void __launch_bounds__(256) lm_head_f32_kernel(const uint16_t* __restrict__ lm, const float* __restrict__ xn, int r0, int r1,
+                                                          float* __restrict__ logits) {
+    const int lane = threadIdx.x & 31;
+    float xr[4][8];
+    #pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float4 a = *(const float4*)(xn + 8 * (lane + 32 * i)), b = *(const float4*)(xn + 8 * (lane + 32 * i) + 4);
+        xr[i][0] = a.x; xr[i][1] = a.y; xr[i][2] = a.z; xr[i][3] = a.w;
+        xr[i][4] = b.x; xr[i][5] = b.y; xr[i][6] = b.z; xr[i][7] = b.w;
+    }
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int r = r0 + 2 * (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); r < r1; r += 2 * warps) {
+        const bool two = r + 1 < r1;
+        const uint4* w0 = reinterpret_cast<const uint4*>(lm + (size_t)r * DIM);
+        const uint4* w1 = reinterpret_cast<const uint4*>(lm + (size_t)(two ? r + 1 : r) * DIM);
+        uint4 a[4], b[4];
+        #pragma unroll
+        for (int i = 0; i < 4; i++) { a[i] = __ldcs(w0 + lane + 32 * i); b[i] = __ldcs(w1 + lane + 32 * i); }
+        float s0 = 0.f, s1 = 0.f;
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t wa[4] = {a[i].x, a[i].y, a[i].z, a[i].w}, wb[4] = {b[i].x, b[i].y, b[i].z, b[i].w};
+            #pragma unroll
+            for (int j = 0; j < 4; j++) {
+                s0 = fmaf(bf_lo(wa[j]), xr[i][2 * j], s0); s0 = fmaf(bf_hi(wa[j]), xr[i][2 * j + 1], s0);
+                s1 = fmaf(bf_lo(wb[j]), xr[i][2 * j], s1); s1 = fmaf(bf_hi(wb[j]), xr[i][2 * j + 1], s1);
+            }
+        }
+        s0 = warp_sum(s0);
+        s1 = warp_sum(s1);
+        if (lane == 0) {
+            logits[r] = s0;
+            if (two) logits[r + 1] = s1;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Causal GQA attention on the tensor cores (mma.m16n8k16, bf16 in, fp32
 // accumulate).  One CTA per (64 query rows, KV head): its 8 warps cover both q
