@@ -142,9 +142,10 @@ int qwen_prefill(qwen_t* ctx, const int* tokens, int n, int pos0, float* logits_
 /* Prompt path of qwen_prefill: gemm != 0 (the default) runs prompts of 65 or
  * more tokens as whole-prompt passes on the tensor cores (every layer's
  * projections as tcgen05 GEMMs over all prompt rows, attention over the KV
- * cache), then one decode launch for the last token; gemm == 0 uses one decode
- * launch per prompt token.  No reference counterpart (the reference runs
- * forward() per prompt token, main.cu:141-145). */
+ * cache), the last position's logits from an fp32 RMSNorm and LM-head GEMV
+ * (with a vocabulary shard set: one decode launch for the last token instead);
+ * gemm == 0 uses one decode launch per prompt token.  No reference counterpart
+ * (the reference runs forward() per prompt token, main.cu:141-145). */
 int qwen_set_prefill_mode(qwen_t* ctx, int gemm);
 
 /* Number of positions currently held in the KV cache. */
