@@ -195,6 +195,8 @@ struct qwen_ctx {
     uint64_t* xchg = nullptr;      // all exchange words (one allocation)
     size_t xchg_words = 0;
     unsigned long long launches = 0;   // since the last reset (bounds the 32-bit sequence tag)
+    cudaGraphExec_t step_exec = nullptr;   // qwen_decode_step's copy-in, launch, copy-out, replayed
+    bool step_graph_off = false;           // capture failed once: direct launches from then on
     float *cand_v = nullptr, *top_v = nullptr;
     int *cand_i = nullptr, *top_i = nullptr, *prompt = nullptr, *tokens = nullptr, *chunk_count = nullptr;
     uint32_t* ctr = nullptr;
@@ -224,6 +226,7 @@ static void ctx_free(qwen_t* c) {
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
     for (void* p : host) if (p) cudaFreeHost(p);
+    if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -353,13 +356,17 @@ extern "C" float* qwen_host_logits(qwen_t* c) { return c ? c->h_logits : nullptr
 extern "C" const float* qwen_device_logits(qwen_t* c) { return c ? c->logits : nullptr; }
 extern "C" int qwen_cached_positions(const qwen_t* c) { return c ? c->cached : -1; }
 
-static int launch_decode(qwen_t* c) {
+static int count_launch(qwen_t* c) {
     if (++c->launches >= 0xFFFFFF00ull) {   // the 32-bit exchange tag is about to wrap: start over
         CU(cudaStreamSynchronize(c->stream));
         const int rc = reset_device_state(c);
         if (rc != QWEN_OK) return rc;
         c->launches = 1;
     }
+    return QWEN_OK;
+}
+
+static int enqueue_decode(qwen_t* c) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c->nsm);
     cfg.blockDim = dim3(kThreads);
@@ -373,6 +380,37 @@ static int launch_decode(qwen_t* c) {
     if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true>, c->params));
     else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false>, c->params));
     return QWEN_OK;
+}
+
+static int launch_decode(qwen_t* c) {
+    const int rc = count_launch(c);
+    return rc != QWEN_OK ? rc : enqueue_decode(c);
+}
+
+// qwen_decode_step's device work — StepIn in, one decode launch, StepOut out —
+// as a CUDA graph, captured once per handle and replayed (one API call per
+// token instead of three).  The launch tag lives in device memory, so the
+// same graph serves every step; changes to the kernel's by-value parameters
+// (vocabulary shard, tracing) drop it.  If capture or instantiation fails the
+// handle keeps the direct launches.
+static void drop_step_graph(qwen_t* c) {
+    if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+    c->step_exec = nullptr;
+}
+
+static void build_step_graph(qwen_t* c) {
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) { c->step_graph_off = true; return; }
+    bool ok = cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream) == cudaSuccess;
+    ok = ok && enqueue_decode(c) == QWEN_OK;
+    ok = ok && cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream) == cudaSuccess;
+    const bool ended = cudaStreamEndCapture(c->stream, &g) == cudaSuccess;
+    if (ok && ended && g && cudaGraphInstantiate(&c->step_exec, g, 0) != cudaSuccess) c->step_exec = nullptr;
+    if (g) cudaGraphDestroy(g);
+    if (!c->step_exec) {
+        c->step_graph_off = true;
+        cudaGetLastError();   // clear a capture error; the direct path reports its own
+    }
 }
 
 // After a synchronised launch sequence: surface a device-side wait timeout.
@@ -436,10 +474,16 @@ extern "C" int qwen_decode_step(qwen_t* c, int token, int pos, const qwen_sampli
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
     CU(cudaSetDevice(c->device));
+    if (!c->step_exec && !c->step_graph_off && !c->params.trace) build_step_graph(c);
     fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, kFlagWriteLogits);
-    CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
-    if ((rc = launch_decode(c)) != QWEN_OK) return rc;
-    CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    if (c->step_exec && !c->params.trace) {
+        if ((rc = count_launch(c)) != QWEN_OK) return rc;
+        CU(cudaGraphLaunch(c->step_exec, c->stream));
+    } else {
+        CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+        if ((rc = launch_decode(c)) != QWEN_OK) return rc;
+        CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    }
     CU(cudaStreamSynchronize(c->stream));
     c->last_k = (!sp || sp->temperature == 0.0f || sp->top_k == 1) ? 1 : sp->top_k;
     if ((rc = check_step(c)) != QWEN_OK) return rc;
@@ -644,6 +688,7 @@ extern "C" int qwen_set_vocab_shard(qwen_t* c, int row_begin, int row_end) {
         return fail(QWEN_E_ARG, "bad vocabulary shard");
     c->params.lm_begin = row_begin;
     c->params.lm_end = row_end;
+    drop_step_graph(c);
     return QWEN_OK;
 }
 
@@ -689,6 +734,7 @@ extern "C" int qwen_trace_enable(qwen_t* c, int enable) {
         CU(cudaMemset(c->params.trace, 0, n * sizeof(unsigned long long)));
     }
     if (!enable && c->params.trace) { CU(cudaFree(c->params.trace)); c->params.trace = nullptr; }
+    drop_step_graph(c);
     return QWEN_OK;
 }
 
