@@ -285,8 +285,8 @@ PREFILL_LINEAR_FLOP = 2 * 440_401_920     # per prompt token: 2 x the 28 layers'
 
 
 def prefill_bench(qb, ck, n_prompt=2048, n_gen=32):
-    """2048 seeded prompt tokens through qwen_prefill (tensor-core passes for the
-    first 2047 positions, the decode kernel for the last), then 32 greedy
+    """2048 seeded prompt tokens through qwen_prefill (tensor-core passes over all
+    positions, the last one's logits from an LM-head GEMV), then 32 greedy
     tokens; prefill time is the wall time of the synchronous call after one
     warm-up call.  Algorithmic FLOPs: the projections (2 x 440,401,920 per
     token) plus causal attention (28 x 16 x 2 x S^2 x 128 for QK^T and P.V
@@ -308,7 +308,7 @@ def prefill_bench(qb, ck, n_prompt=2048, n_gen=32):
             "algorithmic_tflop": alg / 1e12, "achieved_tflops": alg / dt / 1e12,
             "executed_tensor_tflop": 3 * PREFILL_LINEAR_FLOP * n_prompt / 1e12,
             "path": "28 layers x (4 persistent tcgen05 GEMM launches over all prompt rows + causal attention on mma.m16n8k16), "
-                    "decode kernel for the last token",
+                    "last position's logits by fp32 RMSNorm + LM-head GEMV",
             "decode_after": {"tokens": n_gen, "tok_s": n_gen / (ms / 1e3)}}
 
 
