@@ -173,6 +173,34 @@ int qwen_sample_host(const float* logits, int n, const qwen_sampling_t* sp,
 int qwen_sample_candidates(const float* values, const int* ids, int n, const qwen_sampling_t* sp,
                            unsigned long long* rng_state, int* token_out);
 
+/* ---- batched decode (no reference counterpart) ---------------------------- */
+/* The reference keeps one sequence per model (its run state is batch-1,
+ * qwen_model.cuh:63-80).  These serve up to 128 sequences per step on one GPU,
+ * every weight read once per step for all of them: each step is one pass over
+ * B rows — the projections as tensor-core GEMMs over the B rows (activations
+ * in three bf16 parts, fp32-exact products), attention of each row over its own
+ * cache slot in fp32, the LM head as one GEMM, top-k per row on the device and
+ * the sampler's math on the host (the device sampler's, as in
+ * qwen_sample_candidates).  Same numerics as the batch-1 chain up to fp32
+ * summation order. */
+
+/* Allocates max_batch (1..128) KV cache slots, each holding SEQ_LEN positions
+ * (939 MiB per slot).  Once per handle (QWEN_E_STATE after). */
+int qwen_batch_init(qwen_t* ctx, int max_batch);
+
+/* Positions 0 .. n-1 of slot `slot` from `tokens` (the slot's previous
+ * contents are dropped); logits_host (may be NULL) receives the last
+ * position's logits. */
+int qwen_batch_prefill(qwen_t* ctx, int slot, const int* tokens, int n, float* logits_host);
+
+/* One step for slots 0 .. batch-1: row r feeds tokens[r] at position pos[r]
+ * (at most the slot's current length) and returns the sampled next[r];
+ * rng_states[r] is slot r's sampler state (may be NULL for greedy sampling:
+ * temperature 0 or top_k 1).  Sampling as qwen_decode_step serves it
+ * (1 <= top_k <= 64 unless greedy). */
+int qwen_batch_step(qwen_t* ctx, int batch, const int* tokens, const int* pos, const qwen_sampling_t* sp,
+                    unsigned long long* rng_states, int* next);
+
 /* ---- tokenizer (tokenizer.h, export.py) ---------------------------------- */
 
 typedef struct qwen_tokenizer qwen_tokenizer_t;

@@ -196,6 +196,12 @@ struct qwen_ctx {
     size_t xchg_words = 0;
     unsigned long long launches = 0;   // since the last reset (bounds the 32-bit sequence tag)
     cudaGraphExec_t step_exec = nullptr;   // qwen_decode_step's copy-in, launch, copy-out, replayed
+    // batched decode (qwen_batch_*): one KV cache per slot, allocated by qwen_batch_init
+    int b_max = 0;
+    uint16_t *bkc = nullptr, *bvc = nullptr;
+    int *b_tokens = nullptr, *b_pos = nullptr, *b_ci = nullptr;
+    float *b_logits = nullptr, *b_cv = nullptr;
+    std::vector<int> b_cached;
     bool step_graph_off = false;           // capture failed once: direct launches from then on
     float *cand_v = nullptr, *top_v = nullptr;
     int *cand_i = nullptr, *top_i = nullptr, *prompt = nullptr, *tokens = nullptr, *chunk_count = nullptr;
@@ -227,6 +233,8 @@ static void ctx_free(qwen_t* c) {
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
     for (void* p : host) if (p) cudaFreeHost(p);
     if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+    void* bdev[] = {c->bkc, c->bvc, c->b_tokens, c->b_pos, c->b_ci, c->b_logits, c->b_cv};
+    for (void* p : bdev) if (p) cudaFree(p);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -566,7 +574,16 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
 // Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
 // layer's projections as tcgen05 GEMMs over all rows, attention over the KV
 // cache; fills the cache, computes no logits.  Tokens are in c->prompt.
-static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr) {
+// What a pass reads and writes besides the handle's scratch buffers.
+struct PassIO {
+    const int* tokens;      // device; prompt mode: token of position p at tokens[p]; batch mode: row r's at tokens[r]
+    uint16_t* kc;           // K and V caches (layer 0) of the sequence (prompt mode) or of row 0 (batch mode)
+    uint16_t* vc;
+    const int* pos_rows;    // NULL: rows are positions pos0 + r of one sequence; else row r is one position of sequence r
+    size_t row_stride;      // batch mode: elements between consecutive rows' caches
+};
+
+static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, const PassIO* io = nullptr) {
     using namespace qb::pf;
     constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM, kLdQKV = Q_DIM + 2 * KV_DIM;
     if (!c->pf_x) {
@@ -581,17 +598,25 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr) 
     const DecodeParams& P = c->params;
     cudaStream_t st = c->stream;
     const int rows = (m + tc::kBM - 1) / tc::kBM * tc::kBM;
-    embed_kernel<<<rows, 256, 0, st>>>(P.embed, c->prompt + pos0, m, rows, c->pf_x);
+    const bool batch = io && io->pos_rows;
+    const int* tok = io ? (batch ? io->tokens : io->tokens + pos0) : c->prompt + pos0;
+    uint16_t* kc0 = io ? io->kc : c->kc;
+    uint16_t* vc0 = io ? io->vc : c->vc;
+    embed_kernel<<<rows, 256, 0, st>>>(P.embed, tok, m, rows, c->pf_x);
     int rc, sp_o = 1, sp_d = 1;   // K splits of the O and down GEMMs: partial sums side by side in pf_y
     for (int l = 0; l < N_LAYERS; l++) {
-        uint16_t* kc_l = c->kc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
-        uint16_t* vc_l = c->vc + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
+        uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
+        uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, sp_d, P.in_ln[l], c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, kLdQKV, rows, 3 * DIM, DIM,
                           true, st)) != QWEN_OK)
             return rc;
-        qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l);
-        attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
+        qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
+                                                  batch ? io->pos_rows : nullptr, batch ? io->row_stride : 0);
+        if (batch)
+            attention_rows_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, c->pf_o);
+        else
+            attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o)) !=
             QWEN_OK)
@@ -664,6 +689,114 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     if ((rc = gemm_check(c)) != QWEN_OK) return rc;
     if ((rc = check_step(c)) != QWEN_OK) return rc;
     c->cached = pos0 + n;
+    return QWEN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// batched decode: B sequences per step, each in its own KV cache slot
+// ---------------------------------------------------------------------------
+constexpr int kMaxBatch = 128;
+static size_t slot_elems() { return (size_t)N_LAYERS * kGroups * SEQ_LEN * HEAD_DIM; }
+
+extern "C" int qwen_batch_init(qwen_t* c, int max_batch) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (max_batch < 1 || max_batch > kMaxBatch) return fail(QWEN_E_ARG, "max_batch must be in [1, 128]");
+    if (c->b_max) return fail(QWEN_E_STATE, "batched decode already initialised on this handle");
+    CU(cudaSetDevice(c->device));
+    const size_t cache = (size_t)max_batch * slot_elems();
+    const int rows = (max_batch + 127) / 128 * 128;
+    if (cudaMalloc(&c->bkc, cache * sizeof(uint16_t)) != cudaSuccess || cudaMalloc(&c->bvc, cache * sizeof(uint16_t)) != cudaSuccess) {
+        cudaGetLastError();
+        if (c->bkc) cudaFree(c->bkc);
+        c->bkc = nullptr;
+        return fail(QWEN_E_CUDA, "cannot allocate " + std::to_string(max_batch) + " KV cache slots (" +
+                                     std::to_string(2 * cache * sizeof(uint16_t) >> 20) + " MiB)");
+    }
+    TRY(dalloc(&c->b_tokens, (size_t)max_batch));
+    TRY(dalloc(&c->b_pos, (size_t)max_batch));
+    TRY(dalloc(&c->b_logits, (size_t)rows * VOCAB_SIZE));
+    TRY(dalloc(&c->b_cv, (size_t)max_batch * kMaxCand));
+    TRY(dalloc(&c->b_ci, (size_t)max_batch * kMaxCand));
+    // positions past a slot's length are read (and weighted zero) by the prompt pass's tiles: keep them finite
+    CU(cudaMemsetAsync(c->bkc, 0, cache * sizeof(uint16_t), c->stream));
+    CU(cudaMemsetAsync(c->bvc, 0, cache * sizeof(uint16_t), c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    c->b_cached.assign(max_batch, 0);
+    c->b_max = max_batch;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_batch_prefill(qwen_t* c, int slot, const int* tokens, int n, float* logits_host) {
+    if (!c || !tokens) return fail(QWEN_E_ARG, "NULL argument");
+    if (!c->b_max) return fail(QWEN_E_STATE, "qwen_batch_init first");
+    if (slot < 0 || slot >= c->b_max) return fail(QWEN_E_ARG, "slot out of range");
+    if (n <= 0 || n > SEQ_LEN) return fail(QWEN_E_ARG, "prompt does not fit [0, SEQ_LEN)");
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= VOCAB_SIZE) return fail(QWEN_E_ARG, "prompt token out of range");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpyAsync(c->prompt, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    const PassIO io{c->prompt, c->bkc + (size_t)slot * slot_elems(), c->bvc + (size_t)slot * slot_elems(), nullptr, 0};
+    int rc, s = 0, m = 0, sp = 1;
+    for (; s < n; s += m) {
+        m = std::min(qb::pf::kMaxRows, n - s);
+        if ((rc = prefill_pass(c, s, m, &sp, &io)) != QWEN_OK) return rc;
+    }
+    qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, 2 * HIDDEN_DIM, sp, c->params.final_ln, m - 1, c->pf_xn);
+    qb::pf::lm_head_f32_kernel<<<c->nsm * 8, 256, 0, c->stream>>>(c->params.lm, c->pf_xn, 0, VOCAB_SIZE, c->logits);
+    CU(cudaGetLastError());
+    if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    if ((rc = gemm_check(c)) != QWEN_OK) { c->b_cached[slot] = 0; return rc; }
+    c->b_cached[slot] = n;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const int* pos, const qwen_sampling_t* sp,
+                               unsigned long long* rng_states, int* next) {
+    if (!c || !tokens || !pos || !next) return fail(QWEN_E_ARG, "NULL argument");
+    if (!c->b_max) return fail(QWEN_E_STATE, "qwen_batch_init first");
+    if (batch < 1 || batch > c->b_max) return fail(QWEN_E_ARG, "batch out of [1, max_batch]");
+    int rc = check_sampling(sp);
+    if (rc != QWEN_OK) return rc;
+    const bool greedy = !sp || sp->temperature == 0.0f || sp->top_k == 1;
+    if (!greedy && !rng_states) return fail(QWEN_E_ARG, "sampling needs rng_states");
+    for (int r = 0; r < batch; r++) {
+        if (tokens[r] < 0 || tokens[r] >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
+        if (pos[r] < 0 || pos[r] >= SEQ_LEN) return fail(QWEN_E_ARG, "pos out of range [0, SEQ_LEN)");
+        if (pos[r] > c->b_cached[r]) return fail(QWEN_E_STATE, "pos skips uncached positions of its slot");
+    }
+    const int K = greedy ? 1 : sp->top_k;
+    const int rows = (batch + 127) / 128 * 128;
+    constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM;
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpyAsync(c->b_tokens, tokens, (size_t)batch * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->b_pos, pos, (size_t)batch * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems()};
+    int sp_d = 1;
+    if ((rc = prefill_pass(c, 0, batch, &sp_d, &io)) != QWEN_OK) return rc;
+    // final RMSNorm of every row (split into three bf16 parts), the LM head as one GEMM, top-k per row
+    qb::pf::norm_split_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->pf_x, c->pf_y, kLdY, sp_d, c->params.final_ln, c->pf_as, kLdAs,
+                                                                       rows);
+    if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true, c->stream)) !=
+        QWEN_OK)
+        return rc;
+    qb::pf::row_topk_kernel<<<batch, 1024, 0, c->stream>>>(c->b_logits, VOCAB_SIZE, VOCAB_SIZE, K, c->b_cv, c->b_ci);
+    CU(cudaGetLastError());
+    std::vector<float> cv((size_t)batch * K);
+    std::vector<int> ci((size_t)batch * K);
+    CU(cudaMemcpyAsync(cv.data(), c->b_cv, cv.size() * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaMemcpyAsync(ci.data(), c->b_ci, ci.size() * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    if ((rc = gemm_check(c)) != QWEN_OK) {
+        std::fill(c->b_cached.begin(), c->b_cached.end(), 0);
+        return rc;
+    }
+    for (int r = 0; r < batch; r++) {
+        if (greedy) next[r] = ci[r];
+        else if ((rc = qwen_sample_candidates(&cv[(size_t)r * K], &ci[(size_t)r * K], K, sp, &rng_states[r], &next[r])) != QWEN_OK)
+            return rc;
+        c->b_cached[r] = pos[r] + 1;
+    }
     return QWEN_OK;
 }
 

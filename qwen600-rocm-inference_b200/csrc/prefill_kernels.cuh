@@ -118,13 +118,17 @@ __global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, uint1
 // heads, 16..23 k heads, 24..31 v heads; lane l holds dims 4l..4l+3.  QK-norm
 // (qwen_model.cuh:215-245) and NeoX RoPE (:327-364) as in the decode chain; k
 // and v go to the bf16 cache (rows < m only), q to Q (fp32).
+// Rows r < m are prompt positions pos0 + r of one sequence (pos_rows NULL), or
+// (batched decode) one position pos_rows[r] each of sequence r, whose cache
+// starts row_cache_stride elements after sequence r - 1's.
 __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int m, int rows, int pos0, const uint16_t* __restrict__ qn,
                                 const uint16_t* __restrict__ kn, const float* __restrict__ rope, float* __restrict__ Q,
-                                uint16_t* __restrict__ kc_l, uint16_t* __restrict__ vc_l) {
+                                uint16_t* __restrict__ kc_l, uint16_t* __restrict__ vc_l, const int* __restrict__ pos_rows,
+                                size_t row_cache_stride) {
     const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int r = w >> 5, slot = w & 31;
     if (r >= rows) return;
-    const int pos = min(pos0 + r, SEQ_LEN - 1);
+    const int pos = pos_rows ? (r < m ? min(max(pos_rows[r], 0), SEQ_LEN - 1) : 0) : min(pos0 + r, SEQ_LEN - 1);
     const int col = slot < 16 ? 128 * slot : (slot < 24 ? Q_DIM + 128 * (slot - 16) : Q_DIM + KV_DIM + 128 * (slot - 24));
     const float4 a = *(const float4*)(Y + (size_t)r * ld_y + col + 4 * lane);
     float x[4] = {a.x, a.y, a.z, a.w};
@@ -147,7 +151,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int m, in
         *(float4*)(Q + (size_t)r * Q_DIM + 128 * slot + 4 * lane) = make_float4(x[0], x[1], x[2], x[3]);
     } else if (r < m) {
         const int h = slot < 24 ? slot - 16 : slot - 24;
-        uint16_t* dst = (slot < 24 ? kc_l : vc_l) + ((size_t)h * SEQ_LEN + pos) * HEAD_DIM + 4 * lane;
+        uint16_t* dst = (slot < 24 ? kc_l : vc_l) + (pos_rows ? (size_t)r * row_cache_stride : 0) + ((size_t)h * SEQ_LEN + pos) * HEAD_DIM +
+                        4 * lane;
         *(uint2*)dst = make_uint2((uint32_t)f2bf(x[0]) | ((uint32_t)f2bf(x[1]) << 16), (uint32_t)f2bf(x[2]) | ((uint32_t)f2bf(x[3]) << 16));
     }
 }
@@ -215,6 +220,144 @@ __global__ void __launch_bounds__(256) lm_head_f32_kernel(const uint16_t* __rest
             logits[r] = s0;
             if (two) logits[r + 1] = s1;
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Batched decode: one query row per sequence.
+// ---------------------------------------------------------------------------
+// Row r (sequence r, its position pos_rows[r]; its cache already holds that
+// position) against keys 0 .. pos_rows[r] of its own cache, for the two q heads
+// of KV head hk = blockIdx.x % N_KV_HEADS: the decode chain's attention
+// (qwen_model.cuh:809-810, attention_gpu) in fp32 — q fp32, K and V bf16, scores / sqrt(d),
+// online softmax.  8 warps take keys 8 at a time (four lanes per key, 32 dims
+// each), one softmax step per warp and head per 8 keys; P.V with lane l holding
+// dims 4l .. 4l+3; the 8 warps are combined in shared memory.
+constexpr int kDecAttThreads = 256;
+__global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const float* __restrict__ Q, const int* __restrict__ pos_rows,
+                                                                        const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
+                                                                        size_t row_cache_stride, float* __restrict__ O) {
+    __shared__ float qs[2][HEAD_DIM];
+    __shared__ float wm[8][2], wl[8][2];
+    __shared__ __align__(16) float wacc[8][2][HEAD_DIM];
+    const int r = blockIdx.x / N_KV_HEADS, hk = blockIdx.x % N_KV_HEADS;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, kq = lane >> 2, qq = lane & 3;
+    const int npos = min(max(pos_rows[r], 0), SEQ_LEN - 1) + 1;
+    const float sqrt_hd = sqrtf((float)HEAD_DIM);
+    qs[tid >> 7][tid & 127] = Q[(size_t)r * Q_DIM + 128 * (2 * hk) + tid];
+    __syncthreads();
+    float qr[2][32];
+    #pragma unroll
+    for (int j = 0; j < 32; j++) { qr[0][j] = qs[0][32 * qq + j]; qr[1][j] = qs[1][32 * qq + j]; }
+    const size_t base = (size_t)r * row_cache_stride + (size_t)hk * SEQ_LEN * HEAD_DIM;
+    const uint16_t* kb = kc_l + base;
+    const uint16_t* vb = vc_l + base;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int k0 = 8 * warp; k0 < npos; k0 += 64) {
+        const int key = k0 + kq;
+        const bool valid = key < npos;
+        float s[2] = {0.f, 0.f};
+        if (valid) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)key * HEAD_DIM + 32 * qq);
+            #pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint4 w4 = kr[i];
+                const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+                #pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    #pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        s[h] = fmaf(bf_lo(w[e]), qr[h][8 * i + 2 * e], s[h]);
+                        s[h] = fmaf(bf_hi(w[e]), qr[h][8 * i + 2 * e + 1], s[h]);
+                    }
+                }
+            }
+        }
+        float p[2];
+        #pragma unroll
+        for (int h = 0; h < 2; h++) {
+            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
+            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+            s[h] = valid ? s[h] / sqrt_hd : -INFINITY;
+            float mx = fmaxf(s[h], __shfl_xor_sync(0xffffffffu, s[h], 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(m[h], mx);   // finite: key k0 is valid
+            const float sc = expf(m[h] - mn);
+            p[h] = valid ? expf(s[h] - mn) : 0.f;
+            float ps = p[h] + __shfl_xor_sync(0xffffffffu, p[h], 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l[h] = fmaf(l[h], sc, ps);
+            #pragma unroll
+            for (int e = 0; e < 4; e++) acc[h][e] *= sc;
+            m[h] = mn;
+        }
+        #pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float p0 = __shfl_sync(0xffffffffu, p[0], 4 * i), p1 = __shfl_sync(0xffffffffu, p[1], 4 * i);
+            if (k0 + i < npos) {
+                const uint2 vw = *reinterpret_cast<const uint2*>(vb + (size_t)(k0 + i) * HEAD_DIM + 4 * lane);
+                const float v[4] = {bf_lo(vw.x), bf_hi(vw.x), bf_lo(vw.y), bf_hi(vw.y)};
+                #pragma unroll
+                for (int e = 0; e < 4; e++) { acc[0][e] = fmaf(p0, v[e], acc[0][e]); acc[1][e] = fmaf(p1, v[e], acc[1][e]); }
+            }
+        }
+    }
+    if (lane == 0) { wm[warp][0] = m[0]; wm[warp][1] = m[1]; wl[warp][0] = l[0]; wl[warp][1] = l[1]; }
+    #pragma unroll
+    for (int h = 0; h < 2; h++) *(float4*)&wacc[warp][h][4 * lane] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    __syncthreads();
+    const int h = tid >> 7, d = tid & 127;
+    float M = -INFINITY;
+    #pragma unroll
+    for (int w = 0; w < 8; w++) M = fmaxf(M, wm[w][h]);
+    float L = 0.f, A = 0.f;
+    #pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const float sc = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+        L = fmaf(wl[w][h], sc, L);
+        A = fmaf(wacc[w][h][d], sc, A);
+    }
+    O[(size_t)r * Q_DIM + 128 * (2 * hk + h) + d] = A / L;
+}
+
+// Per row of fp32 logits (n columns, rows ld apart): the k largest values in
+// decreasing order with their column ids (ties to the smaller id), by k block
+// argmax passes; chosen entries are overwritten with -inf.  One block of 1024
+// threads per row.
+__global__ void __launch_bounds__(1024) row_topk_kernel(float* __restrict__ logits, int ld, int n, int k, float* __restrict__ out_v,
+                                                        int* __restrict__ out_i) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float* row = logits + (size_t)blockIdx.x * ld;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int kk = 0; kk < k; kk++) {
+        float v = -INFINITY;
+        int id = 0x7fffffff;
+        for (int j = tid; j < n; j += 1024) {
+            const float x = row[j];
+            if (x > v || (x == v && j < id)) { v = x; id = j; }
+        }
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, id, o);
+            if (v2 > v || (v2 == v && i2 < id)) { v = v2; id = i2; }
+        }
+        if (lane == 0) { sv[warp] = v; si[warp] = id; }
+        __syncthreads();
+        if (tid == 0) {
+            float bv = sv[0];
+            int bi = si[0];
+            for (int w = 1; w < 32; w++)
+                if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+            out_v[(size_t)blockIdx.x * k + kk] = bv;
+            out_i[(size_t)blockIdx.x * k + kk] = bi < n ? bi : 0;
+            if (bi < n) row[bi] = -INFINITY;
+        }
+        __syncthreads();
     }
 }
 

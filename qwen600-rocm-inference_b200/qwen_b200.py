@@ -69,6 +69,9 @@ _SIGS = {
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
     "qwen_set_prefill_mode": (_c.c_int, [_P, _c.c_int]),
+    "qwen_batch_init": (_c.c_int, [_P, _c.c_int]),
+    "qwen_batch_prefill": (_c.c_int, [_P, _c.c_int, _P, _c.c_int, _P]),
+    "qwen_batch_step": (_c.c_int, [_P, _c.c_int, _P, _P, _P, _P, _P]),
     "qwen_tokenizer_load": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
     "qwen_tokenizer_free": (None, [_P]),
     "qwen_tokenizer_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
@@ -261,6 +264,26 @@ class Engine:
         _check(self._lib.qwen_generate_timed(self._h, int(token), int(pos), int(n_steps), ctypes.byref(sampling), ctypes.byref(r),
                                              _ptr(out), ctypes.byref(ms)))
         return out.tolist(), r.value, ms.value
+
+    # ---- batched decode (qwen_batch_*) ----
+    def batch_init(self, max_batch):
+        _check(self._lib.qwen_batch_init(self._h, int(max_batch)))
+
+    def batch_prefill(self, slot, tokens, want_logits=False):
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        lg = np.zeros(VOCAB_SIZE, dtype=np.float32) if want_logits else None
+        _check(self._lib.qwen_batch_prefill(self._h, int(slot), _ptr(tk), tk.size, _ptr(lg) if want_logits else None))
+        return lg
+
+    def batch_step(self, tokens, positions, sampling=GREEDY, rng_states=None):
+        """One step for slots 0 .. len(tokens)-1; returns (next tokens, rng states)."""
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        ps = np.ascontiguousarray(positions, dtype=np.int32)
+        nx = np.zeros(tk.size, dtype=np.int32)
+        rs = None if rng_states is None else np.ascontiguousarray(rng_states, dtype=np.uint64)
+        _check(self._lib.qwen_batch_step(self._h, tk.size, _ptr(tk), _ptr(ps), ctypes.byref(sampling),
+                                         _ptr(rs) if rs is not None else None, _ptr(nx)))
+        return nx.tolist(), (rs.tolist() if rs is not None else None)
 
     def set_prefill_mode(self, gemm=True):
         """Long prompts on the tensor cores (True, default) or one decode launch per token."""
