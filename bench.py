@@ -281,6 +281,39 @@ def long_context(qb, ck, n_prompt=4096, n_gen=512):
             "prefill_tok_s": n_prompt / pre_s}
 
 
+def batched_decode(qb, ck, batches=(8, 32, 128), n_prompt=1024, n_steps=24, warmup=3):
+    """qwen_batch_step at 1K context: 128 slots prefilled with seeded 1024-token
+    prompts, then for each B greedy steps over slots 0..B-1 (every slot at its
+    own next position).  Wall time of the synchronous calls (inputs from host
+    memory, next tokens back to host memory every step) after `warmup` steps;
+    aggregate tok/s = B x steps / time."""
+    eng = qb.Engine(ck, 0)
+    out = []
+    try:
+        top = max(batches)
+        eng.batch_init(top)
+        pos = []
+        for slot in range(top):
+            prompt = np.random.default_rng(5000 + slot).integers(0, 151936, n_prompt).tolist()
+            eng.batch_prefill(slot, prompt)
+            pos.append(n_prompt)
+        for b in batches:
+            toks = [5] * b
+            for i in range(warmup + n_steps):
+                if i == warmup:
+                    t0 = time.perf_counter()
+                toks, _ = eng.batch_step(toks, pos[:b])
+                for r in range(b):
+                    pos[r] += 1
+            dt = time.perf_counter() - t0
+            out.append({"batch": b, "tok_s": b * n_steps / dt, "ms_per_step": dt / n_steps * 1e3,
+                        "context": [min(pos[:b]) - n_steps, max(pos[:b])]})
+    finally:
+        eng.close()
+    return {"unit": "tok/s (aggregate over the batch)", "sampling": "greedy", "prompt_tokens": n_prompt, "points": out,
+            "path": "qwen_batch_step: projections and LM head as tcgen05 GEMMs over the batch rows, fp32 attention per row"}
+
+
 PREFILL_LINEAR_FLOP = 2 * 440_401_920     # per prompt token: 2 x the 28 layers' projection weights (SURVEY §8(d))
 
 
@@ -427,6 +460,7 @@ def run_mine(args):
                                   "l2": "flushed (256 MB write) between timed launches"}
             line["long_context"] = long_context(qb, ck)
             line["prefill"] = prefill_bench(qb, ck)
+            line["batched_decode"] = batched_decode(qb, ck)
             import oracle_py as O
             threads = os.cpu_count() or 1
             rate, n, dt = cpu_oracle_rate(ck, O.FP32, 15.0, 400, threads)

@@ -21,6 +21,7 @@
 #include <cstring>
 #include <initializer_list>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/qwen_b200.h"
@@ -200,8 +201,10 @@ struct qwen_ctx {
     int b_max = 0;
     uint16_t *bkc = nullptr, *bvc = nullptr;
     int *b_tokens = nullptr, *b_pos = nullptr, *b_ci = nullptr;
-    float *b_logits = nullptr, *b_cv = nullptr;
+    float *b_logits = nullptr, *b_cv = nullptr, *b_part = nullptr;
     std::vector<int> b_cached;
+    std::unordered_map<int, cudaGraphExec_t> b_graphs;   // batch step per (batch, k), replayed
+    bool b_graph_off = false;
     bool step_graph_off = false;           // capture failed once: direct launches from then on
     float *cand_v = nullptr, *top_v = nullptr;
     int *cand_i = nullptr, *top_i = nullptr, *prompt = nullptr, *tokens = nullptr, *chunk_count = nullptr;
@@ -233,7 +236,8 @@ static void ctx_free(qwen_t* c) {
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
     for (void* p : host) if (p) cudaFreeHost(p);
     if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
-    void* bdev[] = {c->bkc, c->bvc, c->b_tokens, c->b_pos, c->b_ci, c->b_logits, c->b_cv};
+    for (auto& kv : c->b_graphs) cudaGraphExecDestroy(kv.second);
+    void* bdev[] = {c->bkc, c->bvc, c->b_tokens, c->b_pos, c->b_ci, c->b_logits, c->b_cv, c->b_part};
     for (void* p : bdev) if (p) cudaFree(p);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -574,6 +578,22 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
 // Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
 // layer's projections as tcgen05 GEMMs over all rows, attention over the KV
 // cache; fills the cache, computes no logits.  Tokens are in c->prompt.
+static int gemm_prepare(int dev);
+
+// The prompt pass's scratch (kMaxRows rows), allocated on first use.
+static int pf_alloc(qwen_t* c) {
+    using namespace qb::pf;
+    if (c->pf_x) return QWEN_OK;
+    TRY(dalloc(&c->pf_x, (size_t)kMaxRows * DIM));
+    TRY(dalloc(&c->pf_y, (size_t)kMaxRows * 2 * HIDDEN_DIM));
+    TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
+    TRY(dalloc(&c->pf_o, (size_t)kMaxRows * Q_DIM));
+    TRY(dalloc(&c->pf_as, (size_t)kMaxRows * 3 * HIDDEN_DIM));
+    TRY(dalloc(&c->pf_xn, (size_t)DIM));
+    CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
+    return gemm_prepare(c->device);
+}
+
 // What a pass reads and writes besides the handle's scratch buffers.
 struct PassIO {
     const int* tokens;      // device; prompt mode: token of position p at tokens[p]; batch mode: row r's at tokens[r]
@@ -581,20 +601,14 @@ struct PassIO {
     uint16_t* vc;
     const int* pos_rows;    // NULL: rows are positions pos0 + r of one sequence; else row r is one position of sequence r
     size_t row_stride;      // batch mode: elements between consecutive rows' caches
+    float* part;            // batch mode: attention partials, room for kMaxKeySplits ranges per (row, KV head)
 };
+constexpr int kMaxKeySplits = 16;
 
 static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, const PassIO* io = nullptr) {
     using namespace qb::pf;
     constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM, kLdQKV = Q_DIM + 2 * KV_DIM;
-    if (!c->pf_x) {
-        TRY(dalloc(&c->pf_x, (size_t)kMaxRows * DIM));
-        TRY(dalloc(&c->pf_y, (size_t)kMaxRows * kLdY));
-        TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
-        TRY(dalloc(&c->pf_o, (size_t)kMaxRows * Q_DIM));
-        TRY(dalloc(&c->pf_as, (size_t)kMaxRows * kLdAs));
-        TRY(dalloc(&c->pf_xn, (size_t)DIM));
-        CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
-    }
+    TRY(pf_alloc(c));
     const DecodeParams& P = c->params;
     cudaStream_t st = c->stream;
     const int rows = (m + tc::kBM - 1) / tc::kBM * tc::kBM;
@@ -604,28 +618,38 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     uint16_t* vc0 = io ? io->vc : c->vc;
     embed_kernel<<<rows, 256, 0, st>>>(P.embed, tok, m, rows, c->pf_x);
     int rc, sp_o = 1, sp_d = 1;   // K splits of the O and down GEMMs: partial sums side by side in pf_y
+    // with few rows pf_y also has room for split-K partials of the q|k|v and
+    // gate|up GEMMs (their row strides widened to hold up to 4 / 6 of them)
+    const size_t ycap = (size_t)kMaxRows * kLdY;
+    const int ld_qkv = kLdQKV * (int)std::max<size_t>(1, std::min<size_t>(4, ycap / ((size_t)rows * kLdQKV)));
+    const int ld_gu = kLdY * (int)std::max<size_t>(1, std::min<size_t>(6, ycap / ((size_t)rows * kLdY)));
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, sp_d, P.in_ln[l], c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, kLdQKV, rows, 3 * DIM, DIM,
-                          true, st)) != QWEN_OK)
+        int sp_q = 1, sp_gu = 1;
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, 3 * DIM, DIM,
+                          true, st, kLdQKV, &sp_q)) != QWEN_OK)
             return rc;
-        qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
+        qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, ld_qkv, sp_q, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
                                                   batch ? io->pos_rows : nullptr, batch ? io->row_stride : 0);
-        if (batch)
-            attention_rows_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, c->pf_o);
-        else
+        if (batch) {
+            // key ranges per (row, KV head): enough blocks for two per SM
+            const int S = std::max(1, std::min(kMaxKeySplits, (2 * c->nsm + m * N_KV_HEADS - 1) / (m * N_KV_HEADS)));
+            attention_rows_kernel<<<m * N_KV_HEADS * S, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, S, c->pf_o,
+                                                                                 io->part);
+            if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_o);
+        } else
             attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o)) !=
             QWEN_OK)
             return rc;
         norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, sp_o, P.post_ln[l], c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, kLdY, rows, 3 * DIM, DIM, true, st)) !=
-            QWEN_OK)
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, 3 * DIM, DIM, true, st,
+                          kLdY, &sp_gu)) != QWEN_OK)
             return rc;
-        swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, kLdY, c->pf_as, kLdAs, rows);
+        swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, kLdY, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
                           &sp_d)) != QWEN_OK)
             return rc;
@@ -717,10 +741,12 @@ extern "C" int qwen_batch_init(qwen_t* c, int max_batch) {
     TRY(dalloc(&c->b_logits, (size_t)rows * VOCAB_SIZE));
     TRY(dalloc(&c->b_cv, (size_t)max_batch * kMaxCand));
     TRY(dalloc(&c->b_ci, (size_t)max_batch * kMaxCand));
+    TRY(dalloc(&c->b_part, (size_t)max_batch * N_KV_HEADS * kMaxKeySplits * qb::pf::kPartFloats));
     // positions past a slot's length are read (and weighted zero) by the prompt pass's tiles: keep them finite
     CU(cudaMemsetAsync(c->bkc, 0, cache * sizeof(uint16_t), c->stream));
     CU(cudaMemsetAsync(c->bvc, 0, cache * sizeof(uint16_t), c->stream));
     CU(cudaStreamSynchronize(c->stream));
+    TRY(pf_alloc(c));
     c->b_cached.assign(max_batch, 0);
     c->b_max = max_batch;
     return QWEN_OK;
@@ -735,7 +761,7 @@ extern "C" int qwen_batch_prefill(qwen_t* c, int slot, const int* tokens, int n,
         if (tokens[i] < 0 || tokens[i] >= VOCAB_SIZE) return fail(QWEN_E_ARG, "prompt token out of range");
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(c->prompt, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
-    const PassIO io{c->prompt, c->bkc + (size_t)slot * slot_elems(), c->bvc + (size_t)slot * slot_elems(), nullptr, 0};
+    const PassIO io{c->prompt, c->bkc + (size_t)slot * slot_elems(), c->bvc + (size_t)slot * slot_elems(), nullptr, 0, nullptr};
     int rc, s = 0, m = 0, sp = 1;
     for (; s < n; s += m) {
         m = std::min(qb::pf::kMaxRows, n - s);
@@ -771,17 +797,38 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(c->b_tokens, tokens, (size_t)batch * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     CU(cudaMemcpyAsync(c->b_pos, pos, (size_t)batch * sizeof(int), cudaMemcpyHostToDevice, c->stream));
-    const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems()};
-    int sp_d = 1;
-    if ((rc = prefill_pass(c, 0, batch, &sp_d, &io)) != QWEN_OK) return rc;
-    // final RMSNorm of every row (split into three bf16 parts), the LM head as one GEMM, top-k per row
-    qb::pf::norm_split_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->pf_x, c->pf_y, kLdY, sp_d, c->params.final_ln, c->pf_as, kLdAs,
-                                                                       rows);
-    if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true, c->stream)) !=
-        QWEN_OK)
-        return rc;
-    qb::pf::row_topk_kernel<<<batch, 1024, 0, c->stream>>>(c->b_logits, VOCAB_SIZE, VOCAB_SIZE, K, c->b_cv, c->b_ci);
-    CU(cudaGetLastError());
+    // the step's device work: the pass over the batch rows, the final RMSNorm of
+    // every row (split into three bf16 parts), the LM head as one GEMM, top-k
+    // per row; captured once per (batch, k) as a CUDA graph and replayed
+    auto body = [&]() -> int {
+        const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems(), c->b_part};
+        int sp_d = 1, r2;
+        if ((r2 = prefill_pass(c, 0, batch, &sp_d, &io)) != QWEN_OK) return r2;
+        qb::pf::norm_split_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->pf_x, c->pf_y, kLdY, sp_d, c->params.final_ln, c->pf_as, kLdAs,
+                                                                           rows);
+        if ((r2 = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true,
+                          c->stream)) != QWEN_OK)
+            return r2;
+        qb::pf::row_topk_kernel<<<batch, 1024, 0, c->stream>>>(c->b_logits, VOCAB_SIZE, VOCAB_SIZE, K, c->b_cv, c->b_ci);
+        CU(cudaGetLastError());
+        return QWEN_OK;
+    };
+    const int key = (batch << 8) | K;
+    auto it = c->b_graphs.find(key);
+    if (it == c->b_graphs.end() && !c->b_graph_off) {
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ge = nullptr;
+        if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int brc = body();
+            const bool ended = cudaStreamEndCapture(c->stream, &g) == cudaSuccess;
+            if (brc == QWEN_OK && ended && g && cudaGraphInstantiate(&ge, g, 0) != cudaSuccess) ge = nullptr;
+            if (g) cudaGraphDestroy(g);
+        }
+        if (ge) it = c->b_graphs.emplace(key, ge).first;
+        else { c->b_graph_off = true; cudaGetLastError(); }
+    }
+    if (it != c->b_graphs.end()) CU(cudaGraphLaunch(it->second, c->stream));
+    else if ((rc = body()) != QWEN_OK) return rc;
     std::vector<float> cv((size_t)batch * K);
     std::vector<int> ci((size_t)batch * K);
     CU(cudaMemcpyAsync(cv.data(), c->b_cv, cv.size() * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
@@ -944,6 +991,38 @@ bool kmajor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 }
 
 uint32_t* g_gemm_err[64] = {nullptr};
+int g_nsm[64] = {0};
+
+// Tensor maps by (base, rows, cols, ld, box rows): the weights and the prompt
+// pass's buffers keep their addresses, so each map is encoded once (a pass
+// issues ~10 maps per layer; encoding them every call made short passes
+// host-bound).
+struct MapKey {
+    const void* base;
+    uint64_t rows, cols, ld;
+    uint32_t box;
+    bool operator==(const MapKey& o) const { return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && box == o.box; }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        size_t h = std::hash<const void*>()(k.base);
+        for (uint64_t v : {k.rows, k.cols, k.ld, (uint64_t)k.box}) h = h * 1000003u ^ std::hash<uint64_t>()(v);
+        return h;
+    }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+bool cached_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+    const MapKey key{base, rows, cols, ld, box_rows};
+    std::lock_guard<std::mutex> lock(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) { *m = it->second; return true; }
+    if (!kmajor_map(m, base, rows, cols, ld, box_rows)) return false;
+    if (g_maps.size() > 4096) g_maps.clear();   // bound the cache (freed buffers' keys never hit again)
+    g_maps.emplace(key, *m);
+    return true;
+}
 
 template <int BN, bool F32>
 int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
@@ -962,6 +1041,23 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
     return QWEN_OK;
 }
 }  // namespace
+
+// Device-side set-up of the GEMM on `dev` (its error word, the kernels'
+// shared-memory limits), so that later launches allocate and configure
+// nothing (they can then be captured into a CUDA graph).
+static int gemm_prepare(int dev) {
+    if (dev < 0 || dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
+    if (!g_gemm_err[dev]) {
+        CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
+        CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
+    }
+    if (!g_nsm[dev]) CU(cudaDeviceGetAttribute(&g_nsm[dev], cudaDevAttrMultiProcessorCount, dev));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<256>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<256>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
+    return QWEN_OK;
+}
 
 // C[M][N] (rows ldc apart) = A[M][K] (rows lda apart) . (B[N][Kb] repeated
 // K / Kb times along K)^T, where B is the segments stacked along N (each
@@ -986,10 +1082,11 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
         return fail(QWEN_E_ARG, "M must be a multiple of 128, N of 128, K of 64");
     if (align & 15) return fail(QWEN_E_ARG, "A, B and C must be 16-byte aligned");
     if (lda < K || ldb < Kb || ldc < N || lda % 8 || ldb % 8 || ldc % 8) return fail(QWEN_E_ARG, "bad leading dimension");
-    int dev = 0, nsm = 0;
+    int dev = 0;
     CU(cudaGetDevice(&dev));
     if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
-    CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    if (!g_nsm[dev]) CU(cudaDeviceGetAttribute(&g_nsm[dev], cudaDevAttrMultiProcessorCount, dev));
+    const int nsm = g_nsm[dev];
     if (!g_gemm_err[dev]) {
         CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
         CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
@@ -1004,10 +1101,10 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     const int bn = all256 && (splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;
     qb::tc::BMaps bm;
-    if (!kmajor_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     int s = 0, end = 0;
     for (const BSeg& sg : segs) {
-        if (!kmajor_map(&bm.map[s], sg.B, (uint64_t)sg.rows, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)bn))
+        if (!cached_map(&bm.map[s], sg.B, (uint64_t)sg.rows, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)bn))
             return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
         end += sg.rows / bn;
         bm.end[s++] = end;

@@ -103,12 +103,20 @@ __global__ void split_kernel(const float* __restrict__ src, int ld_src, int K, u
 }
 
 // h = silu(g) * u for the gate (Y columns 0..H) and up (H..2H) outputs, then split into As.
-__global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, uint16_t* __restrict__ As, int ld_as, int rows) {
+// Y: gate | up (n_add partial sums of both, part_stride columns apart, added in order)
+__global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, int n_add, int part_stride, uint16_t* __restrict__ As, int ld_as,
+                                    int rows) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int q = HIDDEN_DIM / 4;
     if (i >= (size_t)rows * q) return;
     const int r = (int)(i / q), c = (int)(i % q) * 4;
-    const float4 g = *(const float4*)(Y + (size_t)r * ld_y + c), u = *(const float4*)(Y + (size_t)r * ld_y + HIDDEN_DIM + c);
+    const float* yr = Y + (size_t)r * ld_y + c;
+    float4 g = *(const float4*)yr, u = *(const float4*)(yr + HIDDEN_DIM);
+    for (int sp = 1; sp < n_add; sp++) {
+        const float4 g2 = *(const float4*)(yr + (size_t)sp * part_stride), u2 = *(const float4*)(yr + (size_t)sp * part_stride + HIDDEN_DIM);
+        g.x += g2.x; g.y += g2.y; g.z += g2.z; g.w += g2.w;
+        u.x += u2.x; u.y += u2.y; u.z += u2.z; u.w += u2.w;
+    }
     const float4 h = make_float4((g.x / (1.0f + expf(-g.x))) * u.x, (g.y / (1.0f + expf(-g.y))) * u.y,
                                  (g.z / (1.0f + expf(-g.z))) * u.z, (g.w / (1.0f + expf(-g.w))) * u.w);
     put_split4(As + (size_t)r * ld_as, HIDDEN_DIM, c, h);
@@ -121,16 +129,23 @@ __global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, uint1
 // Rows r < m are prompt positions pos0 + r of one sequence (pos_rows NULL), or
 // (batched decode) one position pos_rows[r] each of sequence r, whose cache
 // starts row_cache_stride elements after sequence r - 1's.
-__global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int m, int rows, int pos0, const uint16_t* __restrict__ qn,
-                                const uint16_t* __restrict__ kn, const float* __restrict__ rope, float* __restrict__ Q,
-                                uint16_t* __restrict__ kc_l, uint16_t* __restrict__ vc_l, const int* __restrict__ pos_rows,
-                                size_t row_cache_stride) {
+// Y may hold n_add partial sums (a GEMM with split K) part_stride columns apart;
+// they are added in order.
+__global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int n_add, int part_stride, int m, int rows, int pos0,
+                                const uint16_t* __restrict__ qn, const uint16_t* __restrict__ kn, const float* __restrict__ rope,
+                                float* __restrict__ Q, uint16_t* __restrict__ kc_l, uint16_t* __restrict__ vc_l,
+                                const int* __restrict__ pos_rows, size_t row_cache_stride) {
     const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int r = w >> 5, slot = w & 31;
     if (r >= rows) return;
     const int pos = pos_rows ? (r < m ? min(max(pos_rows[r], 0), SEQ_LEN - 1) : 0) : min(pos0 + r, SEQ_LEN - 1);
     const int col = slot < 16 ? 128 * slot : (slot < 24 ? Q_DIM + 128 * (slot - 16) : Q_DIM + KV_DIM + 128 * (slot - 24));
-    const float4 a = *(const float4*)(Y + (size_t)r * ld_y + col + 4 * lane);
+    const float* yr = Y + (size_t)r * ld_y + col + 4 * lane;
+    float4 a = *(const float4*)yr;
+    for (int sp = 1; sp < n_add; sp++) {
+        const float4 b = *(const float4*)(yr + (size_t)sp * part_stride);
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
     float x[4] = {a.x, a.y, a.z, a.w};
     if (slot < 24) {
         const uint2 gn = *(const uint2*)((slot < 16 ? qn : kn) + 4 * lane);
@@ -228,21 +243,28 @@ __global__ void __launch_bounds__(256) lm_head_f32_kernel(const uint16_t* __rest
 // ---------------------------------------------------------------------------
 // Row r (sequence r, its position pos_rows[r]; its cache already holds that
 // position) against keys 0 .. pos_rows[r] of its own cache, for the two q heads
-// of KV head hk = blockIdx.x % N_KV_HEADS: the decode chain's attention
-// (qwen_model.cuh:809-810, attention_gpu) in fp32 — q fp32, K and V bf16, scores / sqrt(d),
-// online softmax.  8 warps take keys 8 at a time (four lanes per key, 32 dims
-// each), one softmax step per warp and head per 8 keys; P.V with lane l holding
-// dims 4l .. 4l+3; the 8 warps are combined in shared memory.
+// of KV head hk: the decode chain's attention (qwen_model.cuh:809-810,
+// attention_gpu) in fp32 — q fp32, K and V bf16, scores / sqrt(d), online
+// softmax.  Block b: row b / (N_KV_HEADS S), KV head (b / S) % N_KV_HEADS, key
+// split b % S of S (the keys cut into S contiguous ranges, so small batches
+// still fill the GPU).  8 warps take keys 8 at a time (four lanes per key, 32
+// dims each; the 8 keys' V rows are loaded with their K rows), one softmax
+// step per warp and head per 8 keys; P.V with lane l holding dims 4l .. 4l+3.
+// The warps are merged in shared memory; with S = 1 the result goes to O,
+// else (max, sum, accumulator) per head to part[b] for attention_combine_kernel.
 constexpr int kDecAttThreads = 256;
+constexpr int kPartFloats = 2 * (HEAD_DIM + 2);   // per block: per head 128 accumulators, max, sum
 __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const float* __restrict__ Q, const int* __restrict__ pos_rows,
                                                                         const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
-                                                                        size_t row_cache_stride, float* __restrict__ O) {
+                                                                        size_t row_cache_stride, int S, float* __restrict__ O,
+                                                                        float* __restrict__ part) {
     __shared__ float qs[2][HEAD_DIM];
     __shared__ float wm[8][2], wl[8][2];
     __shared__ __align__(16) float wacc[8][2][HEAD_DIM];
-    const int r = blockIdx.x / N_KV_HEADS, hk = blockIdx.x % N_KV_HEADS;
+    const int sp = blockIdx.x % S, hk = (blockIdx.x / S) % N_KV_HEADS, r = blockIdx.x / (S * N_KV_HEADS);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, kq = lane >> 2, qq = lane & 3;
     const int npos = min(max(pos_rows[r], 0), SEQ_LEN - 1) + 1;
+    const int per = (npos + S - 1) / S, kb0 = sp * per, kb1 = min(npos, kb0 + per);
     const float sqrt_hd = sqrtf((float)HEAD_DIM);
     qs[tid >> 7][tid & 127] = Q[(size_t)r * Q_DIM + 128 * (2 * hk) + tid];
     __syncthreads();
@@ -254,23 +276,26 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
     const uint16_t* vb = vc_l + base;
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    for (int k0 = 8 * warp; k0 < npos; k0 += 64) {
+    for (int k0 = kb0 + 8 * warp; k0 < kb1; k0 += 64) {
         const int key = k0 + kq;
-        const bool valid = key < npos;
+        const bool valid = key < kb1;
+        uint4 kw[4];
+        uint2 vw[8];
+        #pragma unroll
+        for (int i = 0; i < 4; i++) kw[i] = valid ? reinterpret_cast<const uint4*>(kb + (size_t)key * HEAD_DIM + 32 * qq)[i] : make_uint4(0, 0, 0, 0);
+        #pragma unroll
+        for (int i = 0; i < 8; i++)
+            vw[i] = k0 + i < kb1 ? *reinterpret_cast<const uint2*>(vb + (size_t)(k0 + i) * HEAD_DIM + 4 * lane) : make_uint2(0u, 0u);
         float s[2] = {0.f, 0.f};
-        if (valid) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)key * HEAD_DIM + 32 * qq);
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t w[4] = {kw[i].x, kw[i].y, kw[i].z, kw[i].w};
             #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint4 w4 = kr[i];
-                const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+            for (int e = 0; e < 4; e++) {
                 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        s[h] = fmaf(bf_lo(w[e]), qr[h][8 * i + 2 * e], s[h]);
-                        s[h] = fmaf(bf_hi(w[e]), qr[h][8 * i + 2 * e + 1], s[h]);
-                    }
+                for (int h = 0; h < 2; h++) {
+                    s[h] = fmaf(bf_lo(w[e]), qr[h][8 * i + 2 * e], s[h]);
+                    s[h] = fmaf(bf_hi(w[e]), qr[h][8 * i + 2 * e + 1], s[h]);
                 }
             }
         }
@@ -297,12 +322,9 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
         #pragma unroll
         for (int i = 0; i < 8; i++) {
             const float p0 = __shfl_sync(0xffffffffu, p[0], 4 * i), p1 = __shfl_sync(0xffffffffu, p[1], 4 * i);
-            if (k0 + i < npos) {
-                const uint2 vw = *reinterpret_cast<const uint2*>(vb + (size_t)(k0 + i) * HEAD_DIM + 4 * lane);
-                const float v[4] = {bf_lo(vw.x), bf_hi(vw.x), bf_lo(vw.y), bf_hi(vw.y)};
-                #pragma unroll
-                for (int e = 0; e < 4; e++) { acc[0][e] = fmaf(p0, v[e], acc[0][e]); acc[1][e] = fmaf(p1, v[e], acc[1][e]); }
-            }
+            const float v[4] = {bf_lo(vw[i].x), bf_hi(vw[i].x), bf_lo(vw[i].y), bf_hi(vw[i].y)};
+            #pragma unroll
+            for (int e = 0; e < 4; e++) { acc[0][e] = fmaf(p0, v[e], acc[0][e]); acc[1][e] = fmaf(p1, v[e], acc[1][e]); }
         }
     }
     if (lane == 0) { wm[warp][0] = m[0]; wm[warp][1] = m[1]; wl[warp][0] = l[0]; wl[warp][1] = l[1]; }
@@ -319,6 +341,29 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
         const float sc = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
         L = fmaf(wl[w][h], sc, L);
         A = fmaf(wacc[w][h][d], sc, A);
+    }
+    if (S == 1) {
+        O[(size_t)r * Q_DIM + 128 * (2 * hk + h) + d] = A / L;
+    } else {
+        float* pb = part + (size_t)blockIdx.x * kPartFloats + h * (HEAD_DIM + 2);
+        pb[d] = A;
+        if (d == 0) { pb[HEAD_DIM] = M; pb[HEAD_DIM + 1] = L; }
+    }
+}
+
+// Merges the S key ranges of attention_rows_kernel: block b = (row, KV head),
+// thread (h, d) -> O.  An empty range (max -inf) contributes nothing.
+__global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ O) {
+    const int r = blockIdx.x / N_KV_HEADS, hk = blockIdx.x % N_KV_HEADS, h = threadIdx.x >> 7, d = threadIdx.x & 127;
+    const float* pb = part + (size_t)blockIdx.x * S * kPartFloats + h * (HEAD_DIM + 2);
+    float M = -INFINITY;
+    for (int i = 0; i < S; i++) M = fmaxf(M, pb[(size_t)i * kPartFloats + HEAD_DIM]);
+    float L = 0.f, A = 0.f;
+    for (int i = 0; i < S; i++) {
+        const float mi = pb[(size_t)i * kPartFloats + HEAD_DIM];
+        const float sc = mi == -INFINITY ? 0.f : expf(mi - M);
+        L = fmaf(pb[(size_t)i * kPartFloats + HEAD_DIM + 1], sc, L);
+        A = fmaf(pb[(size_t)i * kPartFloats + d], sc, A);
     }
     O[(size_t)r * Q_DIM + 128 * (2 * hk + h) + d] = A / L;
 }
