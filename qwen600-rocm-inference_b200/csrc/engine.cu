@@ -605,7 +605,10 @@ struct PassIO {
 };
 constexpr int kMaxKeySplits = 16;
 
-static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, const PassIO* io = nullptr) {
+// *down_splits / *down_ld: how the last down projection left its output in
+// pf_y (partial sums DIM columns apart, rows down_ld apart) for the caller's
+// final residual add.
+static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, const PassIO* io = nullptr, int* down_ld = nullptr) {
     using namespace qb::pf;
     constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM, kLdQKV = Q_DIM + 2 * KV_DIM;
     TRY(pf_alloc(c));
@@ -621,12 +624,13 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     // with few rows pf_y also has room for split-K partials of the q|k|v and
     // gate|up GEMMs (their row strides widened to hold up to 4 / 6 of them)
     const size_t ycap = (size_t)kMaxRows * kLdY;
-    const int ld_qkv = kLdQKV * (int)std::max<size_t>(1, std::min<size_t>(4, ycap / ((size_t)rows * kLdQKV)));
+    const int ld_qkv = kLdQKV * (int)std::max<size_t>(1, std::min<size_t>(8, ycap / ((size_t)rows * kLdQKV)));
     const int ld_gu = kLdY * (int)std::max<size_t>(1, std::min<size_t>(6, ycap / ((size_t)rows * kLdY)));
+    const int ld_od = std::max(kLdY, DIM * (int)std::min<size_t>(24, ycap / ((size_t)rows * DIM)));   // O and down partials
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
-        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, kLdY, sp_d, P.in_ln[l], c->pf_as, kLdAs, rows);
+        norm_split_kernel<<<rows, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, rows);
         int sp_q = 1, sp_gu = 1;
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, 3 * DIM, DIM,
                           true, st, kLdQKV, &sp_q)) != QWEN_OK)
@@ -642,20 +646,21 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         } else
             attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
         split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, kLdY, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o)) !=
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o)) !=
             QWEN_OK)
             return rc;
-        norm_split_kernel<<<(rows + 7) / 8, 256, 0, st>>>(c->pf_x, c->pf_y, kLdY, sp_o, P.post_ln[l], c->pf_as, kLdAs, rows);
+        norm_split_kernel<<<rows, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, rows);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, 3 * DIM, DIM, true, st,
                           kLdY, &sp_gu)) != QWEN_OK)
             return rc;
         swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, kLdY, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
                           &sp_d)) != QWEN_OK)
             return rc;
     }
     CU(cudaGetLastError());
     if (down_splits) *down_splits = sp_d;
+    if (down_ld) *down_ld = ld_od;
     return QWEN_OK;
 }
 
@@ -676,13 +681,13 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
     if (n - 1 >= kGemmPrefillMin && c->gemm_prefill && full_vocab) {
         // every position in tensor-core passes; the logits of the last one from
         // its final residual: RMSNorm + an fp32-input LM-head GEMV
-        int s = 0, m = 0, sp = 1;
+        int s = 0, m = 0, sp = 1, ld = 0;
         for (; s < n; s += m) {
             m = std::min(qb::pf::kMaxRows, n - s);
-            if ((rc = prefill_pass(c, pos0 + s, m, &sp)) != QWEN_OK) return rc;
+            if ((rc = prefill_pass(c, pos0 + s, m, &sp, nullptr, &ld)) != QWEN_OK) return rc;
         }
         const int last_row = m - 1;
-        qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, 2 * HIDDEN_DIM, sp, c->params.final_ln, last_row, c->pf_xn);
+        qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld, sp, c->params.final_ln, last_row, c->pf_xn);
         qb::pf::lm_head_f32_kernel<<<c->nsm * 8, 256, 0, c->stream>>>(c->params.lm, c->pf_xn, 0, VOCAB_SIZE, c->logits);
         CU(cudaGetLastError());
         if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
@@ -762,12 +767,12 @@ extern "C" int qwen_batch_prefill(qwen_t* c, int slot, const int* tokens, int n,
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(c->prompt, tokens, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     const PassIO io{c->prompt, c->bkc + (size_t)slot * slot_elems(), c->bvc + (size_t)slot * slot_elems(), nullptr, 0, nullptr};
-    int rc, s = 0, m = 0, sp = 1;
+    int rc, s = 0, m = 0, sp = 1, ld = 0;
     for (; s < n; s += m) {
         m = std::min(qb::pf::kMaxRows, n - s);
-        if ((rc = prefill_pass(c, s, m, &sp, &io)) != QWEN_OK) return rc;
+        if ((rc = prefill_pass(c, s, m, &sp, &io, &ld)) != QWEN_OK) return rc;
     }
-    qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, 2 * HIDDEN_DIM, sp, c->params.final_ln, m - 1, c->pf_xn);
+    qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld, sp, c->params.final_ln, m - 1, c->pf_xn);
     qb::pf::lm_head_f32_kernel<<<c->nsm * 8, 256, 0, c->stream>>>(c->params.lm, c->pf_xn, 0, VOCAB_SIZE, c->logits);
     CU(cudaGetLastError());
     if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
@@ -793,7 +798,7 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
     }
     const int K = greedy ? 1 : sp->top_k;
     const int rows = (batch + 127) / 128 * 128;
-    constexpr int kLdAs = 3 * HIDDEN_DIM, kLdY = 2 * HIDDEN_DIM;
+    constexpr int kLdAs = 3 * HIDDEN_DIM;
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(c->b_tokens, tokens, (size_t)batch * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     CU(cudaMemcpyAsync(c->b_pos, pos, (size_t)batch * sizeof(int), cudaMemcpyHostToDevice, c->stream));
@@ -802,10 +807,9 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
     // per row; captured once per (batch, k) as a CUDA graph and replayed
     auto body = [&]() -> int {
         const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems(), c->b_part};
-        int sp_d = 1, r2;
-        if ((r2 = prefill_pass(c, 0, batch, &sp_d, &io)) != QWEN_OK) return r2;
-        qb::pf::norm_split_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->pf_x, c->pf_y, kLdY, sp_d, c->params.final_ln, c->pf_as, kLdAs,
-                                                                           rows);
+        int sp_d = 1, ld_d = 0, r2;
+        if ((r2 = prefill_pass(c, 0, batch, &sp_d, &io, &ld_d)) != QWEN_OK) return r2;
+        qb::pf::norm_split_kernel<<<rows, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld_d, sp_d, c->params.final_ln, c->pf_as, kLdAs, rows);
         if ((r2 = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true,
                           c->stream)) != QWEN_OK)
             return r2;
@@ -1064,8 +1068,10 @@ static int gemm_prepare(int dev) {
 // [rows][Kb], rows ldb apart; at most three) and N their total rows.  One
 // persistent launch; 128 x 256 tiles when they fill every SM, else 128 x 128.
 // With split_cols > 0 the caller accepts K split s ways when 128 x 256 tiles
-// would leave SMs idle: partial sum i lands at columns i * split_cols + [0, N)
-// (within ldc) and *splits_used = s, for the caller to add in order.
+// would leave SMs idle (s the largest divisor of the K steps that keeps the
+// work items within the SM count and the partials within ldc): partial sum i
+// lands at columns i * split_cols + [0, N) and *splits_used = s, for the
+// caller to add in order.
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
                    cudaStream_t st, int split_cols, int* splits_used) {
     if (!A || !C || segs.size() < 1 || segs.size() > 3) return fail(QWEN_E_ARG, "NULL argument or bad segment count");
@@ -1094,9 +1100,8 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     const int tiles256 = (N / 256) * (M / qb::tc::kBM);
     int splits = 1;
     if (split_cols >= N && all256 && 2 * tiles256 <= nsm)
-        while (splits < 6 && (splits + 1) * tiles256 <= nsm && (K / qb::tc::kBK) % (splits + 1) == 0 &&
-               splits * split_cols + N <= ldc)
-            splits++;
+        for (int s = 2; s * tiles256 <= nsm && (s - 1) * split_cols + N <= ldc; s++)
+            if ((K / qb::tc::kBK) % s == 0) splits = s;   // the largest that divides the K steps
     if (splits_used) *splits_used = splits;
     const int bn = all256 && (splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;

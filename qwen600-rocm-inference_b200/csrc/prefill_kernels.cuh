@@ -54,43 +54,38 @@ __global__ void embed_kernel(const uint16_t* __restrict__ embed, const int* __re
     *(float4*)(X + (size_t)r * DIM + 4 * t) = v;
 }
 
-// One warp per row: X[r] += add[r] (if add), then RMSNorm with `gain` (the
-// decode chain's formula: (x * (1 / sqrt(mean(x^2) + eps))) * g) into As.
-// `add` may hold n_add partial sums side by side (columns s * DIM ..): a GEMM
-// whose K was split; they are added in order s = 0, 1, ... and then to X.
-__global__ void norm_split_kernel(float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
-                                  const uint16_t* __restrict__ gain, uint16_t* __restrict__ As, int ld_as, int rows) {
-    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+// One block (256 threads, 4 columns each) per row: X[r] += add[r] (if add),
+// then RMSNorm with `gain` (the decode chain's formula: (x * (1 / sqrt(mean(x^2)
+// + eps))) * g) into As.  `add` may hold n_add partial sums side by side
+// (columns s * DIM ..): a GEMM whose K was split; they are added in order
+// s = 0, 1, ... and then to X.
+__global__ void __launch_bounds__(256) norm_split_kernel(float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
+                                                         const uint16_t* __restrict__ gain, uint16_t* __restrict__ As, int ld_as, int rows) {
+    __shared__ float part[8];
+    const int r = blockIdx.x, t = threadIdx.x, c = 4 * t;
     if (r >= rows) return;
     float* x = X + (size_t)r * DIM;
-    float4 v[8];
-    float ss = 0.f;
-    #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int c = 128 * i + 4 * lane;
-        v[i] = *(const float4*)(x + c);
-        if (add) {
-            const float* ar = add + (size_t)r * ld_add + c;
-            float4 a = *(const float4*)ar;
-            for (int sp = 1; sp < n_add; sp++) {
-                const float4 b = *(const float4*)(ar + sp * DIM);
-                a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-            }
-            v[i].x += a.x; v[i].y += a.y; v[i].z += a.z; v[i].w += a.w;
-            *(float4*)(x + c) = v[i];
+    float4 v = *(const float4*)(x + c);
+    if (add) {
+        const float* ar = add + (size_t)r * ld_add + c;
+        float4 a = *(const float4*)ar;
+        for (int sp = 1; sp < n_add; sp++) {
+            const float4 b = *(const float4*)(ar + (size_t)sp * DIM);
+            a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
         }
-        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
+        *(float4*)(x + c) = v;
     }
-    ss = warp_sum(ss);
-    const float rs = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
-    uint16_t* a_row = As + (size_t)r * ld_as;
+    float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    if ((t & 31) == 0) part[t >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
     #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int c = 128 * i + 4 * lane;
-        const uint2 g = *(const uint2*)(gain + c);
-        const float4 y = make_float4((v[i].x * rs) * bf_lo(g.x), (v[i].y * rs) * bf_hi(g.x), (v[i].z * rs) * bf_lo(g.y), (v[i].w * rs) * bf_hi(g.y));
-        put_split4(a_row, DIM, c, y);
-    }
+    for (int w = 0; w < 8; w++) ss += part[w];
+    const float rs = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
+    const uint2 g = *(const uint2*)(gain + c);
+    const float4 y = make_float4((v.x * rs) * bf_lo(g.x), (v.y * rs) * bf_hi(g.x), (v.z * rs) * bf_lo(g.y), (v.w * rs) * bf_hi(g.y));
+    put_split4(As + (size_t)r * ld_as, DIM, c, y);
 }
 
 // As[r] = split(src[r][0..K)), one thread per 4 columns.
