@@ -13,6 +13,10 @@ for N >= 65
     ncu --set full --clock-control none -k regex:decode_kernel -s 2 -c 1 ...
 
 captures the second decode step: position N + 1, context N + 2.
+
+With --batch B it profiles batched decode instead: B slots, each prefilled
+with its own seeded N-token prompt (qwen_batch_prefill), then K greedy
+qwen_batch_step calls over the B slots.
 """
 import argparse
 import importlib.util
@@ -27,12 +31,26 @@ def main():
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=0)
     a = ap.parse_args()
     spec = importlib.util.spec_from_file_location("qwen_b200", os.path.join(HERE, "qwen_b200.py"))
     qb = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(qb)
     import numpy as np
     eng = qb.Engine(qb.default_checkpoint(0), a.device)
+    if a.batch:
+        eng.batch_init(a.batch)
+        for slot in range(a.batch):
+            eng.batch_prefill(slot, np.random.default_rng(1000 + slot).integers(0, qb.VOCAB_SIZE, a.prompt).tolist())
+        toks, pos = [5] * a.batch, [a.prompt] * a.batch
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            toks, _ = eng.batch_step(toks, pos)
+            pos = [p + 1 for p in pos]
+        dt = time.perf_counter() - t0
+        eng.close()
+        print(f"batch {a.batch} prompt {a.prompt} steps {a.steps}: {dt / max(a.steps, 1) * 1e3:.2f} ms per step (host wall time)")
+        return
     prompt = np.random.default_rng(1000).integers(0, qb.VOCAB_SIZE, a.prompt).tolist()
     eng.prefill(prompt, 0)
     tok = prompt[-1]
