@@ -573,7 +573,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
 static int gemm_check(qwen_t* c);
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
-                   cudaStream_t st, int split_cols = 0, int* splits_used = nullptr);
+                   cudaStream_t st, int split_cols = 0, int* splits_used = nullptr, int m_valid = 0);
 
 // Prompt positions [pos0, pos0 + m) in one pass (m <= pf::kMaxRows): every
 // layer's projections as tcgen05 GEMMs over all rows, attention over the KV
@@ -614,6 +614,10 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     TRY(pf_alloc(c));
     const DecodeParams& P = c->params;
     cudaStream_t st = c->stream;
+    // The GEMMs run on rows rounded up to 128; rows m .. rows-1 are padding: the
+    // elementwise kernels skip them, the GEMMs do not store them, and whatever
+    // they hold in the input buffers only reaches padding outputs (every output
+    // row depends on its own input row alone).
     const int rows = (m + tc::kBM - 1) / tc::kBM * tc::kBM;
     const bool batch = io && io->pos_rows;
     const int* tok = io ? (batch ? io->tokens : io->tokens + pos0) : c->prompt + pos0;
@@ -630,12 +634,12 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
-        norm_split_kernel<<<rows, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, rows);
+        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, m);
         int sp_q = 1, sp_gu = 1;
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, 3 * DIM, DIM,
-                          true, st, kLdQKV, &sp_q)) != QWEN_OK)
+                          true, st, kLdQKV, &sp_q, m)) != QWEN_OK)
             return rc;
-        qkv_post_kernel<<<rows * 4, 256, 0, st>>>(c->pf_y, ld_qkv, sp_q, kLdQKV, m, rows, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
+        qkv_post_kernel<<<m * 4, 256, 0, st>>>(c->pf_y, ld_qkv, sp_q, kLdQKV, m, m, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
                                                   batch ? io->pos_rows : nullptr, batch ? io->row_stride : 0);
         if (batch) {
             // key ranges per (row, KV head): enough blocks for two per SM
@@ -645,17 +649,17 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
             if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_o);
         } else
             attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
-        split_kernel<<<(rows * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, rows);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o)) !=
+        split_kernel<<<(m * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, m);
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o, m)) !=
             QWEN_OK)
             return rc;
-        norm_split_kernel<<<rows, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, rows);
+        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, 3 * DIM, DIM, true, st,
-                          kLdY, &sp_gu)) != QWEN_OK)
+                          kLdY, &sp_gu, m)) != QWEN_OK)
             return rc;
-        swiglu_split_kernel<<<(rows * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, rows);
+        swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m);
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
-                          &sp_d)) != QWEN_OK)
+                          &sp_d, m)) != QWEN_OK)
             return rc;
     }
     CU(cudaGetLastError());
@@ -809,9 +813,9 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
         const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems(), c->b_part};
         int sp_d = 1, ld_d = 0, r2;
         if ((r2 = prefill_pass(c, 0, batch, &sp_d, &io, &ld_d)) != QWEN_OK) return r2;
-        qb::pf::norm_split_kernel<<<rows, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld_d, sp_d, c->params.final_ln, c->pf_as, kLdAs, rows);
+        qb::pf::norm_split_kernel<<<batch, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld_d, sp_d, c->params.final_ln, c->pf_as, kLdAs, batch);
         if ((r2 = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true,
-                          c->stream)) != QWEN_OK)
+                          c->stream, 0, nullptr, batch)) != QWEN_OK)
             return r2;
         qb::pf::row_topk_kernel<<<batch, 1024, 0, c->stream>>>(c->b_logits, VOCAB_SIZE, VOCAB_SIZE, K, c->b_cv, c->b_ci);
         CU(cudaGetLastError());
@@ -1030,7 +1034,7 @@ bool cached_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 
 template <int BN, bool F32>
 int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                int nsm, cudaStream_t st, uint32_t* err) {
+                int m_valid, int nsm, cudaStream_t st, uint32_t* err) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -1040,7 +1044,7 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
     }
     const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
     qb::tc::gemm_bf16_tc_persistent<BN, F32><<<std::min(items, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
-        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, err);
+        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err);
     CU(cudaGetLastError());
     return QWEN_OK;
 }
@@ -1067,13 +1071,14 @@ static int gemm_prepare(int dev) {
 // K / Kb times along K)^T, where B is the segments stacked along N (each
 // [rows][Kb], rows ldb apart; at most three) and N their total rows.  One
 // persistent launch; 128 x 256 tiles when they fill every SM, else 128 x 128.
-// With split_cols > 0 the caller accepts K split s ways when 128 x 256 tiles
+// Rows m_valid .. M-1 (when 0 < m_valid < M) are padding: their results are
+// not stored.  With split_cols > 0 the caller accepts K split s ways when 128 x 256 tiles
 // would leave SMs idle (s the largest divisor of the K steps that keeps the
 // work items within the SM count and the partials within ldc): partial sum i
 // lands at columns i * split_cols + [0, N) and *splits_used = s, for the
 // caller to add in order.
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
-                   cudaStream_t st, int split_cols, int* splits_used) {
+                   cudaStream_t st, int split_cols, int* splits_used, int m_valid) {
     if (!A || !C || segs.size() < 1 || segs.size() > 3) return fail(QWEN_E_ARG, "NULL argument or bad segment count");
     int N = 0;
     bool all256 = true;
@@ -1117,10 +1122,11 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     for (; s < 3; s++) { bm.map[s] = bm.map[0]; bm.end[s] = end; }
     const int kb_b = Kb / qb::tc::kBK;
     const int so = splits > 1 ? split_cols : 0;
-    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev])
-                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev]);
-    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev])
-                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, nsm, st, g_gemm_err[dev]);
+    const int mv = m_valid > 0 && m_valid < M ? m_valid : M;
+    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
+                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
+    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
+                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
 }
 
 // The GEMM kernel's error word for the handle's device (a bounded wait ran out

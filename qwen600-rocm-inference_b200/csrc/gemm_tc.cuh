@@ -132,6 +132,8 @@ __device__ __forceinline__ void store32(void* C, int ldc, int m, int n, const fl
 // K steps [s, s + 1) * K / (64 splits) and writing its partial sum at column
 // offset s * c_split_off of C (the caller adds the partials).
 //
+// Rows m_valid .. M-1 of C are not written (padding rows of a short pass).
+//
 // K a multiple of 64 * splits; ldc in elements.  B's K extent may be a divisor
 // kb_b * 64 of K: K step kb reads B columns (kb mod kb_b) * 64, so
 // A = [a_1 | a_2 | a_3] (each K/3 wide) against B gives sum_i a_i . B^T — the
@@ -151,7 +153,7 @@ struct Layout {
 template <int BN, bool kOutF32>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
-                        int kb_b, int m_blocks, int splits, int c_split_off, uint32_t* err) {
+                        int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err) {
     using L = Layout<BN>;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
     static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
@@ -234,12 +236,14 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
             if (!mbar_wait(&acc_full[b], use & 1u, 2 * kWaitNs)) atomicOr(err, 4u);
             tc_fence_after();
             const int t = w % ntiles;
-            const int n0 = (t % n_blocks) * BN + (w / ntiles) * c_split_off, m = (t / n_blocks) * kBM + 32 * q + lane;
-            #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                float v[32];
-                tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
-                store32<kOutF32>(C, ldc, m, n0 + c, v);
+            const int n0 = (t % n_blocks) * BN + (w / ntiles) * c_split_off, m_w = (t / n_blocks) * kBM + 32 * q, m = m_w + lane;
+            if (m_w < m_valid) {   // rows m_valid.. are padding: neither read back nor stored
+                #pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+                    if (m < m_valid) store32<kOutF32>(C, ldc, m, n0 + c, v);
+                }
             }
             tc_fence_before();
             __syncwarp();
