@@ -218,7 +218,7 @@ struct qwen_ctx {
     DecodeParams params{};
     // prompt pass on the tensor cores (allocated on first use)
     const uint16_t* wo_raw[N_LAYERS] = {};   // o_proj in the canonical block
-    float *pf_x = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_o = nullptr, *pf_xn = nullptr;
+    float *pf_x = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_xn = nullptr;
     uint16_t* pf_as = nullptr;
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
@@ -230,7 +230,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_o, c->pf_xn, c->pf_as, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -587,7 +587,6 @@ static int pf_alloc(qwen_t* c) {
     TRY(dalloc(&c->pf_x, (size_t)kMaxRows * DIM));
     TRY(dalloc(&c->pf_y, (size_t)kMaxRows * 2 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
-    TRY(dalloc(&c->pf_o, (size_t)kMaxRows * Q_DIM));
     TRY(dalloc(&c->pf_as, (size_t)kMaxRows * 3 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_xn, (size_t)DIM));
     CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
@@ -644,12 +643,13 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         if (batch) {
             // key ranges per (row, KV head): enough blocks for two per SM
             const int S = std::max(1, std::min(kMaxKeySplits, (2 * c->nsm + m * N_KV_HEADS - 1) / (m * N_KV_HEADS)));
-            attention_rows_kernel<<<m * N_KV_HEADS * S, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, S, c->pf_o,
-                                                                                 io->part);
-            if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_o);
-        } else
-            attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_o);
-        split_kernel<<<(m * (Q_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_o, Q_DIM, Q_DIM, c->pf_as, kLdAs, m);
+            attention_rows_kernel<<<m * N_KV_HEADS * S, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, S,
+                                                                                 c->pf_as, kLdAs, io->part);
+            if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_as, kLdAs);
+        } else {
+            attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_as,
+                                                                                                       kLdAs);
+        }
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o, m)) !=
             QWEN_OK)
             return rc;

@@ -9,8 +9,8 @@
 //   norm_split    X (+= the previous GEMM's output) -> RMSNorm -> As = [hi|mid|lo]
 //   GEMM          As . [Wq; Wk; Wv]^T -> Y (fp32)
 //   qkv_post      QK-norm + RoPE; q -> Q (fp32); k, v -> the bf16 KV cache
-//   attention     causal GQA over the cache on the tensor cores -> O (fp32)
-//   split         O -> As;  GEMM As . Wo^T -> Y
+//   attention     causal GQA over the cache on the tensor cores -> As (the
+//                 output split into three bf16 parts);  GEMM As . Wo^T -> Y
 //   norm_split    X += Y -> RMSNorm (post_attention_layernorm) -> As
 //   GEMM          As . Wg^T, As . Wu^T -> Y;  swiglu_split -> As
 //   GEMM          As . Wd^T -> Y   (added into X by the next layer's norm_split)
@@ -31,6 +31,36 @@ __device__ __forceinline__ void split3(float v, uint16_t& h, uint16_t& m, uint16
     const float r = v - bf2f(h);
     m = f2bf(r);
     l = f2bf(r - bf2f(m));
+}
+// bf16 pair (round to nearest even) of lo, hi: lo in bits 0-15
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+// (a, b) -> three bf16 pairs h + m + l = (a, b) to fp32 precision (each
+// subtraction is exact)
+__device__ __forceinline__ void split3x2(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
+    h = cvt_bf16x2(a, b);
+    const float ra = a - __uint_as_float(h << 16), rb = b - __uint_as_float(h & 0xffff0000u);
+    m = cvt_bf16x2(ra, rb);
+    l = cvt_bf16x2(ra - __uint_as_float(m << 16), rb - __uint_as_float(m & 0xffff0000u));
+}
+// The attention output as the O projection's A operand: value(s) at column col
+// of an As row whose three parts are Q_DIM columns apart.
+__device__ __forceinline__ void put_split2(uint16_t* as_row, int col, float a, float b) {
+    uint32_t h, m, l;
+    split3x2(a, b, h, m, l);
+    *(uint32_t*)(as_row + col) = h;
+    *(uint32_t*)(as_row + Q_DIM + col) = m;
+    *(uint32_t*)(as_row + 2 * Q_DIM + col) = l;
+}
+__device__ __forceinline__ void put_split1(uint16_t* as_row, int col, float v) {
+    uint16_t h, m, l;
+    split3(v, h, m, l);
+    as_row[col] = h;
+    as_row[Q_DIM + col] = m;
+    as_row[2 * Q_DIM + col] = l;
 }
 // v (4 consecutive columns c..c+3 of a K-wide row) -> the three part blocks of As row r
 __device__ __forceinline__ void put_split4(uint16_t* As_row, int K, int c, float4 v) {
@@ -88,16 +118,6 @@ __global__ void __launch_bounds__(256) norm_split_kernel(float* __restrict__ X, 
     put_split4(As + (size_t)r * ld_as, DIM, c, y);
 }
 
-// As[r] = split(src[r][0..K)), one thread per 4 columns.
-__global__ void split_kernel(const float* __restrict__ src, int ld_src, int K, uint16_t* __restrict__ As, int ld_as, int rows) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int q = K / 4;
-    if (i >= (size_t)rows * q) return;
-    const int r = (int)(i / q), c = (int)(i % q) * 4;
-    put_split4(As + (size_t)r * ld_as, K, c, *(const float4*)(src + (size_t)r * ld_src + c));
-}
-
-// h = silu(g) * u for the gate (Y columns 0..H) and up (H..2H) outputs, then split into As.
 // Y: gate | up (n_add partial sums of both, part_stride columns apart, added in order)
 __global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, int n_add, int part_stride, uint16_t* __restrict__ As, int ld_as,
                                     int rows) {
@@ -245,14 +265,15 @@ __global__ void __launch_bounds__(256) lm_head_f32_kernel(const uint16_t* __rest
 // still fill the GPU).  8 warps take keys 8 at a time (four lanes per key, 32
 // dims each; the 8 keys' V rows are loaded with their K rows), one softmax
 // step per warp and head per 8 keys; P.V with lane l holding dims 4l .. 4l+3.
-// The warps are merged in shared memory; with S = 1 the result goes to O,
-// else (max, sum, accumulator) per head to part[b] for attention_combine_kernel.
+// The warps are merged in shared memory; with S = 1 the result goes to As (the
+// O projection's input, three bf16 parts), else (max, sum, accumulator) per
+// head to part[b] for attention_combine_kernel.
 constexpr int kDecAttThreads = 256;
 constexpr int kPartFloats = 2 * (HEAD_DIM + 2);   // per block: per head 128 accumulators, max, sum
 __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const float* __restrict__ Q, const int* __restrict__ pos_rows,
                                                                         const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
-                                                                        size_t row_cache_stride, int S, float* __restrict__ O,
-                                                                        float* __restrict__ part) {
+                                                                        size_t row_cache_stride, int S, uint16_t* __restrict__ As,
+                                                                        int ld_as, float* __restrict__ part) {
     __shared__ float qs[2][HEAD_DIM];
     __shared__ float wm[8][2], wl[8][2];
     __shared__ __align__(16) float wacc[8][2][HEAD_DIM];
@@ -338,7 +359,7 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
         A = fmaf(wacc[w][h][d], sc, A);
     }
     if (S == 1) {
-        O[(size_t)r * Q_DIM + 128 * (2 * hk + h) + d] = A / L;
+        put_split1(As + (size_t)r * ld_as, 128 * (2 * hk + h) + d, A / L);
     } else {
         float* pb = part + (size_t)blockIdx.x * kPartFloats + h * (HEAD_DIM + 2);
         pb[d] = A;
@@ -347,8 +368,9 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
 }
 
 // Merges the S key ranges of attention_rows_kernel: block b = (row, KV head),
-// thread (h, d) -> O.  An empty range (max -inf) contributes nothing.
-__global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const float* __restrict__ part, int S, float* __restrict__ O) {
+// thread (h, d) -> As.  An empty range (max -inf) contributes nothing.
+__global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const float* __restrict__ part, int S, uint16_t* __restrict__ As,
+                                                                           int ld_as) {
     const int r = blockIdx.x / N_KV_HEADS, hk = blockIdx.x % N_KV_HEADS, h = threadIdx.x >> 7, d = threadIdx.x & 127;
     const float* pb = part + (size_t)blockIdx.x * S * kPartFloats + h * (HEAD_DIM + 2);
     float M = -INFINITY;
@@ -360,7 +382,7 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const
         L = fmaf(pb[(size_t)i * kPartFloats + HEAD_DIM + 1], sc, L);
         A = fmaf(pb[(size_t)i * kPartFloats + d], sc, A);
     }
-    O[(size_t)r * Q_DIM + 128 * (2 * hk + h) + d] = A / L;
+    put_split1(As + (size_t)r * ld_as, 128 * (2 * hk + h) + d, A / L);
 }
 
 // Per row of fp32 logits (n columns, rows ld apart): the k largest values in
@@ -426,20 +448,6 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
 }
 __device__ __forceinline__ uint32_t pack_bf16(uint16_t a, uint16_t b) { return (uint32_t)a | ((uint32_t)b << 16); }
-// bf16 pair (round to nearest even) of lo, hi: lo in bits 0-15
-__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
-    uint32_t d;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-}
-// (a, b) -> three bf16 pairs h + m + l = (a, b) to fp32 precision (each
-// subtraction is exact)
-__device__ __forceinline__ void split3x2(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
-    h = cvt_bf16x2(a, b);
-    const float ra = a - __uint_as_float(h << 16), rb = b - __uint_as_float(h & 0xffff0000u);
-    m = cvt_bf16x2(ra, rb);
-    l = cvt_bf16x2(ra - __uint_as_float(m << 16), rb - __uint_as_float(m & 0xffff0000u));
-}
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
@@ -450,7 +458,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // grid: rows / 64 * N_KV_HEADS CTAs (1-D), kTcThreads threads, sizeof(AttTcSmem) bytes.
 __global__ void __launch_bounds__(kTcThreads, 1)
 attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
-                    float* __restrict__ O) {
+                    uint16_t* __restrict__ As, int ld_as) {
     extern __shared__ __align__(16) uint8_t att_tc_smem[];
     AttTcSmem& S = *reinterpret_cast<AttTcSmem*>(att_tc_smem);
     const int nqb = gridDim.x / N_KV_HEADS;
@@ -598,14 +606,14 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
         }
         __syncthreads();   // every warp is done with buffer t & 1 before tile t + 2 is copied into it
     }
-    // O rows g, g + 8 of the warp; dims 8n + 2qd, +1
+    // O rows g, g + 8 of the warp; dims 8n + 2qd, +1 — straight into As, split
     const float inv0 = 1.0f / lrow[0], inv1 = 1.0f / lrow[1];
-    float* o0 = O + (size_t)(q0 + 16 * wr + g) * Q_DIM + 128 * h + 2 * qd;
-    float* o1 = o0 + (size_t)8 * Q_DIM;
+    uint16_t* a0 = As + (size_t)(q0 + 16 * wr + g) * ld_as;
+    uint16_t* a1 = a0 + (size_t)8 * ld_as;
     #pragma unroll
     for (int n = 0; n < 16; n++) {
-        *(float2*)(o0 + 8 * n) = make_float2(o[n][0] * inv0, o[n][1] * inv0);
-        *(float2*)(o1 + 8 * n) = make_float2(o[n][2] * inv1, o[n][3] * inv1);
+        put_split2(a0, 128 * h + 8 * n + 2 * qd, o[n][0] * inv0, o[n][1] * inv0);
+        put_split2(a1, 128 * h + 8 * n + 2 * qd, o[n][2] * inv1, o[n][3] * inv1);
     }
 }
 
