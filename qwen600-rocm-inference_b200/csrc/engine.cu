@@ -163,6 +163,19 @@ __global__ void pack_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __rest
     }
 }
 
+// gate and up rows interleaved in blocks of 128 (block 2j: gate rows 128j ..,
+// block 2j+1: the same up rows), so one 128 x 256 GEMM tile holds both halves
+// of 128 hidden units and its epilogue can apply SwiGLU.
+__global__ void pack_gu_kernel(const uint16_t* __restrict__ wg, const uint16_t* __restrict__ wu, uint16_t* __restrict__ wgu) {
+    const size_t n = (size_t)2 * HIDDEN_DIM * DIM / 8;   // 16-byte units
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t row = i / (DIM / 8), col = i % (DIM / 8);
+        const size_t j = row / 256, k = row % 256;
+        const uint16_t* src = k < 128 ? wg + (128 * j + k) * DIM : wu + (128 * j + k - 128) * DIM;
+        reinterpret_cast<uint4*>(wgu)[i] = reinterpret_cast<const uint4*>(src)[col];
+    }
+}
+
 // RoPE cos/sin of every position, computed the way the reference writes it
 // (qwen_model.cuh:331-334): freq = 1/powf(theta, 2j/128), angle = pos*freq in
 // fp32.  The libm calls go through volatile pointers so the compiler cannot
@@ -220,6 +233,8 @@ struct qwen_ctx {
     const uint16_t* wo_raw[N_LAYERS] = {};   // o_proj in the canonical block
     float *pf_x = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_xn = nullptr;
     uint16_t* pf_as = nullptr;
+    uint16_t* pf_hs = nullptr;   // SwiGLU output in three bf16 parts (written by the fused gate|up GEMM)
+    uint16_t* wgu = nullptr;     // gate|up weights interleaved per 128 rows, all layers
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int last_k = 0;
@@ -230,7 +245,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -294,6 +309,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     TRY(dalloc(&c->wblock, total));
     TRY(upload_checkpoint(path, m, c->wblock, c->stream));
     TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * kGroups * DIM * kWoCols));
+    TRY(dalloc(&c->wgu, (size_t)N_LAYERS * 2 * HIDDEN_DIM * DIM));
     const size_t kv = (size_t)N_LAYERS * N_KV_HEADS * SEQ_LEN * HEAD_DIM;
     TRY(dalloc(&c->kc, kv));
     TRY(dalloc(&c->vc, kv));
@@ -341,6 +357,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         P.qn[l] = W(li.q_norm); P.kn[l] = W(li.k_norm);
         P.wg[l] = W(li.gate); P.wu[l] = W(li.up); P.wd[l] = W(li.down);
         pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * kGroups * DIM * kWoCols);
+        pack_gu_kernel<<<1024, 256, 0, c->stream>>>(W(li.gate), W(li.up), c->wgu + (size_t)l * 2 * HIDDEN_DIM * DIM);
         c->wo_raw[l] = W(li.o_proj);
     }
     if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
@@ -571,6 +588,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
 }
 
 static int gemm_check(qwen_t* c);
+static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st);
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
                    cudaStream_t st, int split_cols = 0, int* splits_used = nullptr, int m_valid = 0);
@@ -588,6 +606,7 @@ static int pf_alloc(qwen_t* c) {
     TRY(dalloc(&c->pf_y, (size_t)kMaxRows * 2 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_q, (size_t)kMaxRows * Q_DIM));
     TRY(dalloc(&c->pf_as, (size_t)kMaxRows * 3 * HIDDEN_DIM));
+    TRY(dalloc(&c->pf_hs, (size_t)kMaxRows * 3 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_xn, (size_t)DIM));
     CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
     return gemm_prepare(c->device);
@@ -654,11 +673,20 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
             QWEN_OK)
             return rc;
         norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, 3 * DIM, DIM, true, st,
-                          kLdY, &sp_gu, m)) != QWEN_OK)
-            return rc;
-        swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m);
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
+        // gate|up + SwiGLU: fused into the GEMM epilogue when 128 x 256 tiles fill the GPU
+        // without splitting K, else GEMM (split K when rows are few) + swiglu_split
+        const bool fused = (2 * HIDDEN_DIM / 256) * (rows / tc::kBM) >= c->nsm;
+        uint16_t* hs = fused ? c->pf_hs : c->pf_as;
+        if (fused) {
+            if ((rc = gemm_swiglu(c->pf_as, kLdAs, c->wgu + (size_t)l * 2 * HIDDEN_DIM * DIM, c->pf_hs, kLdAs, rows, m, st)) != QWEN_OK)
+                return rc;
+        } else {
+            if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, 3 * DIM, DIM, true,
+                              st, kLdY, &sp_gu, m)) != QWEN_OK)
+                return rc;
+            swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m);
+        }
+        if ((rc = gemm_tc(hs, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
                           &sp_d, m)) != QWEN_OK)
             return rc;
     }
@@ -1032,18 +1060,19 @@ bool cached_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
     return true;
 }
 
-template <int BN, bool F32>
+template <int BN, bool F32, int kEpi = 0>
 int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
                 int m_valid, int nsm, cudaStream_t st, uint32_t* err) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
     if (attr_dev != dev) {
-        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<BN>::kSmem));
+        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                qb::tc::Layout<BN>::kSmem));
         attr_dev = dev;
     }
     const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
-    qb::tc::gemm_bf16_tc_persistent<BN, F32><<<std::min(items, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
+    qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi><<<std::min(items, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
         ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err);
     CU(cudaGetLastError());
     return QWEN_OK;
@@ -1064,7 +1093,30 @@ static int gemm_prepare(int dev) {
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<256>::kSmem));
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            qb::tc::Layout<256>::kSmem));
     return QWEN_OK;
+}
+
+// The gate|up projection with SwiGLU in the epilogue: A [M][3 DIM] (three bf16
+// parts) against the interleaved gate|up weights wgu [2 HIDDEN_DIM][DIM];
+// writes h = silu(gate) * up as three bf16 parts into Hs (rows ld_hs apart,
+// parts HIDDEN_DIM apart).  Rows m_valid .. M-1 are not written.
+static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st) {
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
+    const int rc = gemm_prepare(dev);
+    if (rc != QWEN_OK) return rc;
+    CUtensorMap ma;
+    qb::tc::BMaps bm;
+    if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)(3 * DIM), (uint64_t)lda, qb::tc::kBM) ||
+        !cached_map(&bm.map[0], wgu, (uint64_t)(2 * HIDDEN_DIM), (uint64_t)DIM, (uint64_t)DIM, 256))
+        return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    bm.map[1] = bm.map[2] = bm.map[0];
+    bm.end[0] = bm.end[1] = bm.end[2] = 2 * HIDDEN_DIM / 256;
+    return gemm_launch<256, false, 1>(ma, bm, Hs, ld_hs, M, 3 * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev], st,
+                                      g_gemm_err[dev]);
 }
 
 // C[M][N] (rows ldc apart) = A[M][K] (rows lda apart) . (B[N][Kb] repeated

@@ -27,6 +27,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include "ptx.cuh"
+#include "../host/config.h"
 
 namespace qb {
 namespace tc {
@@ -150,7 +151,12 @@ struct Layout {
     static constexpr int kBarOff = kStages * kStageBytes;   // full[S], empty[S], acc_full[2], acc_empty[2], tmem slot
     static constexpr int kSmem = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
 };
-template <int BN, bool kOutF32>
+// kEpi = 1 (BN = 256, no K split): the tile holds the gate and up rows of the
+// same 128 hidden units (columns 0-127 gate, 128-255 up: the weights packed so,
+// n block j covering units 128 j ..); the epilogue writes h = silu(gate) * up as
+// three bf16 parts (C: bf16, rows ldc apart, parts HIDDEN_DIM columns apart),
+// the down projection's A operand.
+template <int BN, bool kOutF32, int kEpi = 0>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
                         int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err) {
@@ -237,7 +243,34 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
             tc_fence_after();
             const int t = w % ntiles;
             const int n0 = (t % n_blocks) * BN + (w / ntiles) * c_split_off, m_w = (t / n_blocks) * kBM + 32 * q, m = m_w + lane;
-            if (m_w < m_valid) {   // rows m_valid.. are padding: neither read back nor stored
+            if constexpr (kEpi == 1) {
+                static_assert(BN == 256, "the SwiGLU epilogue pairs 128 gate and 128 up columns");
+                if (m_w < m_valid) {
+                    const int u0 = (t % n_blocks) * 128;
+                    #pragma unroll 1
+                    for (int c = 0; c < 128; c += 32) {
+                        float g[32], u[32];
+                        tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, g);
+                        tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 + c), u);
+                        if (m < m_valid) {
+                            uint16_t* row = static_cast<uint16_t*>(C) + (size_t)m * ldc + u0 + c;
+                            #pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                uint32_t h[4], md[4], lo[4];
+                                #pragma unroll
+                                for (int j = 0; j < 4; j++) {
+                                    const float g0 = g[i + 2 * j], g1 = g[i + 2 * j + 1];
+                                    split3x2((g0 / (1.0f + expf(-g0))) * u[i + 2 * j], (g1 / (1.0f + expf(-g1))) * u[i + 2 * j + 1], h[j], md[j],
+                                             lo[j]);
+                                }
+                                *(uint4*)(row + i) = make_uint4(h[0], h[1], h[2], h[3]);
+                                *(uint4*)(row + HIDDEN_DIM + i) = make_uint4(md[0], md[1], md[2], md[3]);
+                                *(uint4*)(row + 2 * HIDDEN_DIM + i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            }
+                        }
+                    }
+                }
+            } else if (m_w < m_valid) {   // rows m_valid.. are padding: neither read back nor stored
                 #pragma unroll 1
                 for (int c = 0; c < BN; c += 32) {
                     float v[32];

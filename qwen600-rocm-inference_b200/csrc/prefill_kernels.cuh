@@ -32,20 +32,6 @@ __device__ __forceinline__ void split3(float v, uint16_t& h, uint16_t& m, uint16
     m = f2bf(r);
     l = f2bf(r - bf2f(m));
 }
-// bf16 pair (round to nearest even) of lo, hi: lo in bits 0-15
-__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
-    uint32_t d;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-}
-// (a, b) -> three bf16 pairs h + m + l = (a, b) to fp32 precision (each
-// subtraction is exact)
-__device__ __forceinline__ void split3x2(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
-    h = cvt_bf16x2(a, b);
-    const float ra = a - __uint_as_float(h << 16), rb = b - __uint_as_float(h & 0xffff0000u);
-    m = cvt_bf16x2(ra, rb);
-    l = cvt_bf16x2(ra - __uint_as_float(m << 16), rb - __uint_as_float(m & 0xffff0000u));
-}
 // The attention output as the O projection's A operand: value(s) at column col
 // of an As row whose three parts are Q_DIM columns apart.
 __device__ __forceinline__ void put_split2(uint16_t* as_row, int col, float a, float b) {

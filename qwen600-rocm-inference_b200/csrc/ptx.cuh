@@ -152,6 +152,20 @@ __device__ __forceinline__ float dot8(const uint4 w, const float* x, float acc) 
     acc = fmaf(bf_lo(w.w), x[6], acc); acc = fmaf(bf_hi(w.w), x[7], acc);
     return acc;
 }
+// bf16 pair (round to nearest even) of lo, hi: lo in bits 0-15
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+// (a, b) -> three bf16 pairs h + m + l = (a, b) to fp32 precision (each
+// subtraction is exact)
+__device__ __forceinline__ void split3x2(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
+    h = cvt_bf16x2(a, b);
+    const float ra = a - __uint_as_float(h << 16), rb = b - __uint_as_float(h & 0xffff0000u);
+    m = cvt_bf16x2(ra, rb);
+    l = cvt_bf16x2(ra - __uint_as_float(m << 16), rb - __uint_as_float(m & 0xffff0000u));
+}
 __device__ __forceinline__ float warp_sum(float v) {
     #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
