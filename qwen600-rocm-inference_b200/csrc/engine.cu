@@ -1084,6 +1084,8 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
 // nothing (they can then be captured into a CUDA graph).
 static int gemm_prepare(int dev) {
     if (dev < 0 || dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
+    static std::atomic<bool> done[64];
+    if (done[dev].load(std::memory_order_acquire)) return QWEN_OK;
     if (!g_gemm_err[dev]) {
         CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
         CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
@@ -1095,6 +1097,7 @@ static int gemm_prepare(int dev) {
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             qb::tc::Layout<256>::kSmem));
+    done[dev].store(true, std::memory_order_release);
     return QWEN_OK;
 }
 
