@@ -57,3 +57,21 @@ def test_prefill_two_passes_and_continuation(qb, checkpoint):
         assert int(np.argmax(la)) == int(np.argmax(lb))
     finally:
         a.close(); b.close()
+
+
+# Prompt lengths at the path boundaries: 65 (the smallest prompt of the tensor-core
+# path; 63 padding rows in the 128-row tiles), 129 (127 padding rows), 1281 (a pass
+# whose gate|up GEMM carries SwiGLU in its epilogue while 127 of its rows are
+# padding), 2049 (a full 2048-row pass plus a one-row pass).
+@pytest.mark.parametrize("n", [65, 129, 1281, 2049])
+def test_prefill_edge_lengths(qb, checkpoint, n):
+    la, lb, a, b, pos = _both(qb, checkpoint, [_prompt(n, 20 + n)])
+    try:
+        assert a.cached == n
+        assert np.abs(la - lb).max() <= 2e-2 and rel_rms(la, lb) <= 2.5e-3, (n, np.abs(la - lb).max(), rel_rms(la, lb))
+        assert int(np.argmax(la)) == int(np.argmax(lb))
+        ga, _ = a.generate(int(np.argmax(la)), pos, 4)
+        gb, _ = b.generate(int(np.argmax(lb)), pos, 4)
+        assert ga == gb
+    finally:
+        a.close(); b.close()
