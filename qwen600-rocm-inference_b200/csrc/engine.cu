@@ -764,6 +764,12 @@ extern "C" int qwen_batch_init(qwen_t* c, int max_batch) {
     if (max_batch < 1 || max_batch > kMaxBatch) return fail(QWEN_E_ARG, "max_batch must be in [1, 128]");
     if (c->b_max) return fail(QWEN_E_STATE, "batched decode already initialised on this handle");
     CU(cudaSetDevice(c->device));
+    // an earlier call that failed part-way may have left some buffers: start clean
+    for (void** p : {(void**)&c->bkc, (void**)&c->bvc, (void**)&c->b_tokens, (void**)&c->b_pos, (void**)&c->b_ci, (void**)&c->b_logits,
+                     (void**)&c->b_cv, (void**)&c->b_part}) {
+        if (*p) cudaFree(*p);
+        *p = nullptr;
+    }
     const size_t cache = (size_t)max_batch * slot_elems();
     const int rows = (max_batch + 127) / 128 * 128;
     if (cudaMalloc(&c->bkc, cache * sizeof(uint16_t)) != cudaSuccess || cudaMalloc(&c->bvc, cache * sizeof(uint16_t)) != cudaSuccess) {
