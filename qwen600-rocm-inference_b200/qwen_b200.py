@@ -143,12 +143,23 @@ def write_synthetic_checkpoint(path, seed=0):
 
 
 def default_checkpoint(seed=0, directory=None):
-    """Path of the seed-`seed` synthetic checkpoint, written on first use."""
+    """Path of the seed-`seed` synthetic checkpoint, written on first use.
+
+    Several processes may ask at once (one per GPU under torchrun): each writes
+    its own temporary file and renames it into place, so no process ever maps
+    a file that another is still writing (the rename is atomic; a mapping of
+    the replaced file stays valid)."""
     d = directory or os.environ.get("QWEN_B200_CACHE", os.path.join(REPO, ".cache"))
     os.makedirs(d, exist_ok=True)
     path = os.path.join(d, f"qwen3-0.6b-synthetic-seed{seed}.safetensors")
     if not os.path.exists(path):
-        write_synthetic_checkpoint(path, seed)
+        tmp = f"{path}.tmp.{os.getpid()}"
+        try:
+            write_synthetic_checkpoint(tmp, seed)
+            os.replace(tmp, path)
+        finally:
+            if os.path.exists(tmp):
+                os.remove(tmp)
     return path
 
 
