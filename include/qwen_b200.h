@@ -282,6 +282,14 @@ int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, v
  * main.cu:141-145). */
 int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream);
 
+/* The k best entries (1 <= k <= 64) of each of `rows` rows of fp32 logits (n
+ * columns, rows ld apart): values and column ids, k per row, in column order
+ * (not sorted); best = larger value, ties to the smaller column; NaN ranks
+ * below every number.  The device top-k of qwen_batch_step, whose candidates
+ * feed the sampler's top-k (sampler.h:54-79).  All pointers device; allocates
+ * scratch (4 x rows x ceil(n / 512) x k words) and synchronizes `stream`. */
+int qwen_row_topk(const float* logits, int rows, int n, int ld, int k, float* values, int* ids, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -215,6 +215,7 @@ struct qwen_ctx {
     uint16_t *bkc = nullptr, *bvc = nullptr;
     int *b_tokens = nullptr, *b_pos = nullptr, *b_ci = nullptr;
     float *b_logits = nullptr, *b_cv = nullptr, *b_part = nullptr;
+    uint32_t* b_tk = nullptr;              // top-k level scratch: two key and two id lists
     std::vector<int> b_cached;
     std::unordered_map<int, cudaGraphExec_t> b_graphs;   // batch step per (batch, k), replayed
     bool b_graph_off = false;
@@ -252,7 +253,7 @@ static void ctx_free(qwen_t* c) {
     for (void* p : host) if (p) cudaFreeHost(p);
     if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
     for (auto& kv : c->b_graphs) cudaGraphExecDestroy(kv.second);
-    void* bdev[] = {c->bkc, c->bvc, c->b_tokens, c->b_pos, c->b_ci, c->b_logits, c->b_cv, c->b_part};
+    void* bdev[] = {c->bkc, c->bvc, c->b_tokens, c->b_pos, c->b_ci, c->b_logits, c->b_cv, c->b_part, c->b_tk};
     for (void* p : bdev) if (p) cudaFree(p);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -759,6 +760,34 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
 constexpr int kMaxBatch = 128;
 static size_t slot_elems() { return (size_t)N_LAYERS * kGroups * SEQ_LEN * HEAD_DIM; }
 
+// Entries per row of one top-k level list: k survivors of each 512-entry group of the first level.
+static int topk_scratch_ld(int n, int k) { return (n + qb::pf::kTopkGroup - 1) / qb::pf::kTopkGroup * k; }
+
+// The k best of each of `rows` rows of fp32 logits (n columns, ld apart) into
+// v / i (k per row, in column order), by topk_level_kernel levels until one
+// group is left.  scratch: 4 x E words (two key lists, two id lists), E at
+// least rows x topk_scratch_ld(n, k).
+static cudaError_t launch_row_topk(const float* logits, int rows, int n, int ld, int k, uint32_t* scratch, size_t E, float* v, int* i,
+                                   cudaStream_t st) {
+    namespace pf = qb::pf;
+    const int lds = topk_scratch_ld(n, k);
+    uint32_t* key[2] = {scratch, scratch + E};
+    int* id[2] = {reinterpret_cast<int*>(scratch + 2 * E), reinterpret_cast<int*>(scratch + 3 * E)};
+    auto grid = [&](int m) {
+        const int groups = (m + pf::kTopkGroup - 1) / pf::kTopkGroup;
+        return dim3((unsigned)((groups + pf::kTopkWarps - 1) / pf::kTopkWarps), (unsigned)rows);
+    };
+    pf::topk_level_kernel<true><<<grid(n), 32 * pf::kTopkWarps, 0, st>>>(logits, nullptr, nullptr, ld, n, k, key[0], id[0], lds, v, i, n);
+    int m = n, cur = 0;
+    while (m > pf::kTopkGroup) {
+        m = (m + pf::kTopkGroup - 1) / pf::kTopkGroup * k;
+        pf::topk_level_kernel<false><<<grid(m), 32 * pf::kTopkWarps, 0, st>>>(nullptr, key[cur], id[cur], lds, m, k, key[cur ^ 1],
+                                                                                id[cur ^ 1], lds, v, i, n);
+        cur ^= 1;
+    }
+    return cudaGetLastError();
+}
+
 extern "C" int qwen_batch_init(qwen_t* c, int max_batch) {
     if (!c) return fail(QWEN_E_ARG, "NULL handle");
     if (max_batch < 1 || max_batch > kMaxBatch) return fail(QWEN_E_ARG, "max_batch must be in [1, 128]");
@@ -766,7 +795,7 @@ extern "C" int qwen_batch_init(qwen_t* c, int max_batch) {
     CU(cudaSetDevice(c->device));
     // an earlier call that failed part-way may have left some buffers: start clean
     for (void** p : {(void**)&c->bkc, (void**)&c->bvc, (void**)&c->b_tokens, (void**)&c->b_pos, (void**)&c->b_ci, (void**)&c->b_logits,
-                     (void**)&c->b_cv, (void**)&c->b_part}) {
+                     (void**)&c->b_cv, (void**)&c->b_part, (void**)&c->b_tk}) {
         if (*p) cudaFree(*p);
         *p = nullptr;
     }
@@ -784,6 +813,7 @@ extern "C" int qwen_batch_init(qwen_t* c, int max_batch) {
     TRY(dalloc(&c->b_logits, (size_t)rows * VOCAB_SIZE));
     TRY(dalloc(&c->b_cv, (size_t)max_batch * kMaxCand));
     TRY(dalloc(&c->b_ci, (size_t)max_batch * kMaxCand));
+    TRY(dalloc(&c->b_tk, 4 * (size_t)max_batch * topk_scratch_ld(VOCAB_SIZE, kMaxCand)));
     TRY(dalloc(&c->b_part, (size_t)max_batch * N_KV_HEADS * kMaxKeySplits * qb::pf::kPartFloats));
     // positions past a slot's length are read (and weighted zero) by the prompt pass's tiles: keep them finite
     CU(cudaMemsetAsync(c->bkc, 0, cache * sizeof(uint16_t), c->stream));
@@ -851,8 +881,8 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
         if ((r2 = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true,
                           c->stream, 0, nullptr, batch)) != QWEN_OK)
             return r2;
-        qb::pf::row_topk_kernel<<<batch, 1024, 0, c->stream>>>(c->b_logits, VOCAB_SIZE, VOCAB_SIZE, K, c->b_cv, c->b_ci);
-        CU(cudaGetLastError());
+        const size_t E = (size_t)c->b_max * topk_scratch_ld(VOCAB_SIZE, kMaxCand);
+        CU(launch_row_topk(c->b_logits, batch, VOCAB_SIZE, VOCAB_SIZE, K, c->b_tk, E, c->b_cv, c->b_ci, c->stream));
         return QWEN_OK;
     };
     const int key = (batch << 8) | K;
@@ -1206,6 +1236,20 @@ static int gemm_check(qwen_t* c) {
 
 extern "C" int qwen_gemm_bf16(const void* A, const void* B, void* C, int M, int N, int K, int c_fp32, void* stream) {
     return gemm_tc(A, K, {{B, N}}, K, C, N, M, K, K, c_fp32 != 0, (cudaStream_t)stream);
+}
+
+extern "C" int qwen_row_topk(const float* logits, int rows, int n, int ld, int k, float* values, int* ids, void* stream) {
+    if (!logits || !values || !ids) return fail(QWEN_E_ARG, "NULL argument");
+    if (rows < 1 || rows > 65535 || n < 1 || ld < n || k < 1 || k > kMaxCand) return fail(QWEN_E_ARG, "rows, n, ld or k out of range");
+    const size_t E = (size_t)rows * topk_scratch_ld(n, k);
+    uint32_t* scratch = nullptr;
+    CU(cudaMalloc(&scratch, 4 * E * sizeof(uint32_t)));
+    const cudaError_t e = launch_row_topk(logits, rows, n, ld, k, scratch, E, values, ids, (cudaStream_t)stream);
+    const cudaError_t e2 = cudaStreamSynchronize((cudaStream_t)stream);
+    cudaFree(scratch);
+    CU(e);
+    CU(e2);
+    return QWEN_OK;
 }
 
 // ---------------------------------------------------------------------------

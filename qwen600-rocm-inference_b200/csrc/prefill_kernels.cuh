@@ -371,41 +371,88 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const
     put_split1(As + (size_t)r * ld_as, 128 * (2 * hk + h) + d, A / L);
 }
 
-// Per row of fp32 logits (n columns, rows ld apart): the k largest values in
-// decreasing order with their column ids (ties to the smaller id), by k block
-// argmax passes; chosen entries are overwritten with -inf.  One block of 1024
-// threads per row.
-__global__ void __launch_bounds__(1024) row_topk_kernel(float* __restrict__ logits, int ld, int n, int k, float* __restrict__ out_v,
-                                                        int* __restrict__ out_i) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    float* row = logits + (size_t)blockIdx.x * ld;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int kk = 0; kk < k; kk++) {
-        float v = -INFINITY;
-        int id = 0x7fffffff;
-        for (int j = tid; j < n; j += 1024) {
-            const float x = row[j];
-            if (x > v || (x == v && j < id)) { v = x; id = j; }
-        }
+// Top-k of every row of fp32 logits, in levels: each warp takes a group of 512
+// consecutive entries of a row and keeps its k best (value descending, ties to
+// the smaller id: each entry's key is its value in an order-preserving uint32,
+// and the k-th best key is found by a radix select over the 32 key bits, one
+// warp-wide count per bit), writing them in entry order.  The next level runs
+// the same over the concatenated survivors until one group is left; because
+// every level keeps entry order and level one's entries are in id order, a
+// position in a survivor list orders ties exactly as the id does.  NaN ranks
+// below every number; -0 counts as +0.  k <= 64 (at most 512 / 8 per group).
+constexpr int kTopkGroup = 512;                 // entries per warp
+constexpr int kTopkPerLane = kTopkGroup / 32;
+constexpr int kTopkWarps = 8;                   // warps per block
+
+__device__ __forceinline__ uint32_t order_key(float x) {
+    if (x != x) return 0u;
+    if (x == 0.f) x = 0.f;
+    const uint32_t u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+    if (k == 0u) return -INFINITY;
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Level over `n` entries per row: logits (kFirst: fp32, ids = columns) or the
+// keys / ids of the previous level (rows in_ld apart).  Writes k survivors per
+// group to out_key / out_id (rows out_ld apart), or, when one group covers the
+// row (n <= 512), the k values and ids to fin_v / fin_i (rows k apart; an id
+// past the row, possible only for rows with fewer than k numbers, reads 0).
+template <bool kFirst>
+__global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float* __restrict__ logits, const uint32_t* __restrict__ in_key,
+                                                                     const int* __restrict__ in_id, int in_ld, int n, int k,
+                                                                     uint32_t* __restrict__ out_key, int* __restrict__ out_id, int out_ld,
+                                                                     float* __restrict__ fin_v, int* __restrict__ fin_i, int n_ids) {
+    const int lane = threadIdx.x & 31;
+    const int groups = (n + kTopkGroup - 1) / kTopkGroup;
+    const int g = blockIdx.x * kTopkWarps + (threadIdx.x >> 5);
+    if (g >= groups) return;
+    const int row = blockIdx.y;
+    const size_t rb = (size_t)row * in_ld;
+    const int base = g * kTopkGroup;
+    uint32_t key[kTopkPerLane];
+    #pragma unroll
+    for (int e = 0; e < kTopkPerLane; e++) {
+        const int j = base + e * 32 + lane;
+        key[e] = j < n ? (kFirst ? order_key(logits[rb + j]) : in_key[rb + j]) : 0u;
+    }
+    uint32_t T = 0u;
+    int need = k;
+    #pragma unroll 1
+    for (int bit = 31; bit >= 0; bit--) {
+        const uint32_t m = ~0u << bit, cand = T | (1u << bit);
+        int cnt = 0;
         #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-            const int i2 = __shfl_xor_sync(0xffffffffu, id, o);
-            if (v2 > v || (v2 == v && i2 < id)) { v = v2; id = i2; }
+        for (int e = 0; e < kTopkPerLane; e++) cnt += (key[e] & m) == cand;
+        cnt = __reduce_add_sync(0xffffffffu, cnt);
+        if (cnt >= need) T = cand;
+        else need -= cnt;
+    }
+    // T: the k-th best key of the group; take every key above it and the first `need` equal to it
+    const uint32_t lt = (1u << lane) - 1u;
+    const bool fin = groups == 1;
+    int taken = 0, eq_seen = 0;
+    #pragma unroll
+    for (int e = 0; e < kTopkPerLane; e++) {
+        const int j = base + e * 32 + lane;
+        const uint32_t beq = __ballot_sync(0xffffffffu, key[e] == T);
+        const bool sel = key[e] > T || (key[e] == T && eq_seen + __popc(beq & lt) < need);
+        eq_seen += __popc(beq);
+        const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
+        if (sel) {
+            const int slot = taken + __popc(bsel & lt);
+            const int id = j < n ? (kFirst ? j : in_id[rb + j]) : 0x7fffffff;
+            if (fin) {
+                fin_v[(size_t)row * k + slot] = key_value(key[e]);
+                fin_i[(size_t)row * k + slot] = id < n_ids ? id : 0;
+            } else {
+                out_key[(size_t)row * out_ld + (size_t)g * k + slot] = key[e];
+                out_id[(size_t)row * out_ld + (size_t)g * k + slot] = id;
+            }
         }
-        if (lane == 0) { sv[warp] = v; si[warp] = id; }
-        __syncthreads();
-        if (tid == 0) {
-            float bv = sv[0];
-            int bi = si[0];
-            for (int w = 1; w < 32; w++)
-                if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
-            out_v[(size_t)blockIdx.x * k + kk] = bv;
-            out_i[(size_t)blockIdx.x * k + kk] = bi < n ? bi : 0;
-            if (bi < n) row[bi] = -INFINITY;
-        }
-        __syncthreads();
+        taken += __popc(bsel);
     }
 }
 

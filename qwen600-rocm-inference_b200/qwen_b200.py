@@ -69,6 +69,7 @@ _SIGS = {
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
     "qwen_set_prefill_mode": (_c.c_int, [_P, _c.c_int]),
+    "qwen_row_topk": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P, _P, _P]),
     "qwen_batch_init": (_c.c_int, [_P, _c.c_int]),
     "qwen_batch_prefill": (_c.c_int, [_P, _c.c_int, _P, _c.c_int, _P]),
     "qwen_batch_step": (_c.c_int, [_P, _c.c_int, _P, _P, _P, _P, _P]),
@@ -186,6 +187,13 @@ def gemv_bf16(W_ptr, x_ptr, y_ptr, n, k, stream=0):
     """y = bf16(W x) on device pointers (ints)."""
     _check(load_library().qwen_gemv_bf16(ctypes.c_void_p(W_ptr), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n, k,
                                          ctypes.c_void_p(stream)))
+
+
+def row_topk(logits_ptr, rows, n, ld, k, values_ptr, ids_ptr, stream=0):
+    """The k best entries of each row of fp32 logits (device pointers, ints):
+    values and column ids, k per row, in column order."""
+    _check(load_library().qwen_row_topk(ctypes.c_void_p(logits_ptr), rows, n, ld, k, ctypes.c_void_p(values_ptr),
+                                         ctypes.c_void_p(ids_ptr), ctypes.c_void_p(stream)))
 
 
 def gemm_bf16(A_ptr, B_ptr, C_ptr, M, N, K, c_fp32=True, stream=0):
