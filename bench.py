@@ -281,36 +281,41 @@ def long_context(qb, ck, n_prompt=4096, n_gen=512):
             "prefill_tok_s": n_prompt / pre_s}
 
 
-def batched_decode(qb, ck, batches=(8, 32, 128), n_prompt=1024, n_steps=24, warmup=3):
+def batched_decode(qb, ck, batches=(8, 32, 128), n_prompt=1024, n_steps=24, warmup=3, sampled=(32,)):
     """qwen_batch_step at 1K context: 128 slots prefilled with seeded 1024-token
     prompts, then for each B greedy steps over slots 0..B-1 (every slot at its
-    own next position).  Wall time of the synchronous calls (inputs from host
-    memory, next tokens back to host memory every step) after `warmup` steps;
-    aggregate tok/s = B x steps / time."""
+    own next position), and for each B in `sampled` steps sampled at
+    temperature 0.6, top-p 0.95, top-k 20 (device top-k, host draw per row).
+    Wall time of the synchronous calls (inputs from host memory, next tokens
+    back to host memory every step) after `warmup` steps; aggregate tok/s =
+    B x steps / time."""
     eng = qb.Engine(ck, 0)
     out = []
     try:
-        top = max(batches)
+        top = max(tuple(batches) + tuple(sampled))
         eng.batch_init(top)
         pos = []
         for slot in range(top):
             prompt = np.random.default_rng(5000 + slot).integers(0, 151936, n_prompt).tolist()
             eng.batch_prefill(slot, prompt)
             pos.append(n_prompt)
-        for b in batches:
+        runs = [(b, "greedy") for b in batches] + [(b, "top_k 20") for b in sampled]
+        for b, mode in runs:
             toks = [5] * b
+            sp = qb.GREEDY if mode == "greedy" else qb.Sampling(0.6, 0.95, 20)
+            rs = None if mode == "greedy" else list(range(1, b + 1))
             for i in range(warmup + n_steps):
                 if i == warmup:
                     t0 = time.perf_counter()
-                toks, _ = eng.batch_step(toks, pos[:b])
+                toks, rs = eng.batch_step(toks, pos[:b], sp, rs)
                 for r in range(b):
                     pos[r] += 1
             dt = time.perf_counter() - t0
-            out.append({"batch": b, "tok_s": b * n_steps / dt, "ms_per_step": dt / n_steps * 1e3,
+            out.append({"batch": b, "sampling": mode, "tok_s": b * n_steps / dt, "ms_per_step": dt / n_steps * 1e3,
                         "context": [min(pos[:b]) - n_steps, max(pos[:b])]})
     finally:
         eng.close()
-    return {"unit": "tok/s (aggregate over the batch)", "sampling": "greedy", "prompt_tokens": n_prompt, "points": out,
+    return {"unit": "tok/s (aggregate over the batch)", "prompt_tokens": n_prompt, "points": out,
             "path": "qwen_batch_step: projections and LM head as tcgen05 GEMMs over the batch rows, fp32 attention per row"}
 
 
