@@ -378,8 +378,9 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const
 // warp-wide count per bit), writing them in entry order.  The next level runs
 // the same over the concatenated survivors until one group is left; because
 // every level keeps entry order and level one's entries are in id order, a
-// position in a survivor list orders ties exactly as the id does.  NaN ranks
-// below every number; -0 counts as +0.  k <= 64 (at most 512 / 8 per group).
+// position in a survivor list orders ties exactly as the id does.  k = 1 is a
+// plain warp argmax.  NaN ranks below every number; -0 counts as +0.  k <= 64
+// (at most 512 / 8 per group).
 constexpr int kTopkGroup = 512;                 // entries per warp
 constexpr int kTopkPerLane = kTopkGroup / 32;
 constexpr int kTopkWarps = 8;                   // warps per block
@@ -418,6 +419,32 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
         const int j = base + e * 32 + lane;
         key[e] = j < n ? (kFirst ? order_key(logits[rb + j]) : in_key[rb + j]) : 0u;
     }
+    const bool fin = groups == 1;
+    auto put = [&](int slot, uint32_t kv, int j) {
+        const int id = j < n ? (kFirst ? j : in_id[rb + j]) : 0x7fffffff;
+        if (fin) {
+            fin_v[(size_t)row * k + slot] = key_value(kv);
+            fin_i[(size_t)row * k + slot] = id < n_ids ? id : 0;
+        } else {
+            out_key[(size_t)row * out_ld + (size_t)g * k + slot] = kv;
+            out_id[(size_t)row * out_ld + (size_t)g * k + slot] = id;
+        }
+    };
+    if (k == 1) {   // argmax: best key, first position among equals
+        uint32_t bk = key[0];
+        int bp = lane;
+        #pragma unroll
+        for (int e = 1; e < kTopkPerLane; e++)
+            if (key[e] > bk) { bk = key[e]; bp = e * 32 + lane; }
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
+            const int p2 = __shfl_xor_sync(0xffffffffu, bp, o);
+            if (k2 > bk || (k2 == bk && p2 < bp)) { bk = k2; bp = p2; }
+        }
+        if (lane == 0) put(0, bk, base + bp);
+        return;
+    }
     uint32_t T = 0u;
     int need = k;
     #pragma unroll 1
@@ -432,7 +459,6 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
     }
     // T: the k-th best key of the group; take every key above it and the first `need` equal to it
     const uint32_t lt = (1u << lane) - 1u;
-    const bool fin = groups == 1;
     int taken = 0, eq_seen = 0;
     #pragma unroll
     for (int e = 0; e < kTopkPerLane; e++) {
@@ -441,17 +467,7 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
         const bool sel = key[e] > T || (key[e] == T && eq_seen + __popc(beq & lt) < need);
         eq_seen += __popc(beq);
         const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
-        if (sel) {
-            const int slot = taken + __popc(bsel & lt);
-            const int id = j < n ? (kFirst ? j : in_id[rb + j]) : 0x7fffffff;
-            if (fin) {
-                fin_v[(size_t)row * k + slot] = key_value(key[e]);
-                fin_i[(size_t)row * k + slot] = id < n_ids ? id : 0;
-            } else {
-                out_key[(size_t)row * out_ld + (size_t)g * k + slot] = key[e];
-                out_id[(size_t)row * out_ld + (size_t)g * k + slot] = id;
-            }
-        }
+        if (sel) put(taken + __popc(bsel & lt), key[e], j);
         taken += __popc(bsel);
     }
 }
