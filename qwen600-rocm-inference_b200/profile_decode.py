@@ -16,7 +16,8 @@ captures the second decode step: position N + 1, context N + 2.
 
 With --batch B it profiles batched decode instead: B slots, each prefilled
 with its own seeded N-token prompt (qwen_batch_prefill), then K greedy
-qwen_batch_step calls over the B slots.
+qwen_batch_step calls over the B slots; --top-k k > 1 samples them instead
+(temperature 0.6, top-p 0.95, top-k k, one RNG state per slot).
 """
 import argparse
 import importlib.util
@@ -32,6 +33,7 @@ def main():
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--top-k", type=int, default=1)
     a = ap.parse_args()
     spec = importlib.util.spec_from_file_location("qwen_b200", os.path.join(HERE, "qwen_b200.py"))
     qb = importlib.util.module_from_spec(spec)
@@ -43,13 +45,15 @@ def main():
         for slot in range(a.batch):
             eng.batch_prefill(slot, np.random.default_rng(1000 + slot).integers(0, qb.VOCAB_SIZE, a.prompt).tolist())
         toks, pos = [5] * a.batch, [a.prompt] * a.batch
+        sp = qb.GREEDY if a.top_k <= 1 else qb.Sampling(0.6, 0.95, a.top_k)
+        rs = None if a.top_k <= 1 else list(range(1, a.batch + 1))
         t0 = time.perf_counter()
         for _ in range(a.steps):
-            toks, _ = eng.batch_step(toks, pos)
+            toks, rs = eng.batch_step(toks, pos, sp, rs)
             pos = [p + 1 for p in pos]
         dt = time.perf_counter() - t0
         eng.close()
-        print(f"batch {a.batch} prompt {a.prompt} steps {a.steps}: {dt / max(a.steps, 1) * 1e3:.2f} ms per step (host wall time)")
+        print(f"batch {a.batch} top-k {a.top_k} prompt {a.prompt} steps {a.steps}: {dt / max(a.steps, 1) * 1e3:.2f} ms per step (host wall time)")
         return
     prompt = np.random.default_rng(1000).integers(0, qb.VOCAB_SIZE, a.prompt).tolist()
     eng.prefill(prompt, 0)
