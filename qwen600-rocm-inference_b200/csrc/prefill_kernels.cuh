@@ -414,14 +414,15 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
     const size_t rb = (size_t)row * in_ld;
     const int base = g * kTopkGroup;
     uint32_t key[kTopkPerLane];
+    int idv[kTopkPerLane];   // ids, loaded with the keys (a later level's ids are not its positions)
     #pragma unroll
     for (int e = 0; e < kTopkPerLane; e++) {
         const int j = base + e * 32 + lane;
         key[e] = j < n ? (kFirst ? order_key(logits[rb + j]) : in_key[rb + j]) : 0u;
+        idv[e] = j < n ? (kFirst ? j : in_id[rb + j]) : 0x7fffffff;
     }
     const bool fin = groups == 1;
-    auto put = [&](int slot, uint32_t kv, int j) {
-        const int id = j < n ? (kFirst ? j : in_id[rb + j]) : 0x7fffffff;
+    auto put = [&](int slot, uint32_t kv, int id) {
         if (fin) {
             fin_v[(size_t)row * k + slot] = key_value(kv);
             fin_i[(size_t)row * k + slot] = id < n_ids ? id : 0;
@@ -432,17 +433,18 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
     };
     if (k == 1) {   // argmax: best key, first position among equals
         uint32_t bk = key[0];
-        int bp = lane;
+        int bp = lane, bid = idv[0];
         #pragma unroll
         for (int e = 1; e < kTopkPerLane; e++)
-            if (key[e] > bk) { bk = key[e]; bp = e * 32 + lane; }
+            if (key[e] > bk) { bk = key[e]; bp = e * 32 + lane; bid = idv[e]; }
         #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const uint32_t k2 = __shfl_xor_sync(0xffffffffu, bk, o);
             const int p2 = __shfl_xor_sync(0xffffffffu, bp, o);
-            if (k2 > bk || (k2 == bk && p2 < bp)) { bk = k2; bp = p2; }
+            const int i2 = __shfl_xor_sync(0xffffffffu, bid, o);
+            if (k2 > bk || (k2 == bk && p2 < bp)) { bk = k2; bp = p2; bid = i2; }
         }
-        if (lane == 0) put(0, bk, base + bp);
+        if (lane == 0) put(0, bk, bid);
         return;
     }
     uint32_t T = 0u;
@@ -462,12 +464,11 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
     int taken = 0, eq_seen = 0;
     #pragma unroll
     for (int e = 0; e < kTopkPerLane; e++) {
-        const int j = base + e * 32 + lane;
         const uint32_t beq = __ballot_sync(0xffffffffu, key[e] == T);
         const bool sel = key[e] > T || (key[e] == T && eq_seen + __popc(beq & lt) < need);
         eq_seen += __popc(beq);
         const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
-        if (sel) put(taken + __popc(bsel & lt), key[e], j);
+        if (sel) put(taken + __popc(bsel & lt), key[e], idv[e]);
         taken += __popc(bsel);
     }
 }
