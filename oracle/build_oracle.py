@@ -13,8 +13,9 @@ Outputs:
                                  static_loader.h, config.h) compiled for sm_100a
                                  from the reference tree, linked with cuBLAS
 
-The _ref builds read the reference sources where they lie (REFERENCE_DIR,
-default /root/reference) and write only into oracle/_ref/.  Nothing is copied
+The _ref builds read the reference sources where they lie (REFERENCE_DIR, by
+default a directory named "reference" beside the repository) and write only
+into oracle/_ref/.  Nothing is copied
 into this repository.  When the reference tree is absent (as on a GPU box),
 prebuilt _ref libraries that travelled with the snapshot are kept.
 """
@@ -23,7 +24,7 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("REFERENCE_DIR") or os.path.normpath(os.path.join(HERE, os.pardir, os.pardir, "reference"))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 OUT = os.path.join(HERE, "liboracle.so")
 REF_OUT = os.path.join(HERE, "_ref")

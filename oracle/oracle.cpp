@@ -505,4 +505,94 @@ int oracle_sample(const float* logits, int n, float temperature, float topp, int
     return pi[nc - 1].i;
 }
 
+// ---------------------------------------------------------------------------
+// Synthetic checkpoint writer, so that bench.py's reference arm (the timed CPU
+// baseline) obtains its weights without the product library.  It writes the
+// same safetensors file as the library's qwen_write_synthetic_checkpoint (a
+// CPU test compares the two byte for byte): tensors in byte-sorted name order
+// packed from offset 0 (the layout of the reference's TENSOR_METADATA,
+// static_loader.h:80-400), every matrix N(0, 0.02) in bf16 by Box-Muller on
+// splitmix64 uniforms keyed on the seed and the tensor name (FNV-1a), every
+// 1-D gain 1.0, lm_head a copy of the embedding (tied weights).
+// ---------------------------------------------------------------------------
+static uint64_t sm64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+int oracle_write_synthetic(const char* path, unsigned long long seed) {
+    struct T { std::string name; std::vector<int64_t> shape; size_t bytes = 0, off = 0; };
+    std::vector<T> t;
+    auto add = [&](const std::string& n, std::vector<int64_t> sh) {
+        T x; x.name = n; x.shape = sh; size_t e = 1; for (auto d : sh) e *= (size_t)d; x.bytes = 2 * e; t.push_back(x);
+    };
+    add("lm_head.weight", {VOCAB, DIM});
+    add("model.embed_tokens.weight", {VOCAB, DIM});
+    add("model.norm.weight", {DIM});
+    for (int l = 0; l < LAYERS; l++) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        add(p + "input_layernorm.weight", {DIM});
+        add(p + "mlp.down_proj.weight", {DIM, HIDDEN});
+        add(p + "mlp.gate_proj.weight", {HIDDEN, DIM});
+        add(p + "mlp.up_proj.weight", {HIDDEN, DIM});
+        add(p + "post_attention_layernorm.weight", {DIM});
+        add(p + "self_attn.k_norm.weight", {HD});
+        add(p + "self_attn.k_proj.weight", {KVD, DIM});
+        add(p + "self_attn.o_proj.weight", {DIM, QD});
+        add(p + "self_attn.q_norm.weight", {HD});
+        add(p + "self_attn.q_proj.weight", {QD, DIM});
+        add(p + "self_attn.v_proj.weight", {KVD, DIM});
+    }
+    std::sort(t.begin(), t.end(), [](const T& a, const T& b) { return a.name < b.name; });
+    size_t total = 0;
+    for (auto& x : t) { x.off = total; total += x.bytes; }
+    std::string js = "{\"__metadata__\":{\"format\":\"pt\",\"generator\":\"qwen_b200 synthetic N(0,0.02) seed " + std::to_string(seed) + "\"}";
+    for (const auto& x : t) {
+        js += ",\"" + x.name + "\":{\"dtype\":\"BF16\",\"shape\":[";
+        for (size_t k = 0; k < x.shape.size(); k++) js += (k ? "," : "") + std::to_string(x.shape[k]);
+        js += "],\"data_offsets\":[" + std::to_string(x.off) + "," + std::to_string(x.off + x.bytes) + "]}";
+    }
+    js += "}";
+    while ((8 + js.size()) % 256) js.push_back(' ');
+    const uint64_t hl = js.size();
+    const size_t file_bytes = 8 + hl + total;
+    const std::string tmp = std::string(path) + ".oracle-partial";
+    int fd = open(tmp.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0644);
+    if (fd < 0) return -1;
+    if (ftruncate(fd, (off_t)file_bytes) != 0) { close(fd); return -1; }
+    char* m = (char*)mmap(nullptr, file_bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    close(fd);
+    if (m == MAP_FAILED) return -1;
+    memcpy(m, &hl, 8);
+    memcpy(m + 8, js.data(), hl);
+    char* data = m + 8 + hl;
+    size_t emb_off = 0, lm_off = 0, emb_bytes = 0;
+    for (const auto& x : t) {
+        if (x.name == "model.embed_tokens.weight") { emb_off = x.off; emb_bytes = x.bytes; }
+        if (x.name == "lm_head.weight") { lm_off = x.off; continue; }
+        uint16_t* dst = (uint16_t*)(data + x.off);
+        const int64_t n = (int64_t)(x.bytes / 2);
+        if (x.shape.size() == 1) { for (int64_t i = 0; i < n; i++) dst[i] = 0x3F80; continue; }
+        uint64_t h = 1469598103934665603ull;
+        for (char ch : x.name) { h ^= (uint8_t)ch; h *= 1099511628211ull; }
+        const uint64_t key = sm64(seed ^ sm64(h));
+        #pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n / 2; i++) {
+            const uint64_t a = sm64(key + 2 * (uint64_t)i), b = sm64(key + 2 * (uint64_t)i + 1);
+            const double u1 = ((double)(a >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+            const double u2 = (double)(b >> 11) * (1.0 / 9007199254740992.0);
+            const double r = sqrt(-2.0 * log(u1)), th = 6.283185307179586 * u2;
+            dst[2 * i] = f2bf((float)(0.02 * r * cos(th)));
+            dst[2 * i + 1] = f2bf((float)(0.02 * r * sin(th)));
+        }
+    }
+    memcpy(data + lm_off, data + emb_off, emb_bytes);
+    const int ok = msync(m, file_bytes, MS_SYNC) == 0;
+    munmap(m, file_bytes);
+    if (!ok || rename(tmp.c_str(), path) != 0) return -1;
+    return 0;
+}
+
 }  // extern "C"

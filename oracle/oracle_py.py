@@ -38,12 +38,21 @@ def lib():
         L.oracle_random_u32.argtypes = [c.POINTER(c.c_ulonglong)]
         L.oracle_random_u32.restype = c.c_uint
         L.oracle_rope_cs.argtypes = [c.c_int, c.c_int, c.POINTER(c.c_float), c.POINTER(c.c_float)]
+        L.oracle_write_synthetic.argtypes = [c.c_char_p, c.c_ulonglong]
         _lib = L
     return _lib
 
 
 def _p(a):
     return ctypes.c_void_p(a.ctypes.data)
+
+
+def write_synthetic_checkpoint(path, seed=0):
+    """The seed-`seed` synthetic safetensors checkpoint, written by the oracle
+    (byte-identical to the library's own writer; bench.py's reference arm uses
+    this so that it never loads the product library)."""
+    if lib().oracle_write_synthetic(path.encode(), int(seed)) != 0:
+        raise RuntimeError(f"oracle_write_synthetic failed for {path}")
 
 
 def set_threads(n):

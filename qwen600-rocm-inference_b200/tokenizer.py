@@ -127,18 +127,20 @@ def export_from_tokenizer_json(tokenizer_json, bos_token_id, eos_token_id, out_p
     every id of model.vocab and added_tokens in order, each token's characters
     mapped back to bytes (characters outside the byte alphabet as UTF-8), scores
     -log(rank + 1) for tokens that are the result of merge `rank`, -1e6 for the
-    rest; max_token_length = the longest token in characters.  Returns the
-    number of tokens written."""
+    rest (a merge result produced by several merges scores by the last one);
+    max_token_length = the longest token in characters.  Returns the number of
+    tokens written."""
     with open(tokenizer_json, encoding="utf-8") as f:
         data = json.load(f)
     id_to_token = {int(i): t for t, i in data["model"]["vocab"].items()}
     for a in data.get("added_tokens", []):
         id_to_token[int(a["id"])] = a["content"]
     tokens = [id_to_token[i] for i in sorted(id_to_token)]
+    # A string that several merges produce takes the rank of the LAST of them,
+    # as export.py:186 builds its table (a dict comprehension overwrites).
     rank = {}
     for r, m in enumerate(data["model"].get("merges", [])):
-        key = "".join(m if isinstance(m, list) else m.split())
-        rank.setdefault(key, r)
+        rank["".join(m if isinstance(m, list) else m.split())] = r
     u2b = {c: b for b, c in bytes_to_unicode().items()}
     pieces = [b"".join(bytes([u2b[ch]]) if ch in u2b else ch.encode("utf-8") for ch in t) for t in tokens]
     scores = [-math.log(rank[t] + 1) if t in rank else -1e6 for t in tokens]

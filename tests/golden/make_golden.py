@@ -26,7 +26,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
-REF = os.environ.get("REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("REFERENCE_DIR") or os.path.normpath(os.path.join(REPO, os.pardir, "reference"))
 VOCAB = 151936
 
 # (logit seed, scale, temperature, topp, top_k, rng seed, bf16-valued logits)

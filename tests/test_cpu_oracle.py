@@ -138,3 +138,17 @@ def test_oracle_forward_tracks_reference_cuda(O, checkpoint):
         assert abs(lb.astype(np.float64).sum() - s[0]) < 0.03 * np.sqrt(s[1]) * 1.0 + 15.0, pos
     assert agree >= len(toks) - 3, agree
     assert min(late_gap) > 0.04, late_gap      # the reference's softmax defect is visible
+
+
+def test_oracle_checkpoint_writer_matches_library(O, checkpoint, tmp_path):
+    """bench.py's reference arm writes its checkpoint through the oracle (it must
+    not load the engine library); that file is the library's, byte for byte."""
+    import numpy as np
+    p = str(tmp_path / "oracle-seed0.safetensors")
+    O.write_synthetic_checkpoint(p, 0)
+    a = np.memmap(p, dtype=np.uint8, mode="r")
+    b = np.memmap(checkpoint, dtype=np.uint8, mode="r")
+    assert a.shape == b.shape
+    step = 64 << 20
+    for i in range(0, a.shape[0], step):
+        assert np.array_equal(a[i:i + step], b[i:i + step]), f"differs in bytes [{i}, {i + step})"

@@ -3,6 +3,7 @@ templates) against the reference's own tokenizer.h: token ids recorded by
 tests/golden/make_tokenizer_golden.py on a seeded synthetic vocabulary.  Host
 code only (no GPU)."""
 import json
+import math
 import os
 import struct
 import sys
@@ -146,6 +147,27 @@ def test_export_from_tokenizer_json(tmp_path):
         sc.append(s)
         off += 8 + n
     assert sc[3] == 0.0 and abs(sc[4] + 0.6931472) < 1e-6 and sc[0] == sc[5] == pytest.approx(-1e6)
+
+
+def test_export_duplicate_merge_takes_last_rank(tmp_path):
+    """Two merges that produce the same string ("a bc" and "ab c" both give
+    "abc"): the score comes from the later one, rank 2 -> -log(3), the way
+    export.py:186's dict comprehension keeps the last rank."""
+    tj = {"model": {"vocab": {"a": 0, "b": 1, "c": 2, "ab": 3, "bc": 4, "abc": 5},
+                    "merges": ["b c", "a bc", "ab c", "a b"]}}
+    jp = tmp_path / "tokenizer.json"
+    jp.write_text(json.dumps(tj), encoding="utf-8")
+    out = str(tmp_path / "tokenizer.bin")
+    assert T.export_from_tokenizer_json(str(jp), 0, 0, out) == 6
+    raw = open(out, "rb").read()
+    off, sc = 12, []
+    for _ in range(6):
+        s, n = struct.unpack_from("<fI", raw, off)
+        sc.append(s)
+        off += 8 + n
+    assert sc[5] == pytest.approx(-math.log(3))      # "abc": rank 2 ("ab c"), not rank 1
+    assert sc[3] == pytest.approx(-math.log(4))      # "ab": rank 3
+    assert sc[4] == 0.0                              # "bc": rank 0
 
 
 def test_templates(model_dir):
