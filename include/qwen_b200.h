@@ -108,6 +108,12 @@ float* qwen_host_logits(qwen_t* ctx);
 /* Device pointer to the fp32 logits of the last forward / decode step. */
 const float* qwen_device_logits(qwen_t* ctx);
 
+/* Device pointer to the handle's weight block, in the canonical layout of
+ * qwen_tensor_info (tensor i at offset i); the handle owns it.  Lets the C++
+ * names fill Transformer.weights (qwen_model.cuh:53, TransformerWeights
+ * weights) with pointers a reference-written caller can index. */
+const void* qwen_device_weights(const qwen_t* ctx);
+
 /* Copy the fp32 logits of the last forward / decode / generate step (the rows
  * this handle serves: all VOCAB_SIZE, or its vocabulary shard) to host memory;
  * returns the number of floats copied.  The reference's forward() hands these

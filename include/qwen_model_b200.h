@@ -10,7 +10,8 @@
  *     int next = sample(&s, logits);                // sampler.h:120
  *     free_sampler(&s); free_transformer(&t);
  *
- * Same names and argument meaning as qwen_model.cuh:51-60 (Transformer),
+ * Same names and argument meaning as qwen_model.cuh:26-60 (TransformerWeights,
+ * RunState, Transformer with its weights / state / h_logits members),
  * :82 (build_transformer), :94 (free_transformer), :772 (forward) and
  * sampler.h:11-24 (ProbIndex, Sampler), :100 (build_sampler), :115
  * (free_sampler), :120 (sample).  Differences, all in the direction of safety:
@@ -35,10 +36,32 @@
 #include <string>
 
 #include "qwen_b200.h"
+#include "static_loader_b200.h"
 
+using TransformerWeights = qwen_loader::QwenWeights;   /* qwen_model.cuh:26 */
+
+/* RunState (qwen_model.cuh:31-49): the engine keeps its activations in
+ * exchange buffers of its own layout, so only the members with the same
+ * meaning and layout are set; the rest stay nullptr rather than point at
+ * differently laid-out memory (the engine's K/V cache is
+ * [layer][kv_head][pos][head_dim], the reference's [layer][pos][kv_dim]). */
+struct RunState {
+    qwen_loader::bf16 *x = nullptr, *xb = nullptr, *xb2 = nullptr, *hb = nullptr, *hb2 = nullptr, *q = nullptr;
+    float* att = nullptr;
+    qwen_loader::bf16* logits = nullptr;
+    qwen_loader::bf16 *key_cache = nullptr, *value_cache = nullptr;
+    const float* d_logits_fp32 = nullptr;   /* the last step's fp32 logits on the device [VOCAB] */
+};
+
+/* Transformer (qwen_model.cuh:51-60).  `weights` points into the handle's
+ * device weight block (the handle owns it); the engine uses no cuBLAS, so
+ * cublas_handle stays nullptr. */
 struct Transformer {
-    qwen_t* handle = nullptr;
+    TransformerWeights weights;
+    RunState state;
+    void* cublas_handle = nullptr;
     float* h_logits = nullptr;   /* pinned host logits [VOCAB] owned by the handle */
+    qwen_t* handle = nullptr;
 };
 
 inline void qwen_model_b200_check(int rc, const char* what) {
@@ -48,12 +71,17 @@ inline void qwen_model_b200_check(int rc, const char* what) {
 inline void build_transformer(Transformer* t, const char* checkpoint_path, int device = 0) {
     qwen_model_b200_check(qwen_create(checkpoint_path, device, &t->handle), "build_transformer");
     t->h_logits = qwen_host_logits(t->handle);
+    qwen_loader::assign_weight_pointers(const_cast<void*>(qwen_device_weights(t->handle)), t->weights);
+    t->state = RunState{};
+    t->state.d_logits_fp32 = qwen_device_logits(t->handle);
 }
 
 inline void free_transformer(Transformer* t) {
     qwen_destroy(t->handle);
     t->handle = nullptr;
     t->h_logits = nullptr;
+    t->weights = TransformerWeights{};
+    t->state = RunState{};
 }
 
 /* Logits of position `pos` for `token`; positions must arrive in order

@@ -384,6 +384,7 @@ extern "C" void qwen_destroy(qwen_t* c) { ctx_free(c); }
 extern "C" int qwen_device(const qwen_t* c) { return c ? c->device : -1; }
 extern "C" float* qwen_host_logits(qwen_t* c) { return c ? c->h_logits : nullptr; }
 extern "C" const float* qwen_device_logits(qwen_t* c) { return c ? c->logits : nullptr; }
+extern "C" const void* qwen_device_weights(const qwen_t* c) { return c ? c->wblock : nullptr; }
 extern "C" int qwen_cached_positions(const qwen_t* c) { return c ? c->cached : -1; }
 
 static int count_launch(qwen_t* c) {

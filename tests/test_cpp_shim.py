@@ -82,3 +82,60 @@ def test_shim_tokenizer_matches_reference_ids(qb, tmp_path):
         k = lines.index(next(l for l in lines if l.startswith(b"#")))
         assert [int(x) for x in lines[:k]] == case["ids"]
         assert b"\n".join(lines[k:])[1:].rstrip(b"\n") == case["text"].encode("utf-8").rstrip(b"\n")
+
+
+def _build_loader(tmp_path):
+    exe = str(tmp_path / "shim_loader")
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-Werror", "-I", os.path.join(REPO, "include"), "-I", os.path.join(cuda, "include"),
+           os.path.join(REPO, "tests", "cpp", "shim_loader.cpp"), "-o", exe, "-L", LIB_DIR, "-lqwen_b200",
+           "-L", os.path.join(cuda, "lib64"), "-lcudart", "-Wl,-rpath," + LIB_DIR]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def test_loader_names_give_reference_table(qb, tmp_path):
+    """static_loader.h's names (NUM_TENSORS, TOTAL_WEIGHTS_BYTES,
+    TENSOR_METADATA[i].name/.offset/.size_bytes) compile against the library and
+    hold the reference's own table (tests/golden/tensor_table.json, read from
+    static_loader.h:80-400).  No GPU needed."""
+    qb.load_library()
+    exe = _build_loader(tmp_path)
+    r = subprocess.run([exe, "table"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.split("\n")
+    n, total = map(int, lines[0].split())
+    gold = json.load(open(os.path.join(REPO, "tests", "golden", "tensor_table.json")))
+    assert n == 311 and total == gold["total_bytes"]
+    got = [(l.split()[0], int(l.split()[1]), int(l.split()[2])) for l in lines[1:1 + n]]
+    want = [tuple(t) for t in gold["tensors"]]
+    assert got == want                    # same entries, same index order as the reference's array
+
+
+@pytest.mark.gpu
+def test_loader_names_point_into_the_weight_block(qb, checkpoint, tmp_path):
+    """load_qwen_weights and Transformer.weights: every member points at its
+    tensor's canonical offset, and the tensors read back through them equal the
+    checkpoint's bytes."""
+    exe = _build_loader(tmp_path)
+    r = subprocess.run([exe, "load", checkpoint], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr + r.stdout
+    rows = [l.split() for l in r.stdout.strip().split("\n")]
+    hdr = int.from_bytes(open(checkpoint, "rb").read(8), "little")
+    meta = json.loads(open(checkpoint, "rb").read(8 + hdr)[8:])
+
+    def fnv(name):
+        a, b = meta[name]["data_offsets"]
+        with open(checkpoint, "rb") as f:
+            f.seek(8 + hdr + a)
+            data = np.frombuffer(f.read(b - a), dtype=np.uint8)
+        h = 1469598103934665603           # FNV-1a, as shim_loader.cpp hashes
+        for x in data.tobytes():
+            h = ((h ^ x) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+        return f"{h:016x}"
+
+    names = ["model.layers.5.self_attn.q_proj.weight", "model.layers.27.mlp.down_proj.weight", "model.norm.weight"]
+    for row, name in zip(rows, names):
+        want = fnv(name)
+        assert row == [want, want], name
