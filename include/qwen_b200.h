@@ -123,7 +123,12 @@ int qwen_read_logits(qwen_t* ctx, float* logits_host);
 /* forward(token, pos) followed by sample() on the device (main.cu:144-145 with
  * sampler.h:120-175): *next_token receives the sampled id and *rng_state the
  * advanced xorshift64* state.  Only 4 + 8 bytes come back to the host.
- * Device sampling supports argmax and 1 <= top_k <= 64. */
+ * The device samples argmax and, with the nucleus cut on (0 < topp < 1),
+ * 1 <= top_k <= 64 candidates.  Every other setting (topp outside (0, 1),
+ * top_k = 0 or > 64) draws on the host from the step's device logits with
+ * qwen_sample_host, because the reference's candidate order is then the
+ * partition order of its quickselect over the whole vocabulary
+ * (sampler.h:131-134): one VOCAB_SIZE-float copy per step, same token stream. */
 int qwen_decode_step(qwen_t* ctx, int token, int pos, const qwen_sampling_t* sp,
                      unsigned long long* rng_state, int* next_token);
 
@@ -187,12 +192,17 @@ int qwen_sample_candidates(const float* values, const int* ids, int n, const qwe
  * in three bf16 parts, fp32-exact products), attention of each row over its own
  * cache slot in fp32, the LM head as one GEMM, top-k per row on the device and
  * the sampler's math on the host (the device sampler's, as in
- * qwen_sample_candidates).  Same numerics as the batch-1 chain up to fp32
+ * qwen_sample_candidates; settings outside the device sampler's set, as for
+ * qwen_decode_step, draw with qwen_sample_host over each whole logits row).  Same numerics as the batch-1 chain up to fp32
  * summation order. */
 
 /* Allocates max_batch (1..128) KV cache slots, each holding SEQ_LEN positions
  * (939 MiB per slot).  Once per handle (QWEN_E_STATE after). */
 int qwen_batch_init(qwen_t* ctx, int max_batch);
+
+/* Copies the fp32 logits of the last qwen_batch_step's first `rows` rows
+ * (row r is the step's sequence r; VOCAB_SIZE floats per row) to host memory. */
+int qwen_batch_read_logits(qwen_t* ctx, int rows, float* logits_host);
 
 /* Positions 0 .. n-1 of slot `slot` from `tokens` (the slot's previous
  * contents are dropped); logits_host (may be NULL) receives the last

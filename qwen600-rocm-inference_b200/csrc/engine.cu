@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstring>
 #include <initializer_list>
+#include <chrono>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -462,10 +463,24 @@ static int check_step(qwen_t* c) {
 static int check_sampling(const qwen_sampling_t* sp) {
     if (!sp) return QWEN_OK;
     if (!(sp->temperature >= 0.0f)) return fail(QWEN_E_ARG, "temperature must be >= 0");
-    const bool greedy = sp->temperature == 0.0f || sp->top_k == 1;
-    if (!greedy && (sp->top_k < 1 || sp->top_k > kMaxCand))
-        return fail(QWEN_E_UNSUPPORTED, "device sampling serves 1 <= top_k <= 64 (top_k = 0 means the full vocabulary)");
+    if (sp->top_k < 0) return fail(QWEN_E_ARG, "top_k must be >= 0 (0 means the full vocabulary)");
     return QWEN_OK;
+}
+
+static bool is_greedy(const qwen_sampling_t* sp) { return !sp || sp->temperature == 0.0f || sp->top_k == 1; }
+
+// Sampling settings the device sampler reproduces token for token.  The
+// reference draws over its candidates in the order its quickselect leaves them
+// (sampler.h:131-134) and, with the nucleus cut on, re-sorts them by
+// probability first (sampler.h:153-156).  With the cut on and at most kMaxCand
+// candidates the device's descending order is that order (candidates whose
+// fp32 logits are exactly equal aside); with the cut off (topp outside (0, 1))
+// the order is the partition order of a quickselect over the whole
+// vocabulary, which only that sequential pass reproduces, and top_k = 0 or
+// > kMaxCand exceeds the device list.  Those settings sample on the host from
+// the device logits (qwen_sample_host, the reference's own order).
+static bool device_exact(const qwen_sampling_t* sp) {
+    return is_greedy(sp) || (sp->topp > 0.0f && sp->topp < 1.0f && sp->top_k >= 1 && sp->top_k <= kMaxCand);
 }
 
 static void fill_in(qwen_t* c, int token, int pos, const qwen_sampling_t* sp, unsigned long long rng, int flags) {
@@ -497,6 +512,36 @@ extern "C" int qwen_forward(qwen_t* c, int token, int pos, float* logits_host) {
     return QWEN_OK;
 }
 
+// n_steps chained steps whose token is drawn on the host from each step's
+// device logits by qwen_sample_host (settings device_exact() rejects): one
+// launch, one logits copy and one host draw per step.  *device_ms (if given)
+// receives the time of the whole loop, host draws included.
+static int host_sampled_steps(qwen_t* c, int token, int pos, int n_steps, const qwen_sampling_t* sp, unsigned long long* rng_state,
+                              int* tokens_out, float* device_ms) {
+    if (!rng_state) return fail(QWEN_E_ARG, "sampling needs rng_state");
+    if (c->params.lm_begin != 0 || c->params.lm_end != VOCAB_SIZE)
+        return fail(QWEN_E_UNSUPPORTED, "this sampling setting draws over the full vocabulary on the host; the handle serves a vocabulary shard");
+    CU(cudaSetDevice(c->device));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int i = 0; i < n_steps; i++) {
+        fill_in(c, token, pos + i, nullptr, 0, kFlagWriteLogits);
+        CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+        int rc = launch_decode(c);
+        if (rc != QWEN_OK) return rc;
+        CU(cudaMemcpyAsync(c->h_logits, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+        CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+        CU(cudaStreamSynchronize(c->stream));
+        if ((rc = check_step(c)) != QWEN_OK) return rc;
+        c->cached = pos + i + 1;
+        if ((rc = qwen_sample_host(c->h_logits, VOCAB_SIZE, sp, rng_state, &token)) != QWEN_OK)
+            return fail(rc, "host sampling failed");
+        tokens_out[i] = token;
+    }
+    if (device_ms) *device_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    c->last_k = 1;
+    return QWEN_OK;
+}
+
 extern "C" int qwen_decode_step(qwen_t* c, int token, int pos, const qwen_sampling_t* sp, unsigned long long* rng_state, int* next) {
     if (!c || !next) return fail(QWEN_E_ARG, "NULL argument");
     if (token < 0 || token >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
@@ -504,6 +549,7 @@ extern "C" int qwen_decode_step(qwen_t* c, int token, int pos, const qwen_sampli
     if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
+    if (!device_exact(sp)) return host_sampled_steps(c, token, pos, 1, sp, rng_state, next, nullptr);
     CU(cudaSetDevice(c->device));
     if (!c->step_exec && !c->step_graph_off && !c->params.trace) build_step_graph(c);
     fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, kFlagWriteLogits);
@@ -533,6 +579,7 @@ extern "C" int qwen_generate(qwen_t* c, int token, int pos, int n_steps, const q
     if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
+    if (!device_exact(sp)) return host_sampled_steps(c, token, pos, n_steps, sp, rng_state, tokens_out, nullptr);
     CU(cudaSetDevice(c->device));
     fill_in(c, token, pos, sp, rng_state ? *rng_state : 0, kFlagWriteLogits);
     CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
@@ -559,6 +606,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
     if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
+    if (!device_exact(sp)) return host_sampled_steps(c, token, pos, n_steps, sp, rng_state, tokens_out, device_ms);
     CU(cudaSetDevice(c->device));
     cudaEvent_t e0, e1;
     CU(cudaEventCreate(&e0));
@@ -858,14 +906,15 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
     if (batch < 1 || batch > c->b_max) return fail(QWEN_E_ARG, "batch out of [1, max_batch]");
     int rc = check_sampling(sp);
     if (rc != QWEN_OK) return rc;
-    const bool greedy = !sp || sp->temperature == 0.0f || sp->top_k == 1;
+    const bool greedy = is_greedy(sp);
     if (!greedy && !rng_states) return fail(QWEN_E_ARG, "sampling needs rng_states");
+    const bool host_order = !device_exact(sp);   // draw over whole logits rows on the host (the reference's order)
     for (int r = 0; r < batch; r++) {
         if (tokens[r] < 0 || tokens[r] >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
         if (pos[r] < 0 || pos[r] >= SEQ_LEN) return fail(QWEN_E_ARG, "pos out of range [0, SEQ_LEN)");
         if (pos[r] > c->b_cached[r]) return fail(QWEN_E_STATE, "pos skips uncached positions of its slot");
     }
-    const int K = greedy ? 1 : sp->top_k;
+    const int K = greedy || host_order ? 1 : sp->top_k;
     const int rows = (batch + 127) / 128 * 128;
     constexpr int kLdAs = 3 * HIDDEN_DIM;
     CU(cudaSetDevice(c->device));
@@ -904,6 +953,9 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
     else if ((rc = body()) != QWEN_OK) return rc;
     std::vector<float> cv((size_t)batch * K);
     std::vector<int> ci((size_t)batch * K);
+    std::vector<float> rows_host(host_order ? (size_t)batch * VOCAB_SIZE : 0);
+    if (host_order)
+        CU(cudaMemcpyAsync(rows_host.data(), c->b_logits, rows_host.size() * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     CU(cudaMemcpyAsync(cv.data(), c->b_cv, cv.size() * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     CU(cudaMemcpyAsync(ci.data(), c->b_ci, ci.size() * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     CU(cudaStreamSynchronize(c->stream));
@@ -913,10 +965,23 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
     }
     for (int r = 0; r < batch; r++) {
         if (greedy) next[r] = ci[r];
-        else if ((rc = qwen_sample_candidates(&cv[(size_t)r * K], &ci[(size_t)r * K], K, sp, &rng_states[r], &next[r])) != QWEN_OK)
+        else if (host_order) {
+            if ((rc = qwen_sample_host(&rows_host[(size_t)r * VOCAB_SIZE], VOCAB_SIZE, sp, &rng_states[r], &next[r])) != QWEN_OK)
+                return fail(rc, "host sampling failed");
+        } else if ((rc = qwen_sample_candidates(&cv[(size_t)r * K], &ci[(size_t)r * K], K, sp, &rng_states[r], &next[r])) != QWEN_OK)
             return rc;
         c->b_cached[r] = pos[r] + 1;
     }
+    return QWEN_OK;
+}
+
+extern "C" int qwen_batch_read_logits(qwen_t* c, int rows, float* logits_host) {
+    if (!c || !logits_host) return fail(QWEN_E_ARG, "NULL argument");
+    if (!c->b_max) return fail(QWEN_E_STATE, "qwen_batch_init first");
+    if (rows < 1 || rows > c->b_max) return fail(QWEN_E_ARG, "rows out of [1, max_batch]");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpyAsync(logits_host, c->b_logits, (size_t)rows * VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
     return QWEN_OK;
 }
 

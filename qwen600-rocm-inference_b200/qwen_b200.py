@@ -49,6 +49,7 @@ _SIGS = {
     "qwen_forward": (_c.c_int, [_P, _c.c_int, _c.c_int, _P]),
     "qwen_host_logits": (_P, [_P]),
     "qwen_device_logits": (_P, [_P]),
+    "qwen_device_weights": (_P, [_P]),
     "qwen_read_logits": (_c.c_int, [_P, _P]),
     "qwen_decode_step": (_c.c_int, [_P, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _c.POINTER(_c.c_int)]),
     "qwen_generate": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _P]),
@@ -73,6 +74,7 @@ _SIGS = {
     "qwen_batch_init": (_c.c_int, [_P, _c.c_int]),
     "qwen_batch_prefill": (_c.c_int, [_P, _c.c_int, _P, _c.c_int, _P]),
     "qwen_batch_step": (_c.c_int, [_P, _c.c_int, _P, _P, _P, _P, _P]),
+    "qwen_batch_read_logits": (_c.c_int, [_P, _c.c_int, _P]),
     "qwen_tokenizer_load": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
     "qwen_tokenizer_free": (None, [_P]),
     "qwen_tokenizer_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
@@ -303,6 +305,12 @@ class Engine:
         _check(self._lib.qwen_batch_step(self._h, tk.size, _ptr(tk), _ptr(ps), ctypes.byref(sampling),
                                          _ptr(rs) if rs is not None else None, _ptr(nx)))
         return nx.tolist(), (rs.tolist() if rs is not None else None)
+
+    def batch_read_logits(self, rows):
+        """fp32 logits of the last batch_step's first `rows` rows, shape (rows, VOCAB_SIZE)."""
+        out = np.zeros((int(rows), VOCAB_SIZE), dtype=np.float32)
+        _check(self._lib.qwen_batch_read_logits(self._h, int(rows), _ptr(out)))
+        return out
 
     def set_prefill_mode(self, gemm=True):
         """Long prompts on the tensor cores (True, default) or one decode launch per token."""

@@ -104,6 +104,32 @@ def test_batch_sampled_slots_are_independent(qb, checkpoint):
         assert together[slot] == alone, slot
 
 
+@pytest.mark.parametrize("T,p,k", [(0.8, 1.0, 20), (0.7, 1.0, 0), (0.6, 0.95, 20)])
+def test_batch_sampled_tokens_follow_reference_order(qb, O, checkpoint, T, p, k):
+    """Every sampled batch token equals the oracle sampler in the reference's
+    candidate order (order_mode=0) on that row's logits: with the nucleus cut
+    off or k = 0 the step draws over the whole row on the host; with it on,
+    over the device top-k."""
+    sp = qb.Sampling(T, p, k)
+    prompts, seeds = _prompts(), [5, 6, 7, 8]
+    b = qb.Engine(checkpoint, 0)
+    try:
+        b.batch_init(len(prompts))
+        for slot, pr in enumerate(prompts):
+            b.batch_prefill(slot, pr[:-1])
+        toks, pos = [pr[-1] for pr in prompts], [len(pr) - 1 for pr in prompts]
+        rngs = list(seeds)
+        for _ in range(6):
+            nxt, rngs2 = b.batch_step(toks, pos, sp, rngs)
+            lg = b.batch_read_logits(len(prompts))
+            for r in range(len(prompts)):
+                want, want_rng = O.sample(lg[r], T, p, k, rngs[r], order_mode=0)
+                assert (nxt[r], rngs2[r]) == (want, want_rng), r
+            toks, rngs, pos = nxt, rngs2, [q + 1 for q in pos]
+    finally:
+        b.close()
+
+
 def test_batch_errors(qb, checkpoint):
     b = qb.Engine(checkpoint, 0)
     try:

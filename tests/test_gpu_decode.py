@@ -74,7 +74,13 @@ def test_decode_step_argmax_is_first_max(engine):
         tok = nxt
 
 
-@pytest.mark.parametrize("T,p,k", [(0.6, 0.95, 20), (1.0, 0.9, 40), (0.8, 1.0, 64), (0.3, 0.5, 5), (0.6, 0.95, 1)])
+# (T, p, k): nucleus cut on with k <= 64 samples on the device; the cut off
+# (p = 1.0 or 0), k = 0 (whole vocabulary) and k > 64 draw on the host from the
+# device logits.  Every case is checked against the oracle sampler in the
+# reference's own candidate order (order_mode=0: quickselect order, then the
+# top-p sort), so the stream is the one sampler.h would give on these logits.
+@pytest.mark.parametrize("T,p,k", [(0.6, 0.95, 20), (1.0, 0.9, 40), (0.8, 1.0, 64), (0.3, 0.5, 5), (0.6, 0.95, 1),
+                                   (0.7, 1.0, 20), (0.9, 0.0, 8), (0.7, 1.0, 0), (0.8, 0.9, 100)])
 def test_device_sampler_matches_oracle_sampler(engine, O, qb, T, p, k):
     engine.prefill(PROMPT, 0)
     sp = qb.Sampling(T, p, k)
@@ -83,9 +89,22 @@ def test_device_sampler_matches_oracle_sampler(engine, O, qb, T, p, k):
     for pos in range(16, 40):
         nxt, rng2 = engine.decode_step(tok, pos, sp, rng)
         lg = engine.read_logits()
-        want, want_rng = O.sample(lg, T, p, k, rng, order_mode=1)
+        want, want_rng = O.sample(lg, T, p, k, rng, order_mode=0)
         assert (nxt, rng2) == (want, want_rng), pos
         tok, rng = nxt, rng2
+
+
+def test_generate_with_cut_off_matches_decode_steps(engine, qb):
+    """top-p off: generate() draws each step on the host like decode_step()."""
+    sp = qb.Sampling(0.8, 1.0, 20)
+    engine.prefill(PROMPT, 0)
+    a, ra = engine.generate(PROMPT[-1], 16, 12, sp, 7)
+    engine.prefill(PROMPT, 0)
+    b, tok, r = [], PROMPT[-1], 7
+    for pos in range(16, 28):
+        tok, r = engine.decode_step(tok, pos, sp, r)
+        b.append(tok)
+    assert a == b and ra == r
 
 
 def test_generate_matches_decode_steps(engine, qb):
