@@ -269,25 +269,41 @@ int qwen_trace_read(qwen_t* ctx, unsigned long long* out, int max_entries);
 /* ---- isolated kernels ---------------------------------------------------- */
 
 /* y[n] = bf16(W[n][k] . x[k]) with fp32 accumulation; W row-major bf16, x and y
- * bf16, all device pointers; k a multiple of 256, k <= 4096.  `stream` is a
- * cudaStream_t (NULL = legacy default stream).  The GEMV of matmul_cublas
- * (qwen_model.cuh:706-757) with alpha = 1, beta = 0. */
+ * bf16, all device pointers (W and x 16-byte aligned); k a multiple of 256,
+ * k <= 4096.  `stream` is a cudaStream_t (NULL = legacy default stream).  The
+ * GEMV of matmul_cublas (qwen_model.cuh:706-757) with alpha = 1, beta = 0.
+ * Asynchronous: matrices up to 64 MB take a direct-load kernel with no waits;
+ * larger ones a TMA-ring kernel whose bounded waits, if one ever expires,
+ * leave y invalid and set the device's error word, which
+ * qwen_gemv_bf16_status reports. */
 int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* stream);
+
+/* Synchronises `stream` and reports QWEN_E_TIMEOUT if a qwen_gemv_bf16 launch
+ * on the current device since the last query had a device wait expire (its y
+ * is invalid), else QWEN_OK; clears the word.  Replaces the reference's
+ * exit() on a failed cuBLAS call (static_loader.h:22-30). */
+int qwen_gemv_bf16_status(void* stream);
 
 /* qwen_gemv_bf16 without any device allocation.  No counterpart in the
  * reference: it is for callers that must not call cudaMalloc, such as code
  * that runs while a stream is being captured into a CUDA graph, or code inside
  * a framework whose memory pool already holds the device's memory.  (The
- * plain entry point allocates its 4-byte device scratch word on its first call
+ * plain entry point allocates its 4-byte device error word on its first call
  * per device.)  The kernel's scratch lives in a 256-byte file-scope device
  * array that every GPU loading the library holds until exit; this call uses
- * one word of it and clears it before each launch.  Same shapes and
- * arguments as qwen_gemv_bf16: k must be a positive multiple of 256 and at
- * most 4096 (larger k is rejected with QWEN_E_ARG).  The first call on each
- * device looks up the array's device address (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture.  All calls
- * share the one array, so calls whose kernels overlap on the GPU race on it. */
+ * one word of it as the ring kernel's error word, which starts at zero and is
+ * read and cleared by qwen_gemv_bf16_static_status.  Same shapes, arguments
+ * and result as qwen_gemv_bf16 (bit for bit): k must be a positive multiple
+ * of 256 and at most 4096 (larger k is rejected with QWEN_E_ARG).  The first
+ * call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls share the one array, so calls whose
+ * kernels overlap on the GPU race on it. */
 int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, void* stream);
+
+/* qwen_gemv_bf16_status for qwen_gemv_bf16_static's error word (allocates
+ * nothing; not for use while `stream` is being captured: it synchronises). */
+int qwen_gemv_bf16_static_status(void* stream);
 
 /* C[M][N] = A[M][K] . B[N][K]^T on the tensor cores (tcgen05.mma, bf16 in, fp32
  * accumulate in TMEM; 128 x 256 or 128 x 128 tiles, TMA-fed).  A and B bf16

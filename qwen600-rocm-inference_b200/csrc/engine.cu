@@ -1077,29 +1077,84 @@ extern "C" int qwen_debug_chunk_counts(qwen_t* c, int* out, int max_ctas) {
 // ---------------------------------------------------------------------------
 // isolated GEMV
 // ---------------------------------------------------------------------------
-extern "C" int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* stream) {
-    if (!W || !x || !y) return fail(QWEN_E_ARG, "NULL argument");
-    if (n <= 0 || k <= 0 || k % 256 != 0 || k > 4096) return fail(QWEN_E_ARG, "k must be a positive multiple of 256, <= 4096");
-    if (((uintptr_t)W | (uintptr_t)x) & 15) return fail(QWEN_E_ARG, "W and x must be 16-byte aligned");
-    static thread_local int attr_dev = -1;
-    int dev = 0;
-    CU(cudaGetDevice(&dev));
-    if (attr_dev != dev) {
-        CU(cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmemBytes));
-        attr_dev = dev;
-    }
-    static uint32_t* err_flag[64] = {nullptr};
-    if (dev < 64 && !err_flag[dev]) {
-        CU(cudaMalloc(&err_flag[dev], sizeof(uint32_t)));
-        CU(cudaMemset(err_flag[dev], 0, sizeof(uint32_t)));
-    }
+// Matrices up to this size take the direct-load kernel, larger ones the ring
+// kernel (the LM head: one CTA per SM streaming a contiguous row range).
+constexpr size_t kGemvDirectMaxBytes = (size_t)64 << 20;
+
+// y = bf16(W x) on `stream`; err = the error word the ring kernel reports into.
+static int gemv_launch(const void* W, const void* x, void* y, int n, int k, cudaStream_t stream, uint32_t* err, int dev) {
     int nsm = 0;
     CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-    const int grid = n < nsm ? n : nsm;
-    gemv_bf16_kernel<<<grid, kGemvThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
-                                                                                err_flag[dev < 64 ? dev : 0]);
+    if ((size_t)n * (size_t)k * 2 <= kGemvDirectMaxBytes) {
+        const int rows_cta = qb::gemv_direct_rows_cta(k), segs = qb::gemv_direct_segs(k);
+        const int groups = (n + rows_cta - 1) / rows_cta;
+        const int grid = std::min((groups + 1) / 2, nsm * 8);
+        qb::gemv_direct_kernel<<<grid, rows_cta * segs * 32, 0, stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k);
+    } else {
+        const int grid = n < nsm ? n : nsm;
+        gemv_bf16_kernel<<<grid, kGemvThreads, kGemvSmemBytes, stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k, err);
+    }
     CU(cudaGetLastError());
     return QWEN_OK;
+}
+
+static int gemv_check_args(const void* W, const void* x, const void* y, int n, int k) {
+    if (!W || !x || !y) return fail(QWEN_E_ARG, "NULL argument");
+    if (n <= 0 || k <= 0 || k % 256 != 0 || k > 4096) return fail(QWEN_E_ARG, "k must be a positive multiple of 256, <= 4096, and n > 0");
+    if (((uintptr_t)W | (uintptr_t)x) & 15) return fail(QWEN_E_ARG, "W and x must be 16-byte aligned");
+    return QWEN_OK;
+}
+
+// Reads and clears an error word after `stream` has synchronised.
+static int gemv_read_status(uint32_t* word, cudaStream_t stream, const char* who) {
+    CU(cudaStreamSynchronize(stream));
+    uint32_t e = 0;
+    CU(cudaMemcpy(&e, word, sizeof(e), cudaMemcpyDeviceToHost));
+    if (!e) return QWEN_OK;
+    CU(cudaMemset(word, 0, sizeof(e)));
+    return fail(QWEN_E_TIMEOUT, std::string(who) + ": a device wait expired (code " + std::to_string(e) + "); the output of a launch since "
+                                "the last status query is invalid");
+}
+
+// The allocating variant's error word, one per device, allocated and cleared
+// once under a lock.
+static std::atomic<uint32_t*> g_gemv_err[64];
+static std::mutex g_gemv_err_mu;
+
+static int gemv_err_word(int dev, uint32_t** out) {
+    uint32_t* w = g_gemv_err[dev].load();
+    if (!w) {
+        std::lock_guard<std::mutex> lk(g_gemv_err_mu);
+        w = g_gemv_err[dev].load();
+        if (!w) {
+            CU(cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmemBytes));
+            CU(cudaMalloc(&w, sizeof(uint32_t)));
+            CU(cudaMemset(w, 0, sizeof(uint32_t)));
+            g_gemv_err[dev].store(w);
+        }
+    }
+    *out = w;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_gemv_bf16(const void* W, const void* x, void* y, int n, int k, void* stream) {
+    int rc = gemv_check_args(W, x, y, n, k);
+    if (rc != QWEN_OK) return rc;
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(QWEN_E_ARG, "device index beyond 63");
+    uint32_t* err = nullptr;
+    if ((rc = gemv_err_word(dev, &err)) != QWEN_OK) return rc;
+    return gemv_launch(W, x, y, n, k, (cudaStream_t)stream, err, dev);
+}
+
+extern "C" int qwen_gemv_bf16_status(void* stream) {
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(QWEN_E_ARG, "device index beyond 63");
+    uint32_t* err = g_gemv_err[dev].load();
+    if (!err) { CU(cudaStreamSynchronize((cudaStream_t)stream)); return QWEN_OK; }   // no launch yet on this device
+    return gemv_read_status(err, (cudaStream_t)stream, "qwen_gemv_bf16");
 }
 
 // ---------------------------------------------------------------------------
@@ -1321,27 +1376,22 @@ extern "C" int qwen_row_topk(const float* logits, int rows, int n, int ld, int k
 // ---------------------------------------------------------------------------
 // isolated GEMV without allocation
 // ---------------------------------------------------------------------------
-// qwen_gemv_bf16 obtains its device scratch (the kernel's error word) with
-// cudaMalloc on its first call on each device.  Some callers cannot allow
+// qwen_gemv_bf16 obtains its device scratch (the ring kernel's error word)
+// with cudaMalloc on its first call on each device.  Some callers cannot allow
 // that: code that runs while a stream is being captured, or inside a framework
 // whose caching allocator already holds the device's memory.  This variant
 // keeps the scratch in a file-scope device array instead.  Host code must not
 // pass the array's name to a kernel (on the host it is only a stand-in for the
 // symbol); the device address comes from cudaGetSymbolAddress, once per
-// device, on the first call made with that device current.
+// device, on the first call made with that device current.  The word starts
+// at zero (static initialisation) and is cleared by
+// qwen_gemv_bf16_static_status, which reads it.
 constexpr int kGemvStaticScratchWords = 64;   // 256 bytes per device; the GEMV uses word 0
 static __device__ __align__(256) uint32_t g_gemv_static_scratch[kGemvStaticScratchWords];
 static std::atomic<uint32_t*> g_gemv_static_ptr[64];
 static std::mutex g_gemv_static_mu;
 
-extern "C" int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, void* stream) {
-    if (!W || !x || !y) return fail(QWEN_E_ARG, "NULL argument");
-    if (n <= 0 || k <= 0 || k % 256 != 0 || k > 4096)
-        return fail(QWEN_E_ARG, "qwen_gemv_bf16_static serves k a positive multiple of 256, at most 4096, and n > 0");
-    if (((uintptr_t)W | (uintptr_t)x) & 15) return fail(QWEN_E_ARG, "W and x must be 16-byte aligned");
-    int dev = 0;
-    CU(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(QWEN_E_ARG, "device index beyond 63");
+static int gemv_static_word(int dev, uint32_t** out) {
     uint32_t* scratch = g_gemv_static_ptr[dev].load();
     if (!scratch) {   // set-up, once per device, with that device current; allocates nothing
         std::lock_guard<std::mutex> lk(g_gemv_static_mu);
@@ -1354,13 +1404,27 @@ extern "C" int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int 
             g_gemv_static_ptr[dev].store(scratch);
         }
     }
-    int nsm = 0;
-    CU(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-    // the array keeps the previous call's contents: the error word must start at zero
-    CU(cudaMemsetAsync(scratch, 0, sizeof(uint32_t), (cudaStream_t)stream));
-    const int grid = n < nsm ? n : nsm;
-    gemv_bf16_kernel<<<grid, kGemvThreads, kGemvSmemBytes, (cudaStream_t)stream>>>((const uint16_t*)W, (const uint16_t*)x, (uint16_t*)y, n, k,
-                                                                                scratch);
-    CU(cudaGetLastError());
+    *out = scratch;
     return QWEN_OK;
+}
+
+extern "C" int qwen_gemv_bf16_static(const void* W, const void* x, void* y, int n, int k, void* stream) {
+    int rc = gemv_check_args(W, x, y, n, k);
+    if (rc != QWEN_OK) return fail(rc, std::string("qwen_gemv_bf16_static serves k a positive multiple of 256, at most 4096, and n > 0 "
+                                                   "(16-byte aligned W and x): ") + qwen_last_error());
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(QWEN_E_ARG, "device index beyond 63");
+    uint32_t* scratch = nullptr;
+    if ((rc = gemv_static_word(dev, &scratch)) != QWEN_OK) return rc;
+    return gemv_launch(W, x, y, n, k, (cudaStream_t)stream, scratch, dev);
+}
+
+extern "C" int qwen_gemv_bf16_static_status(void* stream) {
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(QWEN_E_ARG, "device index beyond 63");
+    uint32_t* scratch = g_gemv_static_ptr[dev].load();
+    if (!scratch) { CU(cudaStreamSynchronize((cudaStream_t)stream)); return QWEN_OK; }
+    return gemv_read_status(scratch, (cudaStream_t)stream, "qwen_gemv_bf16_static");
 }

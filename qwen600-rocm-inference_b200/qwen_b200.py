@@ -68,6 +68,8 @@ _SIGS = {
     "qwen_trace_read": (_c.c_int, [_P, _P, _c.c_int]),
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
+    "qwen_gemv_bf16_status": (_c.c_int, [_P]),
+    "qwen_gemv_bf16_static_status": (_c.c_int, [_P]),
     "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
     "qwen_set_prefill_mode": (_c.c_int, [_P, _c.c_int]),
     "qwen_row_topk": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P, _P, _P]),
@@ -189,6 +191,14 @@ def gemv_bf16(W_ptr, x_ptr, y_ptr, n, k, stream=0):
     """y = bf16(W x) on device pointers (ints)."""
     _check(load_library().qwen_gemv_bf16(ctypes.c_void_p(W_ptr), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr), n, k,
                                          ctypes.c_void_p(stream)))
+
+
+def gemv_status(stream=0, static=False):
+    """Synchronise `stream`; raise QwenError (QWEN_E_TIMEOUT) if a GEMV launch of
+    the chosen entry point since the last query had a device wait expire."""
+    lib = load_library()
+    f = lib.qwen_gemv_bf16_static_status if static else lib.qwen_gemv_bf16_status
+    _check(f(ctypes.c_void_p(stream)))
 
 
 def row_topk(logits_ptr, rows, n, ld, k, values_ptr, ids_ptr, stream=0):

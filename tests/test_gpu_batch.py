@@ -130,6 +130,39 @@ def test_batch_sampled_tokens_follow_reference_order(qb, O, checkpoint, T, p, k)
         b.close()
 
 
+@pytest.mark.parametrize("batch,slots", [(32, [0, 13, 31]), (128, [0, 77, 127])])
+def test_batch_greedy_at_scale_matches_single_sequences(qb, checkpoint, batch, slots):
+    """B = 32 and 128 at 1K context (the split-K / short-pass GEMM paths of
+    the benchmark's batched steps): the greedy streams of sample slots equal
+    the batch-1 engine's for the same prompts."""
+    sp, n_prompt, n_tokens = qb.Sampling(0.0, 1.0, 1), 1024, 6
+    prompts = [np.random.default_rng(7000 + s).integers(0, VOCAB, n_prompt).tolist() for s in range(batch)]
+    b = qb.Engine(checkpoint, 0)
+    try:
+        b.batch_init(batch)
+        toks = []
+        for slot, pr in enumerate(prompts):
+            b.batch_prefill(slot, pr[:-1])
+            toks.append(pr[-1])
+        pos = [n_prompt - 1] * batch
+        outs = [[] for _ in range(batch)]
+        for _ in range(n_tokens):
+            toks, _ = b.batch_step(toks, pos, sp)
+            for slot in range(batch):
+                outs[slot].append(toks[slot])
+            pos = [q + 1 for q in pos]
+    finally:
+        b.close()
+    for slot in slots:
+        one = qb.Engine(checkpoint, 0)
+        try:
+            one.prefill(prompts[slot][:-1], 0)
+            want, _ = one.generate(prompts[slot][-1], n_prompt - 1, n_tokens)
+        finally:
+            one.close()
+        assert outs[slot] == want, slot
+
+
 def test_batch_errors(qb, checkpoint):
     b = qb.Engine(checkpoint, 0)
     try:

@@ -180,8 +180,8 @@ def test_error_paths(engine, qb):
     assert code(engine.forward, VOCAB, 0) == -1
     assert code(engine.forward, 5, 8192) == -1
     assert code(engine.forward, 5, 10) == -7                 # skips cached positions
-    assert code(engine.decode_step, 5, 4, qb.Sampling(0.6, 0.9, 0)) == -6     # top_k 0 on device
-    assert code(engine.decode_step, 5, 4, qb.Sampling(0.6, 0.9, 65)) == -6
+    assert code(engine.decode_step, 5, 4, qb.Sampling(0.6, 0.9, -1)) == -1    # negative top_k
+    assert code(engine.decode_step, 5, 4, qb.Sampling(-0.5, 0.9, 5)) == -1    # negative temperature
     assert code(engine.generate, 5, 8190, 8) == -1
     # the handle still works after rejected calls
     t, _ = engine.decode_step(5, 4)
