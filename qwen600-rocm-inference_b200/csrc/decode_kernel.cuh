@@ -73,6 +73,7 @@ constexpr int kQKVRows = 2 * HEAD_DIM + 2 * HEAD_DIM;   // 512 rows per group
 constexpr int kCtrStride = 16;              // counters 64 B apart
 constexpr uint64_t kWaitNs = 2000000000ull; // 2 s
 constexpr int kNumCtr = 1;                  // the head's arrival counter
+constexpr int kHopStride = 16;              // hop counters 128 B apart
 // trace slots per CTA: 0 start; 1 + 10l + k for layer l:
 //   k = 0 x ready, 1 QKV done, 2 q/k/v ready, 3 ATT done, 4 partials ready,
 //   5 OPROJ done, 6 y ready, 7 MLP-A done, 8 h ready, 9 MLP-B done;
@@ -132,6 +133,11 @@ struct DecodeParams {
     uint64_t* partw;         // [L][8][kMaxGS][kPartStride]
     uint64_t* yw;            // [L][8][DIM]  O-projection partial of each group
     uint64_t* hw;            // [L][HIDDEN]  SwiGLU output
+    // fused-MLP layout (kFused): residual accumulators and arrival counters
+    const uint16_t* wdt[N_LAYERS];   // W_down transposed: [HIDDEN][DIM], row u = column u of W_down
+    float* xacc;             // [2][L+1][DIM]   x_l, accumulated with red.add (index [seq & 1])
+    float* macc;             // [2][L][DIM]     x_mid of layer l
+    unsigned long long* hop; // [2L+1][kHopStride]: arrivals at x_l (l = 1..L) and x_mid_l, monotone
     float* logits;           // [VOCAB]
     float* cand_v;           // [G][kMaxCand]
     int* cand_i;             // [G][kMaxCand]
@@ -189,7 +195,9 @@ struct __align__(16) DecodeSmem {
     int ai[kNCW];
     float tv[kMaxCand];      // merged top-K (head)
     int ti[kMaxCand];
+    float hl[kMaxMlpRows];   // fused MLP: this CTA's SwiGLU outputs
     int flag;
+    int hfail;               // a hop-counter wait gave up: every consumer stops waiting
     int abort;               // set after a ring wait expired: stop waiting on the ring
     unsigned int copied;     // chunks the producer has issued (read by the prefetch warp)
     Plan pl;                 // this CTA's share of every stage (one copy, in shared memory)
@@ -267,6 +275,7 @@ constexpr int kWoCols = 256 + kPad / 2;                    // packed Wo row, pad
 constexpr int kStrideWo = 2 * kWoCols;                     // 528 B
 constexpr int kRowsWo = kSlotBytes / kStrideWo;            // 62 rows per chunk
 constexpr int kRowsLM = kSlotBytes / (2 * DIM);            // 16 LM-head rows per chunk (unpadded: FFMA path)
+constexpr int kRowsWdT = kSlotBytes / (2 * DIM);           // 16 rows of W_down^T (2 KB each) per chunk
 constexpr int kKVChunk = 64;                               // positions per K|V chunk
 constexpr int kVOff = kKVChunk * 2 * HEAD_DIM;             // V offset in a K|V chunk
 static_assert(2 * kUnitsGU * kStride1024 <= kSlotBytes && kRowsWd * kStrideWd <= kSlotBytes, "chunks fit a slot");
@@ -300,6 +309,7 @@ struct Seg {            // `rows` copies of `bytes` each: source rows src_stride
 struct ChunkIter {
     int l = 0, st = 0, r = 0;
     int cur_st = 0, cur_l = 0;   // stage and layer of the chunk last returned
+    bool fused = false;          // stage 7 streams W_down^T rows of this CTA's hidden units instead of W_down rows
     // Fills seg[] with the next chunk's copies; returns their count (0 at the end).
     __device__ int next(const DecodeParams& P, const Plan& pl, Seg* seg) {
         for (;;) {
@@ -359,10 +369,17 @@ struct ChunkIter {
                     r += n;
                     return 2;
                 }
-                st = 7; r = pl.da;
+                st = 7; r = fused ? pl.ha : pl.da;
                 break;
             case 7:
-                if (r < pl.db) {
+                if (fused) {
+                    if (r < pl.hb) {
+                        const int n = min(kRowsWdT, pl.hb - r);
+                        seg[0] = {(const uint8_t*)(P.wdt[l] + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0, 1, 0, 0};
+                        r += n;
+                        return 1;
+                    }
+                } else if (r < pl.db) {
                     const int n = min(kRowsWd, pl.db - r);
                     seg[0] = {(const uint8_t*)(P.wd[l] + (size_t)r * HIDDEN_DIM), (uint32_t)(2 * HIDDEN_DIM), 0, (uint32_t)n,
                               (uint32_t)(2 * HIDDEN_DIM), (uint32_t)kStrideWd};
@@ -394,11 +411,12 @@ struct ChunkIter {
 // P.prefetch_chunks chunks ahead of the producer; it keeps HBM streaming while
 // the ring is full because consumers wait on another CTA.
 // ---------------------------------------------------------------------------
-template <bool kTr>
+template <bool kTr, bool kFused>
 __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, const Plan& pl) {
     const uint64_t pol = policy_evict_first();
     unsigned long long* tr = (kTr && P.trace) ? P.trace + (size_t)c * kTraceStride : nullptr;
     ChunkIter it;
+    it.fused = kFused;
     Seg seg[3];
     uint32_t k = 0;
     int k13 = -1, last_l = -1;
@@ -435,8 +453,9 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
     P.chunk_count[2 * c] = (int)k;
 }
 
-__device__ __noinline__ void decode_prefetcher(const DecodeParams& P, DecodeSmem* S, const Plan& pl) {
+__device__ __noinline__ void decode_prefetcher(const DecodeParams& P, DecodeSmem* S, const Plan& pl, bool fused) {
     ChunkIter it;
+    it.fused = fused;
     Seg seg[3];
     uint32_t npf = 0;
     const uint32_t lead = (uint32_t)P.prefetch_chunks;
@@ -542,6 +561,39 @@ struct Consumer {
         }
         #pragma unroll
         for (int i = 0; i < 2 * N; i++) v[i] = 0.f;   // after an error the values are never used for a result
+    }
+    // ---- global hops of the fused layout ----
+    // The CTA's red.add contributions to a hop precede this call: one block
+    // barrier orders them before thread 0's release add on the counter.
+    __device__ __forceinline__ void hop_arrive(unsigned long long* ctr) {
+        bar();
+        if (tid == 0) red_release_add_u64(ctr, 1ull);
+    }
+    // Waits until the counter reaches `target` (every CTA arrived for this
+    // launch: the counters only grow, G per launch).  Thread 0 polls with
+    // acquire loads, bounded by kWaitNs; the block barrier after it hands the
+    // outcome to every consumer thread.
+    __device__ __forceinline__ void hop_wait(const unsigned long long* ctr, unsigned long long target, int where) {
+        if (tid == 0 && !failed && !*(volatile int*)&S->hfail) {
+            if (ld_acquire_u64(ctr) < target) {
+                const uint64_t t0 = global_ns();
+                uint32_t it = 0;
+                while (ld_acquire_u64(ctr) < target) {
+                    if ((++it & 31u) == 0) {
+                        if (ld_volatile(&P->out->err)) { S->hfail = 1; break; }
+                        if (global_ns() - t0 > kWaitNs) {
+                            atomicOr(&P->out->err, 1u);
+                            atomicExch(&P->out->err_where, where);
+                            S->hfail = 1;
+                            break;
+                        }
+                    }
+                }
+                if (kTr && tr) xw_ns += global_ns() - t0;
+            }
+        }
+        bar();
+        if (*(volatile int*)&S->hfail) failed = true;
     }
     // Sum over the 512 consumer threads.  One barrier: consecutive calls use
     // alternate buffers, and a call's buffer is not written again before every
@@ -715,7 +767,7 @@ struct Consumer {
     }
 };
 
-template <bool kTr>
+template <bool kTr, bool kFused>
 __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, int G, const Plan& pl,
                                              int token, int pos, int flags, uint32_t seq) {
     Consumer<kTr> C;
@@ -733,6 +785,22 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
     QB_TRACE(0);
 
     if (tid < HEAD_DIM) S->rope[tid] = __ldg(P.rope + (size_t)pos * HEAD_DIM + tid);
+    // fused layout: this launch accumulates into the buffers of parity seq & 1
+    // (cleared by the previous launch) and clears its share of the other
+    // parity's for the next launch; the hop counters reach G * seq.
+    const uint32_t par = seq & 1u;
+    const unsigned long long hop_target = (unsigned long long)G * seq;
+    constexpr int kAccPer = (2 * N_LAYERS + 1) * DIM;   // floats per parity: x_1..x_L (+ unused x_0), x_mid_0..L-1
+    float* const xacc = P.xacc + (size_t)par * (N_LAYERS + 1) * DIM;
+    float* const macc = P.macc + (size_t)par * N_LAYERS * DIM;
+    if constexpr (kFused) {
+        float* const xq = P.xacc + (size_t)(par ^ 1u) * (N_LAYERS + 1) * DIM;
+        float* const mq = P.macc + (size_t)(par ^ 1u) * N_LAYERS * DIM;
+        for (int i = c * kNCT + tid; i < kAccPer; i += G * kNCT) {
+            if (i < (N_LAYERS + 1) * DIM) xq[i] = 0.f;
+            else mq[i - (N_LAYERS + 1) * DIM] = 0.f;
+        }
+    }
 
     for (int l = 0; l < N_LAYERS; l++) {
         const int TB = 1 + 10 * l;
@@ -746,6 +814,10 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             if (l == 0) {
                 const uint32_t w = __ldg((const uint32_t*)(P.embed + (size_t)token * DIM + j));
                 xv[0] = bf_lo(w); xv[1] = bf_hi(w);
+            } else if constexpr (kFused) {
+                C.hop_wait(P.hop + (size_t)(l - 1) * kHopStride, hop_target, 10 * l);
+                const float2 v = ld_relaxed_f2(xacc + (size_t)l * DIM + j);
+                xv[0] = v.x; xv[1] = v.y;
             } else {
                 const uint64_t* p = P.xw + (size_t)l * DIM + j;
                 C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
@@ -960,10 +1032,14 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 if (tid < cnt) {                  // row tid: tile tt, summed over warps tt, tt+4, tt+8, tt+12
                     const int tt = tid >> 4, ri = tid & 15;
                     const float v = ((red[tt * 32 + ri] + red[(tt + 4) * 32 + ri]) + red[(tt + 8) * 32 + ri]) + red[(tt + 12) * 32 + ri];
-                    xw_store(y + r + tid, v, seq);
+                    if constexpr (kFused)   // x_mid = x_l + sum over the 8 groups; group 0 adds the residual
+                        red_add_f32(macc + (size_t)l * DIM + r + tid, g == 0 ? v + S->xres[r + tid] : v);
+                    else
+                        xw_store(y + r + tid, v, seq);
                 }
                 QB_SUB(14);
             }
+            if constexpr (kFused) C.hop_arrive(P.hop + (size_t)(N_LAYERS + l) * kHopStride);
         }
         QB_TRACE(TB + 5);
 
@@ -974,7 +1050,12 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             const uint64_t* yb = P.yw + (size_t)l * kGroups * DIM + j;
             QB_SUB(16);
             float x0 = S->xres[j], x1 = S->xres[j + 1];
-            {
+            if constexpr (kFused) {
+                (void)yb;
+                C.hop_wait(P.hop + (size_t)(N_LAYERS + l) * kHopStride, hop_target, 10 * l + 6);
+                const float2 v = ld_relaxed_f2(macc + (size_t)l * DIM + j);
+                x0 = v.x; x1 = v.y;
+            } else {
                 float yv[2 * kGroups];
                 C.template gather<kGroups>([&](int gg) { return yb + (size_t)gg * DIM; }, (1u << kGroups) - 1u, yv, 10 * l + 6);
                 #pragma unroll
@@ -1012,7 +1093,9 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                     #pragma unroll
                     for (int w = 0; w < kNCW; w++) { gt += red[w * 32 + 16 * t + uu]; up += red[w * 32 + 16 * t + kUnitsGU + uu]; }
                     gt *= rn; up *= rn;
-                    xw_store(hw + u + tid, (gt / (1.0f + expf(-gt))) * up, seq);
+                    const float h = (gt / (1.0f + expf(-gt))) * up;
+                    if constexpr (kFused) S->hl[u + tid - pl.ha] = h;
+                    else xw_store(hw + u + tid, h, seq);
                 }
             }
             QB_SUB(22);
@@ -1021,46 +1104,75 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         QB_SUB(35);
 
         // ---------------- MLP-B ----------------
-        {
-            const uint64_t* hb = P.hw + (size_t)l * HIDDEN_DIM + 2 * tid;
-            constexpr int kHP = HIDDEN_DIM / (2 * kNCT);
-            float hv[2 * kHP];
-            QB_SUB(25);
-            C.template gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
-            #pragma unroll
-            for (int i = 0; i < kHP; i++) C.put_pair(&S->w.bh[0][0][0], 2 * tid + 2 * kNCT * i, hv[2 * i], hv[2 * i + 1]);
-        }
-        C.bar();
-        QB_TRACE(TB + 8);
-        {
-            // rows of Wd, two chunks (8 rows) per round as one tile: tile rows
-            // 0..3 = chunk 0, 4..7 = chunk 1; warp w takes k-tiles 12w..12w+11
-            uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
-            const int lr = lane & 15;
-            for (int r = pl.da; r < pl.db; r += 2 * kRowsWd) {
-                const int n = min(2 * kRowsWd, pl.db - r);
-                const uint32_t nc = n > kRowsWd ? 2 : 1;
-                const uint8_t* c0 = C.chunk(0);
-                const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
-                QB_SUB(28);
-                const uint8_t* rp = lr < n ? (lr < kRowsWd ? c0 + (size_t)lr * kStrideWd : c1 + (size_t)(lr - kRowsWd) * kStrideWd) : c0;
-                uint32_t ta[1] = {smem_addr(rp) + (lane >> 4) * 16};
-                float d[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-                C.template mma_tiles<1>(ta, &S->w.bh[0][0][0], 12 * warp, HIDDEN_DIM / 16 / kNCW, d);
-                float* red = C.next_red();
-                C.put_red(red, 0, d[0]);
-                C.release(nc);
-                C.bar();
-                QB_SUB(30);
-                if (tid < n) {
-                    float v = 0.f;
-                    #pragma unroll
-                    for (int w = 0; w < kNCW; w++) v += red[w * 32 + tid];
-                    xw_store(xn + r + tid, S->xres[r + tid] + v, seq);
+        if constexpr (kFused) {
+            // x_{l+1} = x_mid + W_down h: this CTA's hidden units u in [ha, hb)
+            // times their columns of W_down (rows of W_down^T, 16 per chunk);
+            // thread t owns outputs 2t, 2t+1.  The partial vectors of all CTAs
+            // add up at L2 (red.add); each CTA adds x_mid for its rows [da, db).
+            C.bar();     // S->hl complete
+            QB_TRACE(TB + 8);
+            float a0 = 0.f, a1 = 0.f;
+            for (int u = pl.ha; u < pl.hb; u += kRowsWdT) {
+                const int n = min(kRowsWdT, pl.hb - u);
+                const uint8_t* ch = C.chunk(0);
+                const float* hs = &S->hl[u - pl.ha];
+                #pragma unroll 4
+                for (int i = 0; i < n; i++) {
+                    const uint32_t w = *(const uint32_t*)(ch + (size_t)i * 2 * DIM + 4 * tid);
+                    const float h = hs[i];
+                    a0 = fmaf(bf_lo(w), h, a0);
+                    a1 = fmaf(bf_hi(w), h, a1);
+                }
+                C.release(1);
+            }
+            const int j = 2 * tid;
+            if (j >= pl.da && j < pl.db) a0 += S->xres[j];
+            if (j + 1 >= pl.da && j + 1 < pl.db) a1 += S->xres[j + 1];
+            const float b0 = __shfl_down_sync(0xffffffffu, a0, 1), b1 = __shfl_down_sync(0xffffffffu, a1, 1);
+            if ((tid & 1) == 0) red_add_v4_f32(xacc + (size_t)(l + 1) * DIM + j, a0, a1, b0, b1);
+            C.hop_arrive(P.hop + (size_t)l * kHopStride);   // also the barrier before S->xres / S->hl are reused
+        } else {
+            {
+                const uint64_t* hb = P.hw + (size_t)l * HIDDEN_DIM + 2 * tid;
+                constexpr int kHP = HIDDEN_DIM / (2 * kNCT);
+                float hv[2 * kHP];
+                QB_SUB(25);
+                C.template gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
+                #pragma unroll
+                for (int i = 0; i < kHP; i++) C.put_pair(&S->w.bh[0][0][0], 2 * tid + 2 * kNCT * i, hv[2 * i], hv[2 * i + 1]);
+            }
+            C.bar();
+            QB_TRACE(TB + 8);
+            {
+                // rows of Wd, two chunks (8 rows) per round as one tile: tile rows
+                // 0..3 = chunk 0, 4..7 = chunk 1; warp w takes k-tiles 12w..12w+11
+                uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
+                const int lr = lane & 15;
+                for (int r = pl.da; r < pl.db; r += 2 * kRowsWd) {
+                    const int n = min(2 * kRowsWd, pl.db - r);
+                    const uint32_t nc = n > kRowsWd ? 2 : 1;
+                    const uint8_t* c0 = C.chunk(0);
+                    const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
+                    QB_SUB(28);
+                    const uint8_t* rp = lr < n ? (lr < kRowsWd ? c0 + (size_t)lr * kStrideWd : c1 + (size_t)(lr - kRowsWd) * kStrideWd) : c0;
+                    uint32_t ta[1] = {smem_addr(rp) + (lane >> 4) * 16};
+                    float d[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+                    C.template mma_tiles<1>(ta, &S->w.bh[0][0][0], 12 * warp, HIDDEN_DIM / 16 / kNCW, d);
+                    float* red = C.next_red();
+                    C.put_red(red, 0, d[0]);
+                    C.release(nc);
+                    C.bar();
+                    QB_SUB(30);
+                    if (tid < n) {
+                        float v = 0.f;
+                        #pragma unroll
+                        for (int w = 0; w < kNCW; w++) v += red[w * 32 + tid];
+                        xw_store(xn + r + tid, S->xres[r + tid] + v, seq);
+                    }
                 }
             }
+            C.bar();     // S->w.bh and S->xres are reused by the next layer
         }
-        C.bar();     // S->w.bh and S->xres are reused by the next layer
         QB_TRACE(TB + 9);
         QB_SUB(36);
     }
@@ -1076,9 +1188,15 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         float ss, x0, x1;
         {
             const int j = tid * 2;
-            const uint64_t* p = P.xw + (size_t)N_LAYERS * DIM + j;
             float xv[2];
-            C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
+            if constexpr (kFused) {
+                C.hop_wait(P.hop + (size_t)(N_LAYERS - 1) * kHopStride, hop_target, 10 * N_LAYERS);
+                const float2 v = ld_relaxed_f2(xacc + (size_t)N_LAYERS * DIM + j);
+                xv[0] = v.x; xv[1] = v.y;
+            } else {
+                const uint64_t* p = P.xw + (size_t)N_LAYERS * DIM + j;
+                C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
+            }
             x0 = xv[0]; x1 = xv[1];
             ss = C.block_sum(x0 * x0 + x1 * x1);
         }
@@ -1220,7 +1338,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 
 // kTr: the tracing build (stage time stamps into P.trace); the other build has
 // no trace code at all.
-template <bool kTr>
+template <bool kTr, bool kFused>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
@@ -1229,6 +1347,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (tid == 0) {
         for (int s = 0; s < kSlots; s++) { mbar_init(&S->full[s], 1); mbar_init(&S->empty[s], kNCW); }
         S->abort = 0;
+        S->hfail = 0;
         S->copied = 0;
         fence_barrier_init();
     }
@@ -1246,14 +1365,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     __syncthreads();
     const Plan& pl = S->pl;
     if ((tid >> 5) == kNCW) {
-        if ((tid & 31) == 0) decode_producer<kTr>(P, ring, S, c, pl);
+        if ((tid & 31) == 0) decode_producer<kTr, kFused>(P, ring, S, c, pl);
         return;
     }
     if ((tid >> 5) == kNCW + 1) {
-        if ((tid & 31) == 0) decode_prefetcher(P, S, pl);
+        if ((tid & 31) == 0) decode_prefetcher(P, S, pl, kFused);
         return;
     }
-    decode_consumer<kTr>(P, ring, S, c, G, pl, token, pos, flags, seq);
+    decode_consumer<kTr, kFused>(P, ring, S, c, G, pl, token, pos, flags, seq);
 }
 
 }  // namespace qb

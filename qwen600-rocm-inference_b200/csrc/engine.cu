@@ -164,6 +164,17 @@ __global__ void pack_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __rest
     }
 }
 
+// One layer's W_down [DIM][HIDDEN] -> W_down^T [HIDDEN][DIM]: row u holds the
+// column of hidden unit u, so the decode kernel's fused MLP streams a CTA's
+// units as contiguous 2 KB rows.  32 x 32 tiles through shared memory.
+__global__ void transpose_wd_kernel(const uint16_t* __restrict__ wd, uint16_t* __restrict__ wdt) {
+    __shared__ uint16_t t[32][33];
+    const int u0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) t[i][threadIdx.x] = wd[(size_t)(r0 + i) * HIDDEN_DIM + u0 + threadIdx.x];
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) wdt[(size_t)(u0 + i) * DIM + r0 + threadIdx.x] = t[threadIdx.x][i];
+}
+
 // gate and up rows interleaved in blocks of 128 (block 2j: gate rows 128j ..,
 // block 2j+1: the same up rows), so one 128 x 256 GEMM tile holds both halves
 // of 128 hidden units and its epilogue can apply SwiGLU.
@@ -237,6 +248,8 @@ struct qwen_ctx {
     uint16_t* pf_as = nullptr;
     uint16_t* pf_hs = nullptr;   // SwiGLU output in three bf16 parts (written by the fused gate|up GEMM)
     uint16_t* wgu = nullptr;     // gate|up weights interleaved per 128 rows, all layers
+    uint16_t* wdt = nullptr;     // W_down transposed, all layers (the decode kernel's fused MLP)
+    bool fused = false;          // decode layout: fused MLP with accumulated hops (false: tagged exchange words)
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int last_k = 0;
@@ -247,7 +260,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->wdt, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -296,7 +309,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         (HIDDEN_DIM + c->nsm - 1) / c->nsm > kMaxMlpRows) {
         ctx_free(c); return fail(QWEN_E_UNSUPPORTED, "unsupported SM count " + std::to_string(c->nsm));
     }
-    for (auto kern : {decode_kernel<false>, decode_kernel<true>}) {
+    for (auto kern : {decode_kernel<false, false>, decode_kernel<true, false>, decode_kernel<false, true>, decode_kernel<true, true>}) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemBytes) != cudaSuccess) {
             ctx_free(c); return fail(QWEN_E_CUDA, "cannot reserve " + std::to_string(kDecodeSmemBytes) + " B of shared memory");
         }
@@ -312,6 +325,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     TRY(upload_checkpoint(path, m, c->wblock, c->stream));
     TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * kGroups * DIM * kWoCols));
     TRY(dalloc(&c->wgu, (size_t)N_LAYERS * 2 * HIDDEN_DIM * DIM));
+    TRY(dalloc(&c->wdt, (size_t)N_LAYERS * HIDDEN_DIM * DIM));
     const size_t kv = (size_t)N_LAYERS * N_KV_HEADS * SEQ_LEN * HEAD_DIM;
     TRY(dalloc(&c->kc, kv));
     TRY(dalloc(&c->vc, kv));
@@ -319,7 +333,10 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     const size_t n_xw = (size_t)(N_LAYERS + 1) * DIM, n_qkv = (size_t)N_LAYERS * 4096,
                  n_part = (size_t)N_LAYERS * kGroups * kMaxGS * kPartStride, n_y = (size_t)N_LAYERS * kGroups * DIM,
                  n_h = (size_t)N_LAYERS * HIDDEN_DIM;
-    c->xchg_words = n_xw + n_qkv + n_part + n_y + n_h;
+    // fused layout: fp32 accumulators of both parities (2 x (2L + 1) x DIM floats,
+    // as 64-bit words) and the hop counters, zeroed with the exchange words
+    const size_t n_acc = (size_t)(2 * N_LAYERS + 1) * DIM, n_hop = (size_t)(2 * N_LAYERS + 1) * kHopStride;
+    c->xchg_words = n_xw + n_qkv + n_part + n_y + n_h + n_acc + n_hop;
     TRY(dalloc(&c->xchg, c->xchg_words));
     TRY(dalloc(&c->logits, (size_t)VOCAB_SIZE));
     TRY(dalloc(&c->cand_v, (size_t)c->nsm * kMaxCand));
@@ -360,11 +377,16 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         P.wg[l] = W(li.gate); P.wu[l] = W(li.up); P.wd[l] = W(li.down);
         pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * kGroups * DIM * kWoCols);
         pack_gu_kernel<<<1024, 256, 0, c->stream>>>(W(li.gate), W(li.up), c->wgu + (size_t)l * 2 * HIDDEN_DIM * DIM);
+        transpose_wd_kernel<<<dim3(HIDDEN_DIM / 32, DIM / 32), dim3(32, 8), 0, c->stream>>>(W(li.down), c->wdt + (size_t)l * HIDDEN_DIM * DIM);
+        P.wdt[l] = c->wdt + (size_t)l * HIDDEN_DIM * DIM;
         c->wo_raw[l] = W(li.o_proj);
     }
     if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
     P.wo_g = c->wo_g; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
     P.xw = c->xchg; P.qkvw = P.xw + n_xw; P.partw = P.qkvw + n_qkv; P.yw = P.partw + n_part; P.hw = P.yw + n_y;
+    P.xacc = reinterpret_cast<float*>(P.hw + n_h);
+    P.macc = P.xacc + 2 * (size_t)(N_LAYERS + 1) * DIM;
+    P.hop = reinterpret_cast<unsigned long long*>(P.hw + n_h + n_acc);
     P.logits = c->logits;
     P.cand_v = c->cand_v; P.cand_i = c->cand_i; P.top_v = c->top_v; P.top_i = c->top_i; P.ctr = c->ctr;
     P.in = c->d_in; P.out = c->d_out; P.tokens_out = c->tokens; P.tokens_cap = SEQ_LEN;
@@ -375,6 +397,9 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     P.poll_ns = 0;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
+    // decode layout: "fused" (the fused MLP with accumulated hops, four per
+    // layer) or "tagged" (exchange words, five hops per layer)
+    if (const char* e = getenv("QWEN_B200_DECODE_LAYOUT")) c->fused = strcmp(e, "fused") == 0;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -409,8 +434,13 @@ static int enqueue_decode(qwen_t* c) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true>, c->params));
-    else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false>, c->params));
+    if (c->fused) {
+        if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true, true>, c->params));
+        else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false, true>, c->params));
+    } else {
+        if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true, false>, c->params));
+        else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false, false>, c->params));
+    }
     return QWEN_OK;
 }
 
@@ -1038,6 +1068,14 @@ extern "C" int qwen_debug_read(qwen_t* c, float* resid, float* qkv) {
         return QWEN_OK;
     };
     int rc = QWEN_OK;
+    if (resid && c->fused) {   // x_1 .. x_L of the last launch (parity of its sequence number)
+        StepOut o{};
+        CU(cudaMemcpy(&o, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost));
+        const uint32_t par = (o.seq - 1u) & 1u;
+        CU(cudaMemcpy(resid, c->params.xacc + ((size_t)par * (N_LAYERS + 1) + 1) * DIM, (size_t)N_LAYERS * DIM * sizeof(float),
+                      cudaMemcpyDeviceToHost));
+        resid = nullptr;
+    }
     if (resid) rc = take(c->params.xw + DIM, (size_t)N_LAYERS * DIM, resid);       // residual after layer l = x_{l+1}
     if (rc == QWEN_OK && qkv) rc = take(c->params.qkvw, (size_t)N_LAYERS * 4096, qkv);
     return rc;

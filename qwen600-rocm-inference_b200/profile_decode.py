@@ -12,7 +12,9 @@ for N >= 65
 
     ncu --set full --clock-control none -k regex:decode_kernel -s 2 -c 1 ...
 
-captures the second decode step: position N + 1, context N + 2.
+captures the second decode step: position N + 1, context N + 2.  After the
+K host-timed steps it re-decodes the same positions as K chained launches and
+prints their device time per step.
 
 With --batch B it profiles batched decode instead: B slots, each prefilled
 with its own seeded N-token prompt (qwen_batch_prefill), then K greedy
@@ -62,8 +64,11 @@ def main():
     for pos in range(a.prompt, a.prompt + a.steps):
         tok, _ = eng.decode_step(tok, pos)
     dt = time.perf_counter() - t0
+    # the same positions again as chained launches, timed on the device (CUDA events)
+    _, _, ms = eng.generate_timed(prompt[-1], a.prompt, a.steps)
     eng.close()
-    print(f"prompt {a.prompt} steps {a.steps}: {dt / max(a.steps, 1) * 1e6:.1f} us per step (host wall time)")
+    print(f"prompt {a.prompt} steps {a.steps}: {dt / max(a.steps, 1) * 1e6:.1f} us per step (host wall time), "
+          f"{ms * 1e3 / max(a.steps, 1):.1f} us per step (device time of chained launches)")
 
 
 if __name__ == "__main__":
