@@ -183,39 +183,43 @@ def ref_cuda_rate(ck, n_prompt=768, n_timed=200):
 GEMV_SHAPES = [(1024, 4096), (2048, 1024), (1024, 6144), (3072, 1024), (1024, 151936)]   # (K, N)
 
 
-def gemv_sweep(qb, peak):
+def gemv_sweep(qb, peak, reps=64):
     """Isolated bf16 GEMV y = bf16(W x) through qwen_gemv_bf16 at the decode
     chain's shapes: x ~ N(0,1), W ~ N(0,0.02) from a seed, fp32 accumulate, bf16
-    out.  Each timed launch is bracketed alone by CUDA events on the launching
-    stream, with a 256 MB write between launches to flush the 126 MB L2; the
-    reported time is the median of 20."""
+    out.  `reps` launches back to back, bracketed once by CUDA events on the
+    launching stream, each on the next of enough copies of W that together
+    exceed twice the 126 MB L2 (every launch reads its W from HBM; no flush
+    kernel between launches, so the host's launch latency stays hidden behind
+    the queued work); the reported time is total / reps, median of 5 such runs."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(0)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     out = []
     for k, n in GEMV_SHAPES:
-        W = (torch.randn(n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        nbytes_w = n * k * 2
+        copies = max(1, -(-(256 << 20) // nbytes_w))
+        W = [(torch.randn(n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
         x = torch.randn(k, generator=g, device="cuda").to(torch.bfloat16)
         y = torch.empty(n, dtype=torch.bfloat16, device="cuda")
-        call = lambda: qb.gemv_bf16(W.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, stream.cuda_stream)
-        for _ in range(3):
-            call()
+        ptrs = [w.data_ptr() for w in W]
+        call = lambda i: qb.gemv_bf16(ptrs[i % copies], x.data_ptr(), y.data_ptr(), n, k, stream.cuda_stream)
+        for i in range(copies + 3):
+            call(i)
         ts = []
-        for _ in range(20):
-            flush.fill_(1)
+        for _ in range(5):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            call()
+            for i in range(reps):
+                call(i)
             e1.record(stream)
             e1.synchronize()
-            ts.append(e0.elapsed_time(e1) * 1e3)
+            ts.append(e0.elapsed_time(e1) * 1e3 / reps)
+        qb.gemv_status(stream.cuda_stream)
         us = float(np.median(ts))
         nbytes = n * k * 2 + k * 2 + n * 2
         out.append({"k": k, "n": n, "bytes": nbytes, "us": us, "gbs": nbytes / (us * 1e-6) / 1e9,
-                    "frac": nbytes / (us * 1e-6) / 1e9 / peak})
+                    "frac": nbytes / (us * 1e-6) / 1e9 / peak, "copies_of_w": copies})
         del W, x, y
-    del flush
     torch.cuda.empty_cache()
     return out
 
@@ -488,7 +492,7 @@ def run_mine(args):
                 torch.cuda.empty_cache()
 
             extra("gemv_sweep", lambda: {"shapes": gemv_sweep(qb, peak), "peak_gbs": peak,
-                                         "l2": "flushed (256 MB write) between timed launches"})
+                                         "l2": "inputs larger than L2: 64 launches rotate over copies of W totalling >= 256 MB"})
             bf16_peak = measured_bf16_peak()
             extra("gemm_sweep", lambda: {"shapes": gemm_sweep(qb, bf16_peak), "peak_tflops": bf16_peak,
                                          "peak_source": "bf16_tflops (burst, MEASURED_PEAKS.json)",

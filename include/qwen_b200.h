@@ -159,6 +159,14 @@ int qwen_prefill(qwen_t* ctx, const int* tokens, int n, int pos0, float* logits_
  * (the reference runs forward() per prompt token, main.cu:141-145). */
 int qwen_set_prefill_mode(qwen_t* ctx, int gemm);
 
+/* Precision of the tensor-core passes (qwen_prefill's long prompts and the
+ * batched steps): each fp32 activation enters the bf16 GEMMs as `parts` bf16
+ * terms (hi + mid + lo).  3 (the default) reproduces the fp32 product to fp32
+ * precision; 2 keeps 16 mantissa bits of each activation (relative error
+ * <= 2^-17) for two thirds of the tensor work; 1 is plain bf16 activations.
+ * No reference counterpart (the reference has no prompt pass). */
+int qwen_set_prefill_parts(qwen_t* ctx, int parts);
+
 /* Number of positions currently held in the KV cache. */
 int qwen_cached_positions(const qwen_t* ctx);
 

@@ -252,6 +252,7 @@ struct qwen_ctx {
     bool fused = false;          // decode layout: fused MLP with accumulated hops (false: tagged exchange words)
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
+    int pf_parts = 3;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
     int last_k = 0;
 };
 
@@ -668,7 +669,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
 }
 
 static int gemm_check(qwen_t* c);
-static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st);
+static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st, int parts);
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
                    cudaStream_t st, int split_cols = 0, int* splits_used = nullptr, int m_valid = 0);
@@ -734,7 +735,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, m);
         int sp_q = 1, sp_gu = 1;
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, 3 * DIM, DIM,
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, c->pf_parts * DIM, DIM,
                           true, st, kLdQKV, &sp_q, m)) != QWEN_OK)
             return rc;
         qkv_post_kernel<<<m * 4, 256, 0, st>>>(c->pf_y, ld_qkv, sp_q, kLdQKV, m, m, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
@@ -749,7 +750,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
             attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_as,
                                                                                                        kLdAs);
         }
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, 3 * Q_DIM, Q_DIM, true, st, DIM, &sp_o, m)) !=
+        if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, c->pf_parts * Q_DIM, Q_DIM, true, st, DIM, &sp_o, m)) !=
             QWEN_OK)
             return rc;
         norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m);
@@ -758,15 +759,15 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         const bool fused = (2 * HIDDEN_DIM / 256) * (rows / tc::kBM) >= c->nsm;
         uint16_t* hs = fused ? c->pf_hs : c->pf_as;
         if (fused) {
-            if ((rc = gemm_swiglu(c->pf_as, kLdAs, c->wgu + (size_t)l * 2 * HIDDEN_DIM * DIM, c->pf_hs, kLdAs, rows, m, st)) != QWEN_OK)
+            if ((rc = gemm_swiglu(c->pf_as, kLdAs, c->wgu + (size_t)l * 2 * HIDDEN_DIM * DIM, c->pf_hs, kLdAs, rows, m, st, c->pf_parts)) != QWEN_OK)
                 return rc;
         } else {
-            if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, 3 * DIM, DIM, true,
+            if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, c->pf_parts * DIM, DIM, true,
                               st, kLdY, &sp_gu, m)) != QWEN_OK)
                 return rc;
             swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m);
         }
-        if ((rc = gemm_tc(hs, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, 3 * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
+        if ((rc = gemm_tc(hs, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, c->pf_parts * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
                           &sp_d, m)) != QWEN_OK)
             return rc;
     }
@@ -1012,6 +1013,15 @@ extern "C" int qwen_batch_read_logits(qwen_t* c, int rows, float* logits_host) {
     CU(cudaSetDevice(c->device));
     CU(cudaMemcpyAsync(logits_host, c->b_logits, (size_t)rows * VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     CU(cudaStreamSynchronize(c->stream));
+    return QWEN_OK;
+}
+
+extern "C" int qwen_set_prefill_parts(qwen_t* c, int parts) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (parts < 1 || parts > 3) return fail(QWEN_E_ARG, "parts must be 1, 2 or 3");
+    c->pf_parts = parts;
+    for (auto& kv : c->b_graphs) cudaGraphExecDestroy(kv.second);   // captured batch steps hold the old K
+    c->b_graphs.clear();
     return QWEN_OK;
 }
 
@@ -1300,7 +1310,7 @@ static int gemm_prepare(int dev) {
 // parts) against the interleaved gate|up weights wgu [2 HIDDEN_DIM][DIM];
 // writes h = silu(gate) * up as three bf16 parts into Hs (rows ld_hs apart,
 // parts HIDDEN_DIM apart).  Rows m_valid .. M-1 are not written.
-static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st) {
+static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st, int parts) {
     int dev = 0;
     CU(cudaGetDevice(&dev));
     if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
@@ -1313,7 +1323,7 @@ static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     bm.map[1] = bm.map[2] = bm.map[0];
     bm.end[0] = bm.end[1] = bm.end[2] = 2 * HIDDEN_DIM / 256;
-    return gemm_launch<256, false, 1>(ma, bm, Hs, ld_hs, M, 3 * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev], st,
+    return gemm_launch<256, false, 1>(ma, bm, Hs, ld_hs, M, parts * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev], st,
                                       g_gemm_err[dev]);
 }
 
