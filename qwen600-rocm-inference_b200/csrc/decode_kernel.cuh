@@ -67,7 +67,7 @@ constexpr int kMinGS = 8;                   // min CTAs per group (grid >= 64)
 constexpr int kMaxCand = 64;                // device top-k limit
 constexpr int kHeadPart = 4 + HEAD_DIM;     // m, l, pad, pad, acc[128]
 constexpr int kPartStride = 2 * kHeadPart;  // both q heads of a group
-constexpr int kMaxLocalRows = 1280;         // LM-head rows per CTA at most
+constexpr int kMaxLocalRows = 2048;         // LM-head rows per CTA at most
 constexpr int kMaxMlpRows = 64;             // hidden rows per CTA at most
 constexpr int kQKVRows = 2 * HEAD_DIM + 2 * HEAD_DIM;   // 512 rows per group
 constexpr int kCtrStride = 16;              // counters 64 B apart
@@ -767,6 +767,107 @@ struct Consumer {
     }
 };
 
+// The last CTA to finish: merges the G x K candidates of the CTAs (their
+// local top-K of the LM-head rows), samples the next token (argmax, or
+// sampler.h:137-174 over the K candidates in descending order: temperature
+// softmax, top-p cut, xorshift64* coin, inverse CDF), hands it to the next
+// chained launch and advances the launch tag.
+__device__ __noinline__ void decode_merge_sample(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int tid, int G, int K, bool greedy,
+                                                 bool head, int pos, int flags, uint32_t seq) {
+    const int warp = tid >> 5, lane = tid & 31;
+    struct { __device__ void bar() const { named_bar(1, kNCT); } } C;
+    int tok = -1;
+    if (head) {
+        // all G*K candidates into the (now idle) ring
+        float* cv = (float*)ring;
+        int* ci = (int*)(ring + (size_t)G * kMaxCand * sizeof(float));
+        const int tot = G * K;
+        for (int t = tid; t < tot; t += kNCT) {
+            const int cc = t / K, kk = t % K;
+            cv[t] = __ldcg(P.cand_v + (size_t)cc * kMaxCand + kk);
+            ci[t] = __ldcg(P.cand_i + (size_t)cc * kMaxCand + kk);
+        }
+        C.bar();
+        for (int kk = 0; kk < K; kk++) {
+            float v = -INFINITY; int i = 0x7fffffff, at = -1;
+            for (int t = tid; t < tot; t += kNCT) {
+                const float v2 = cv[t]; const int i2 = ci[t];
+                if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; at = t; }
+            }
+            #pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+                const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+                const int a2 = __shfl_xor_sync(0xffffffffu, at, o);
+                if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; at = a2; }
+            }
+            if (lane == 0) { S->av[warp] = v; S->ai[warp] = i; S->am[warp] = __int_as_float(at); }
+            C.bar();
+            if (tid == 0) {
+                float bv = S->av[0]; int bi = S->ai[0]; int ba = __float_as_int(S->am[0]);
+                for (int w = 1; w < kNCW; w++) {
+                    const float v2 = S->av[w]; const int i2 = S->ai[w];
+                    if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; ba = __float_as_int(S->am[w]); }
+                }
+                P.top_v[kk] = bv; P.top_i[kk] = bi;
+                S->tv[kk] = bv;
+                S->ti[kk] = bi;
+                if (ba >= 0) { cv[ba] = -INFINITY; ci[ba] = 0x7fffffff; }
+            }
+            C.bar();
+        }
+        if (tid == 0) {
+            const int* ids = S->ti;
+            float* prob = S->w.lg;
+            unsigned long long rng = P.in->rng;
+            if (greedy) {
+                tok = ids[0];
+            } else {
+                // sampler.h:137-174 over the K candidates, scanned in descending order
+                const float T = P.in->temperature, topp = P.in->topp;
+                int nc = K;
+                const float mx = S->tv[0];
+                float sum = 0.f;
+                for (int i = 0; i < nc; i++) { const float e = expf((S->tv[i] - mx) / T); prob[i] = e; sum += e; }
+                for (int i = 0; i < nc; i++) prob[i] /= sum;
+                if (topp > 0.0f && topp < 1.0f) {
+                    float cum = 0.f; int last = nc - 1;
+                    for (int i = 0; i < nc; i++) { cum += prob[i]; if (cum > topp) { last = i; break; } }
+                    nc = last + 1; sum = cum;
+                }
+                rng ^= rng >> 12; rng ^= rng << 25; rng ^= rng >> 27;
+                const uint32_t u = (uint32_t)((rng * 0x2545F4914F6CDD1Dull) >> 32);
+                const float coin = ((float)(u >> 8) / 16777216.0f) * sum;
+                float cdf = 0.f;
+                tok = ids[nc - 1];
+                for (int i = 0; i < nc; i++) { cdf += prob[i]; if (coin < cdf) { tok = ids[i]; break; } }
+            }
+            if (tok < 0 || tok >= VOCAB_SIZE) {   // no finite candidate (NaN logits): report, never hand on
+                atomicOr(&P.out->err, 16u);
+                atomicExch(&P.out->err_where, -201);
+                tok = 0;
+            }
+            P.in->rng = rng;
+            P.out->rng = rng;
+        }
+    }
+    if (tid == 0) {
+        P.out->out_token = tok;
+        if (head) {
+            const int nd = P.out->n_done;
+            if (nd < P.tokens_cap) P.tokens_out[nd] = tok;
+            P.out->n_done = nd + 1;
+            P.in->token = tok;
+        } else if (flags & kFlagPromptToken) {
+            P.in->token = P.prompt[min(pos + 1, SEQ_LEN - 1)];
+        }
+        P.in->pos = pos + 1;
+        P.ctr[0] = 0;                 // every CTA has arrived: reset for the next launch
+        __threadfence();
+        P.out->seq = seq + 1;
+    }
+}
+
 template <bool kTr, bool kFused>
 __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, int G, const Plan& pl,
                                              int token, int pos, int flags, uint32_t seq) {
@@ -1239,98 +1340,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
     }
     C.bar();
     QB_TRACE(kTrHead + 2);
-    if (!S->flag) return;
-
-    int tok = -1;
-    if (head) {
-        // all G*K candidates into the (now idle) ring
-        float* cv = (float*)ring;
-        int* ci = (int*)(ring + (size_t)G * kMaxCand * sizeof(float));
-        const int tot = G * K;
-        for (int t = tid; t < tot; t += kNCT) {
-            const int cc = t / K, kk = t % K;
-            cv[t] = __ldcg(P.cand_v + (size_t)cc * kMaxCand + kk);
-            ci[t] = __ldcg(P.cand_i + (size_t)cc * kMaxCand + kk);
-        }
-        C.bar();
-        for (int kk = 0; kk < K; kk++) {
-            float v = -INFINITY; int i = 0x7fffffff, at = -1;
-            for (int t = tid; t < tot; t += kNCT) {
-                const float v2 = cv[t]; const int i2 = ci[t];
-                if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; at = t; }
-            }
-            #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-                const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
-                const int a2 = __shfl_xor_sync(0xffffffffu, at, o);
-                if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; at = a2; }
-            }
-            if (lane == 0) { S->av[warp] = v; S->ai[warp] = i; S->am[warp] = __int_as_float(at); }
-            C.bar();
-            if (tid == 0) {
-                float bv = S->av[0]; int bi = S->ai[0]; int ba = __float_as_int(S->am[0]);
-                for (int w = 1; w < kNCW; w++) {
-                    const float v2 = S->av[w]; const int i2 = S->ai[w];
-                    if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; ba = __float_as_int(S->am[w]); }
-                }
-                P.top_v[kk] = bv; P.top_i[kk] = bi;
-                S->tv[kk] = bv;
-                S->ti[kk] = bi;
-                if (ba >= 0) { cv[ba] = -INFINITY; ci[ba] = 0x7fffffff; }
-            }
-            C.bar();
-        }
-        if (tid == 0) {
-            const int* ids = S->ti;
-            float* prob = S->w.lg;
-            unsigned long long rng = P.in->rng;
-            if (greedy) {
-                tok = ids[0];
-            } else {
-                // sampler.h:137-174 over the K candidates, scanned in descending order
-                const float T = P.in->temperature, topp = P.in->topp;
-                int nc = K;
-                const float mx = S->tv[0];
-                float sum = 0.f;
-                for (int i = 0; i < nc; i++) { const float e = expf((S->tv[i] - mx) / T); prob[i] = e; sum += e; }
-                for (int i = 0; i < nc; i++) prob[i] /= sum;
-                if (topp > 0.0f && topp < 1.0f) {
-                    float cum = 0.f; int last = nc - 1;
-                    for (int i = 0; i < nc; i++) { cum += prob[i]; if (cum > topp) { last = i; break; } }
-                    nc = last + 1; sum = cum;
-                }
-                rng ^= rng >> 12; rng ^= rng << 25; rng ^= rng >> 27;
-                const uint32_t u = (uint32_t)((rng * 0x2545F4914F6CDD1Dull) >> 32);
-                const float coin = ((float)(u >> 8) / 16777216.0f) * sum;
-                float cdf = 0.f;
-                tok = ids[nc - 1];
-                for (int i = 0; i < nc; i++) { cdf += prob[i]; if (coin < cdf) { tok = ids[i]; break; } }
-            }
-            if (tok < 0 || tok >= VOCAB_SIZE) {   // no finite candidate (NaN logits): report, never hand on
-                atomicOr(&P.out->err, 16u);
-                atomicExch(&P.out->err_where, -201);
-                tok = 0;
-            }
-            P.in->rng = rng;
-            P.out->rng = rng;
-        }
-    }
-    if (tid == 0) {
-        P.out->out_token = tok;
-        if (head) {
-            const int nd = P.out->n_done;
-            if (nd < P.tokens_cap) P.tokens_out[nd] = tok;
-            P.out->n_done = nd + 1;
-            P.in->token = tok;
-        } else if (flags & kFlagPromptToken) {
-            P.in->token = P.prompt[min(pos + 1, SEQ_LEN - 1)];
-        }
-        P.in->pos = pos + 1;
-        P.ctr[0] = 0;                 // every CTA has arrived: reset for the next launch
-        __threadfence();
-        P.out->seq = seq + 1;
-    }
+    if (S->flag) decode_merge_sample(P, ring, S, tid, G, K, greedy, head, pos, flags, seq);
     QB_TRACE(kTrHead + 3);
 #undef QB_TRACE
 #undef QB_SUB

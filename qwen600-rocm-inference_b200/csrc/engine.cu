@@ -27,6 +27,7 @@
 
 #include "../../include/qwen_b200.h"
 #include "decode_kernel.cuh"
+#include "decode_cluster.cuh"
 #include "gemv_kernel.cuh"
 #include "gemm_tc.cuh"
 #include "prefill_kernels.cuh"
@@ -250,9 +251,13 @@ struct qwen_ctx {
     uint16_t* wgu = nullptr;     // gate|up weights interleaved per 128 rows, all layers
     uint16_t* wdt = nullptr;     // W_down transposed, all layers (the decode kernel's fused MLP)
     bool fused = false;          // decode layout: fused MLP with accumulated hops (false: tagged exchange words)
+    bool cluster = false;        // decode layout: 8-CTA clusters (decode_cluster.cuh)
+    int ncl = 0;                 // clusters the cluster layout runs (0: not available on this device)
+    bool cl_coop = true;         // the cluster launch also asks for co-residency (cooperative); dropped if refused
+    int grid = 0;                // CTAs of the decode launch in use
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
-    int pf_parts = 3;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
+    int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
     int last_k = 0;
 };
 
@@ -319,6 +324,31 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
             ctx_free(c); return fail(QWEN_E_CUDA, "decode kernel cannot be resident on every SM");
         }
     }
+    // the cluster layout: as many 8-CTA clusters as the device keeps resident at
+    // once (15 on a B200), if that is enough for its shares (8 KV-head clusters,
+    // at most kMaxMlpRows hidden units and kMaxLocalRows LM-head rows per CTA)
+    for (auto kern : {decode_cluster_kernel<false>, decode_cluster_kernel<true>}) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmemBytes) != cudaSuccess) { c->ncl = -1; break; }
+    }
+    if (c->ncl == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)kCl);
+        cfg.blockDim = dim3(kClThreads);
+        cfg.dynamicSmemBytes = kClSmemBytes;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = kCl; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+        cfg.attrs = at; cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, decode_cluster_kernel<false>, &cfg) != cudaSuccess) n = 0;
+        n = std::min(n, kClMaxClusters);
+        const int G = n * kCl, mlp_ctas = (n - kGroups) * kCl;
+        const bool ok = n > kGroups && (VOCAB_SIZE + G - 1) / G <= kMaxLocalRows &&
+                        (HIDDEN_DIM - kGroups * kCl * kClAttUnits + mlp_ctas - 1) / std::max(mlp_ctas, 1) <= kMaxMlpRows;
+        c->ncl = ok ? n : 0;
+    }
+    if (c->ncl < 0) c->ncl = 0;
+    cudaGetLastError();
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "stream creation failed"); }
 
     const size_t total = canonical_total_bytes();
@@ -331,7 +361,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     TRY(dalloc(&c->kc, kv));
     TRY(dalloc(&c->vc, kv));
     TRY(dalloc(&c->rope, (size_t)SEQ_LEN * HEAD_DIM));
-    const size_t n_xw = (size_t)(N_LAYERS + 1) * DIM, n_qkv = (size_t)N_LAYERS * 4096,
+    const size_t n_xw = (size_t)(N_LAYERS + 1) * kClMaxClusters * DIM, n_qkv = (size_t)N_LAYERS * 4096,
                  n_part = (size_t)N_LAYERS * kGroups * kMaxGS * kPartStride, n_y = (size_t)N_LAYERS * kGroups * DIM,
                  n_h = (size_t)N_LAYERS * HIDDEN_DIM;
     // fused layout: fp32 accumulators of both parities (2 x (2L + 1) x DIM floats,
@@ -398,9 +428,15 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     P.poll_ns = 0;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
-    // decode layout: "fused" (the fused MLP with accumulated hops, four per
-    // layer) or "tagged" (exchange words, five hops per layer)
-    if (const char* e = getenv("QWEN_B200_DECODE_LAYOUT")) c->fused = strcmp(e, "fused") == 0;
+    // decode layout: "cluster" (8-CTA clusters: two L2 hops and three
+    // distributed-shared-memory hops per layer), "fused" (the fused MLP with
+    // accumulated hops, four per layer) or "tagged" (exchange words, five hops
+    // per layer)
+    if (const char* e = getenv("QWEN_B200_DECODE_LAYOUT")) {
+        c->fused = strcmp(e, "fused") == 0;
+        c->cluster = strcmp(e, "cluster") == 0 && c->ncl > 0;
+    }
+    c->grid = c->cluster ? c->ncl * kCl : c->nsm;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -425,6 +461,33 @@ static int count_launch(qwen_t* c) {
 }
 
 static int enqueue_decode(qwen_t* c) {
+    if (c->cluster) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(c->ncl * kCl));
+        cfg.blockDim = dim3(kClThreads);
+        cfg.dynamicSmemBytes = kClSmemBytes;
+        cfg.stream = c->stream;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = kCl; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+        at[1].id = cudaLaunchAttributeCooperative;
+        at[1].val.cooperative = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = c->cl_coop ? 2 : 1;
+        auto kern = c->params.trace ? decode_cluster_kernel<true> : decode_cluster_kernel<false>;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, c->params);
+        if (e != cudaSuccess && c->cl_coop) {
+            // co-residency is requested where the runtime accepts it with clusters;
+            // the grid is the number of clusters the device keeps resident, so
+            // every CTA runs at once without it too (each wait is bounded)
+            cudaGetLastError();
+            c->cl_coop = false;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, kern, c->params);
+        }
+        CU(e);
+        return QWEN_OK;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c->nsm);
     cfg.blockDim = dim3(kThreads);
@@ -1077,6 +1140,7 @@ extern "C" int qwen_debug_read(qwen_t* c, float* resid, float* qkv) {
         for (size_t i = 0; i < n; i++) { const uint32_t u = (uint32_t)w[i]; memcpy(&dst[i], &u, 4); }
         return QWEN_OK;
     };
+    if (c->cluster) return fail(QWEN_E_UNSUPPORTED, "the cluster layout keeps no whole-vector copy of the residual stream");
     int rc = QWEN_OK;
     if (resid && c->fused) {   // x_1 .. x_L of the last launch (parity of its sequence number)
         StepOut o{};
@@ -1116,10 +1180,10 @@ extern "C" int qwen_trace_read(qwen_t* c, unsigned long long* out, int max_entri
 
 extern "C" int qwen_debug_chunk_counts(qwen_t* c, int* out, int max_ctas) {
     if (!c || !out) return fail(QWEN_E_ARG, "NULL argument");
-    if (max_ctas < c->nsm) return fail(QWEN_E_ARG, "buffer too small");
+    if (max_ctas < c->grid) return fail(QWEN_E_ARG, "buffer too small");
     CU(cudaSetDevice(c->device));
-    CU(cudaMemcpy(out, c->chunk_count, (size_t)2 * c->nsm * sizeof(int), cudaMemcpyDeviceToHost));
-    return c->nsm;
+    CU(cudaMemcpy(out, c->chunk_count, (size_t)2 * c->grid * sizeof(int), cudaMemcpyDeviceToHost));
+    return c->grid;
 }
 
 // ---------------------------------------------------------------------------
