@@ -274,6 +274,23 @@ int qwen_debug_read(qwen_t* ctx, float* resid, float* qkv);
  * stride and the meaning of each slot are documented in
  * csrc/decode_kernel.cuh (kTraceStride). */
 int qwen_trace_enable(qwen_t* ctx, int enable);
+
+/* The decode launch this handle uses: *layout 0 (exchange words, one CTA per
+ * SM), 1 (fused MLP with accumulated hops) or 2 (8-CTA clusters); *grid its
+ * CTAs; *clusters the clusters the cluster layout would run (0: not available
+ * on this device); *probe the device's answer to the cluster occupancy query
+ * (clusters, or minus a CUDA error code).  Any pointer may be NULL.  No
+ * reference counterpart. */
+int qwen_decode_info(const qwen_t* ctx, int* layout, int* grid, int* clusters, int* probe);
+
+/* Failure testing without a GPU fault (no reference counterpart; the
+ * reference exit()s on errors, static_loader.h:22-30): every later launch
+ * waits at most wait_ns (>= 1 ms; 0 restores the default 2 s) for another
+ * CTA's values, and, with group >= 0, the CTAs of KV head `group` withhold
+ * their layer-0 q|k|v.  The peers' waits then run out, the call returns
+ * QWEN_E_TIMEOUT, the device state is reset and the KV cache invalidated;
+ * qwen_debug_inject_wait(ctx, 0, -1) restores normal operation. */
+int qwen_debug_inject_wait(qwen_t* ctx, unsigned long long wait_ns, int group);
 int qwen_trace_read(qwen_t* ctx, unsigned long long* out, int max_entries);
 
 /* ---- isolated kernels ---------------------------------------------------- */

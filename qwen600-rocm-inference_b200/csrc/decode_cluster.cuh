@@ -35,7 +35,8 @@
 //
 // Numerics: as decode_kernel.cuh (bf16 weights and KV cache, fp32 everything
 // else, every sum in a fixed order: bit-reproducible for a given grid).
-// Every wait is bounded (kWaitNs): on expiry the kernel records an error,
+// Every wait is bounded (P.wait_ns on another CTA's values, kWaitNs multiples
+// on the ring): on expiry the kernel records an error,
 // stops waiting and still drains its copies; the host resets the device state.
 #pragma once
 #include "decode_kernel.cuh"
@@ -240,7 +241,7 @@ struct ClConsumer : Consumer<kTr> {
         const uint64_t t0 = global_ns();
         uint32_t it = 0;
         while (!mbar_try_wait_cluster(mb, parity)) {
-            if ((++it & 63u) == 0 && global_ns() - t0 > kWaitNs) {
+            if ((++it & 63u) == 0 && global_ns() - t0 > this->P->wait_ns) {
                 atomicOr(&this->P->out->err, 32u);
                 atomicExch(&this->P->out->err_where, where);
                 this->failed = true;
@@ -305,11 +306,12 @@ __device__ __forceinline__ void cl_consumer(const DecodeParams& P, uint8_t* ring
             // ---------------- QKV (cluster g) ----------------
             {
                 const float rn = C.gain_bx(x0, x1, C.gain_fetch(P.in_ln[l]));
+                const bool withhold = l == 0 && pl.k == P.debug_skip;   // failure tests only
                 C.rows_1024(kClQRows * pl.r, kClQRows * (pl.r + 1), &S->bx[0][0][0], [&](int row, float v) {
                     // row's raw projection to every CTA of the cluster
                     const float val = v * rn;
-                    for (uint32_t d = 0; d < (uint32_t)kCl; d++)
-                        st_async_v1(C.remote(&CS->qkv[row], d), val, C.remote(&CS->mb_q, d));
+                    if (!withhold)
+                        for (uint32_t d = 0; d < (uint32_t)kCl; d++) st_async_v1(C.remote(&CS->qkv[row], d), val, C.remote(&CS->mb_q, d));
                 });
             }
             QB_TRACE(TB + 1);

@@ -151,6 +151,8 @@ struct DecodeParams {
     int lm_begin, lm_end;    // LM-head rows served by this device
     int* chunk_count;        // [G][2] chunks issued (producer) / consumed (consumers)
     unsigned long long* trace;   // [G][kTraceStride] %globaltimer stamps, or nullptr
+    unsigned long long wait_ns;  // limit of each wait on another CTA's values (kWaitNs; shorter for failure tests)
+    int debug_skip;          // >= 0: the CTAs of this group / cluster withhold their layer-0 q|k|v (failure tests)
     int prefetch_chunks;     // L2 prefetch lead of the producer, in chunks (0 = none)
     int poll_ns;             // back-off between polls of an exchange word
 };
@@ -551,7 +553,7 @@ struct Consumer {
             if (P->poll_ns) __nanosleep(P->poll_ns);
             if ((++it & 31u) == 0) {
                 if (ld_volatile(&P->out->err)) failed = true;
-                else if (global_ns() - t0 > kWaitNs) {
+                else if (global_ns() - t0 > P->wait_ns) {
                     atomicOr(&P->out->err, 1u);
                     atomicExch(&P->out->err_where, where);
                     failed = true;
@@ -581,7 +583,7 @@ struct Consumer {
                 while (ld_acquire_u64(ctr) < target) {
                     if ((++it & 31u) == 0) {
                         if (ld_volatile(&P->out->err)) { S->hfail = 1; break; }
-                        if (global_ns() - t0 > kWaitNs) {
+                        if (global_ns() - t0 > P->wait_ns) {
                             atomicOr(&P->out->err, 1u);
                             atomicExch(&P->out->err_where, where);
                             S->hfail = 1;
@@ -928,7 +930,10 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             QB_SUB(31);
             QB_TRACE(TB + 0);
             uint64_t* qkv = P.qkvw + (size_t)l * 4096;
-            C.rows_1024(pl.qa, pl.qb, &S->bx[0][0][0], [&](int row, float v) { xw_store(qkv + qkv_dst(g, row), v * rn, seq); });
+            const bool withhold = l == 0 && g == P.debug_skip;   // failure tests only
+            C.rows_1024(pl.qa, pl.qb, &S->bx[0][0][0], [&](int row, float v) {
+                if (!withhold) xw_store(qkv + qkv_dst(g, row), v * rn, seq);
+            });
         }
         QB_TRACE(TB + 1);
         QB_SUB(32);

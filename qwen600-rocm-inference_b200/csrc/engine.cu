@@ -255,6 +255,7 @@ struct qwen_ctx {
     int ncl = 0;                 // clusters the cluster layout runs (0: not available on this device)
     bool cl_coop = true;         // the cluster launch also asks for co-residency (cooperative); dropped if refused
     int grid = 0;                // CTAs of the decode launch in use
+    int cl_probe = 0;            // clusters the occupancy query reported (or -cudaError_t of the failed query)
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
@@ -328,7 +329,8 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     // once (15 on a B200), if that is enough for its shares (8 KV-head clusters,
     // at most kMaxMlpRows hidden units and kMaxLocalRows LM-head rows per CTA)
     for (auto kern : {decode_cluster_kernel<false>, decode_cluster_kernel<true>}) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmemBytes) != cudaSuccess) { c->ncl = -1; break; }
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmemBytes);
+        if (e != cudaSuccess) { c->ncl = -1; c->cl_probe = -(int)e; break; }
     }
     if (c->ncl == 0) {
         cudaLaunchConfig_t cfg = {};
@@ -340,7 +342,9 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         at[0].val.clusterDim.x = kCl; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
         cfg.attrs = at; cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, decode_cluster_kernel<false>, &cfg) != cudaSuccess) n = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, decode_cluster_kernel<false>, &cfg);
+        c->cl_probe = e == cudaSuccess ? n : -(int)e;
+        if (e != cudaSuccess) n = 0;
         n = std::min(n, kClMaxClusters);
         const int G = n * kCl, mlp_ctas = (n - kGroups) * kCl;
         const bool ok = n > kGroups && (VOCAB_SIZE + G - 1) / G <= kMaxLocalRows &&
@@ -426,6 +430,8 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     // chunks, back-off in ns between polls of an exchange word
     P.prefetch_chunks = 0;
     P.poll_ns = 0;
+    P.wait_ns = kWaitNs;
+    P.debug_skip = -1;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
     // decode layout: "cluster" (8-CTA clusters: two L2 hops and three
@@ -1153,6 +1159,25 @@ extern "C" int qwen_debug_read(qwen_t* c, float* resid, float* qkv) {
     if (resid) rc = take(c->params.xw + DIM, (size_t)N_LAYERS * DIM, resid);       // residual after layer l = x_{l+1}
     if (rc == QWEN_OK && qkv) rc = take(c->params.qkvw, (size_t)N_LAYERS * 4096, qkv);
     return rc;
+}
+
+extern "C" int qwen_decode_info(const qwen_t* c, int* layout, int* grid, int* clusters, int* probe) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (layout) *layout = c->cluster ? 2 : (c->fused ? 1 : 0);
+    if (grid) *grid = c->grid;
+    if (clusters) *clusters = c->ncl;
+    if (probe) *probe = c->cl_probe;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_debug_inject_wait(qwen_t* c, unsigned long long wait_ns, int group) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (group < -1 || group >= kGroups) return fail(QWEN_E_ARG, "group must be -1 or a KV head index");
+    if (wait_ns != 0 && wait_ns < 1000000ull) return fail(QWEN_E_ARG, "wait limit below 1 ms");
+    c->params.wait_ns = wait_ns ? wait_ns : kWaitNs;
+    c->params.debug_skip = group;
+    drop_step_graph(c);
+    return QWEN_OK;
 }
 
 extern "C" int qwen_trace_enable(qwen_t* c, int enable) {

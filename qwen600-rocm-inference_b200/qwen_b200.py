@@ -65,6 +65,8 @@ _SIGS = {
     "qwen_debug_capture": (_c.c_int, [_P, _c.c_int]),
     "qwen_debug_read": (_c.c_int, [_P, _P, _P]),
     "qwen_trace_enable": (_c.c_int, [_P, _c.c_int]),
+    "qwen_debug_inject_wait": (_c.c_int, [_P, _c.c_ulonglong, _c.c_int]),
+    "qwen_decode_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
     "qwen_trace_read": (_c.c_int, [_P, _P, _c.c_int]),
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
@@ -355,6 +357,17 @@ class Engine:
         return r, q
 
     TRACE_STRIDE = 576
+
+    def decode_info(self):
+        """{'layout': 'tagged' | 'fused' | 'cluster', 'grid': CTAs, 'clusters': ..., 'probe': ...}"""
+        v = [ctypes.c_int() for _ in range(4)]
+        _check(self._lib.qwen_decode_info(self._h, *[ctypes.byref(x) for x in v]))
+        return {"layout": ["tagged", "fused", "cluster"][v[0].value], "grid": v[1].value, "clusters": v[2].value, "probe": v[3].value}
+
+    def debug_inject_wait(self, wait_ns=0, group=-1):
+        """Failure testing: wait limit for later launches (0 = default) and a KV
+        head whose CTAs withhold their layer-0 q|k|v (-1 = none)."""
+        _check(self._lib.qwen_debug_inject_wait(self._h, int(wait_ns), int(group)))
 
     def trace_enable(self, enable=True):
         _check(self._lib.qwen_trace_enable(self._h, 1 if enable else 0))
