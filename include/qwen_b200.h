@@ -68,6 +68,17 @@ int qwen_tensor_info(int index, const char** name, size_t* offset, size_t* bytes
  * may appear in any order.  Replaces the header read of static_loader.h:415-427. */
 int qwen_checkpoint_validate(const char* path);
 
+/* Write the reference's ordered weight blob (weights_qwen600.bin, export.py:80-146)
+ * of a BF16 safetensors checkpoint: the raw tensors back to back, no header, in
+ * the order embed_tokens, lm_head, final norm, then per layer q, k, v, o,
+ * q_norm, k_norm, gate, up, down, input_layernorm, post_attention_layernorm.
+ * Every loading entry point (qwen_create, qwen_weights_load,
+ * qwen_checkpoint_validate) accepts such a blob in place of the safetensors
+ * file, and, like static_loader.hip.h:185-202, reads weights_qwen600.bin from
+ * the checkpoint's directory instead of the checkpoint when one of the exact
+ * size lies there. */
+int qwen_write_ordered_blob(const char* safetensors_path, const char* out_path);
+
 /* Load a checkpoint into ONE device allocation laid out in the canonical order
  * (static_loader.h:402-494, load_qwen_weights).  *dev_block receives the device
  * pointer (free with qwen_weights_free); tensor i sits at qwen_tensor_info(i).offset. */

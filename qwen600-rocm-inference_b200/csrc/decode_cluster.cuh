@@ -497,6 +497,7 @@ __device__ __forceinline__ void cl_consumer(const DecodeParams& P, uint8_t* ring
         // ---------------- MLP ----------------
         {
             const uint32_t g2 = C.gain_fetch(P.post_ln[l]);
+            x0 = S->xres[j]; x1 = S->xres[j + 1];        // x_l (reloaded: not kept live across the attention stage)
             float yv[2 * kGroups];
             C.template gather<kGroups>([&](int gg) { return P.yw + ((size_t)l * kGroups + gg) * DIM + j; }, (1u << kGroups) - 1u, yv,
                                        10 * l + 6);
@@ -633,7 +634,7 @@ __device__ __forceinline__ void cl_consumer(const DecodeParams& P, uint8_t* ring
 
 // kTr: the tracing build.  Launched with cluster dimension kCl; grid = clusters x kCl.
 template <bool kTr>
-__global__ void __maxnreg__(120) decode_cluster_kernel(const __grid_constant__ DecodeParams P) {
+__global__ void __launch_bounds__(kClThreads, 1) decode_cluster_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
     ClSmem* CS = reinterpret_cast<ClSmem*>(smem + (size_t)kSlots * kSlotBytes);

@@ -71,6 +71,13 @@ extern "C" int qwen_checkpoint_validate(const char* path) {
     const int rc = parse_checkpoint(path, m, err);
     return rc == QWEN_OK ? QWEN_OK : fail(rc, err);
 }
+extern "C" int qwen_write_ordered_blob(const char* safetensors_path, const char* out_path) {
+    if (!safetensors_path || !out_path) return fail(QWEN_E_ARG, "NULL argument");
+    std::string err;
+    const int rc = write_blob(safetensors_path, out_path, err);
+    return rc == QWEN_OK ? QWEN_OK : fail(rc, err);
+}
+
 extern "C" int qwen_write_synthetic_checkpoint(const char* path, uint64_t seed) {
     if (!path) return fail(QWEN_E_ARG, "path is NULL");
     std::string err;
@@ -92,8 +99,9 @@ static int upload_checkpoint(const std::string& path, const CheckpointMap& m, ui
         if (!segs.empty() && segs.back().f + segs.back().n == s.f && segs.back().d + segs.back().n == s.d) segs.back().n += s.n;
         else segs.push_back(s);
     }
-    const int fd = open(path.c_str(), O_RDONLY);
-    if (fd < 0) return fail(QWEN_E_IO, "cannot open checkpoint: " + path);
+    (void)path;
+    const int fd = open(m.source.c_str(), O_RDONLY);
+    if (fd < 0) return fail(QWEN_E_IO, "cannot open checkpoint: " + m.source);
     const size_t CH = (size_t)64 << 20;
     void* stage[2] = {nullptr, nullptr};
     cudaEvent_t ev[2] = {nullptr, nullptr};

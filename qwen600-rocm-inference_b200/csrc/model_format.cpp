@@ -143,13 +143,65 @@ int embed_index() { return canonical_index("model.embed_tokens.weight"); }
 int lm_head_index() { return canonical_index("lm_head.weight"); }
 int final_norm_index() { return canonical_index("model.norm.weight"); }
 
+const std::vector<int>& blob_order() {
+    static const std::vector<int> o = [] {
+        std::vector<int> v = {embed_index(), lm_head_index(), final_norm_index()};
+        for (int l = 0; l < N_LAYERS; l++) {
+            const LayerIndex x = layer_index(l);
+            for (int i : {x.q_proj, x.k_proj, x.v_proj, x.o_proj, x.q_norm, x.k_norm, x.gate, x.up, x.down, x.in_ln, x.post_ln}) v.push_back(i);
+        }
+        return v;
+    }();
+    return o;
+}
+
+namespace {
+
+// A blob has no header: its size is exactly the sum of the tensors, and its
+// first 8 bytes do not announce a safetensors JSON header that fits the file.
+bool looks_like_blob(int fd, size_t bytes) {
+    if (bytes != canonical_total_bytes()) return false;
+    uint64_t hl = 0;
+    char c = 0;
+    if (pread(fd, &hl, 8, 0) != 8) return false;
+    if (hl == 0 || hl > (100u << 20) || 8 + hl > bytes) return true;
+    if (pread(fd, &c, 1, 8) != 1) return false;
+    return c != '{';
+}
+
+void map_blob(const std::string& path, size_t bytes, CheckpointMap& out) {
+    const auto& table = canonical_table();
+    out.file_offset.assign(table.size(), 0);
+    size_t off = 0;
+    for (int i : blob_order()) { out.file_offset[i] = off; off += table[i].bytes; }
+    out.file_bytes = bytes;
+    out.data_start = 0;
+    out.blob = true;
+    out.source = path;
+    out.canonical_order = false;
+}
+
+std::string sibling_blob(const std::string& path) {
+    const size_t p = path.find_last_of('/');
+    return (p == std::string::npos ? std::string(".") : path.substr(0, p)) + "/weights_qwen600.bin";
+}
+
+}  // namespace
+
 int parse_checkpoint(const std::string& path, CheckpointMap& out, std::string& err) {
     const auto& table = canonical_table();
+    out = CheckpointMap{};
+    out.source = path;
     int fd = open(path.c_str(), O_RDONLY);
     if (fd < 0) { err = "cannot open checkpoint: " + path; return QWEN_E_IO; }
     struct stat st;
     if (fstat(fd, &st) != 0) { close(fd); err = "cannot stat checkpoint: " + path; return QWEN_E_IO; }
     out.file_bytes = (size_t)st.st_size;
+    if (looks_like_blob(fd, out.file_bytes)) {
+        close(fd);
+        map_blob(path, out.file_bytes, out);
+        return QWEN_OK;
+    }
     uint64_t hl = 0;
     if (out.file_bytes < 8 || pread(fd, &hl, 8, 0) != 8) { close(fd); err = "checkpoint shorter than its 8-byte header length"; return QWEN_E_FORMAT; }
     if (hl == 0 || hl > (100u << 20) || 8 + hl > out.file_bytes) {
@@ -220,7 +272,47 @@ int parse_checkpoint(const std::string& path, CheckpointMap& out, std::string& e
     out.canonical_order = true;
     for (size_t i = 0; i < table.size(); i++)
         if (out.file_offset[i] != out.data_start + table[i].offset) { out.canonical_order = false; break; }
+    // the reference's preference for an ordered blob beside the checkpoint
+    const std::string sib = sibling_blob(path);
+    struct stat sb;
+    if (stat(sib.c_str(), &sb) == 0 && S_ISREG(sb.st_mode) && (size_t)sb.st_size == canonical_total_bytes()) {
+        const int bfd = open(sib.c_str(), O_RDONLY);
+        if (bfd >= 0) {
+            const bool ok = looks_like_blob(bfd, (size_t)sb.st_size);
+            close(bfd);
+            if (ok) map_blob(sib, (size_t)sb.st_size, out);
+        }
+    }
     return QWEN_OK;
+}
+
+int write_blob(const std::string& safetensors_path, const std::string& out_path, std::string& err) {
+    CheckpointMap m;
+    int rc = parse_checkpoint(safetensors_path, m, err);
+    if (rc != QWEN_OK) return rc;
+    const auto& table = canonical_table();
+    const int in = open(m.source.c_str(), O_RDONLY);
+    if (in < 0) { err = "cannot open " + m.source; return QWEN_E_IO; }
+    const std::string tmp = out_path + ".partial";
+    const int out = open(tmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC, 0644);
+    if (out < 0) { close(in); err = "cannot create " + tmp; return QWEN_E_IO; }
+    std::vector<char> buf((size_t)16 << 20);
+    rc = QWEN_OK;
+    for (int i : blob_order()) {
+        size_t done = 0;
+        while (done < table[i].bytes && rc == QWEN_OK) {
+            const size_t n = std::min(buf.size(), table[i].bytes - done);
+            if (pread(in, buf.data(), n, (off_t)(m.file_offset[i] + done)) != (ssize_t)n) { err = "short read of " + table[i].name; rc = QWEN_E_IO; break; }
+            if (write(out, buf.data(), n) != (ssize_t)n) { err = "short write to " + tmp; rc = QWEN_E_IO; break; }
+            done += n;
+        }
+        if (rc != QWEN_OK) break;
+    }
+    close(in);
+    if (close(out) != 0 && rc == QWEN_OK) { err = "cannot close " + tmp; rc = QWEN_E_IO; }
+    if (rc == QWEN_OK && rename(tmp.c_str(), out_path.c_str()) != 0) { err = "cannot rename " + tmp; rc = QWEN_E_IO; }
+    if (rc != QWEN_OK) unlink(tmp.c_str());
+    return rc;
 }
 
 int write_synthetic(const std::string& path, uint64_t seed, std::string& err) {

@@ -37,11 +37,26 @@ int final_norm_index();
 struct CheckpointMap {
     std::vector<size_t> file_offset;   // indexed like canonical_table()
     size_t file_bytes = 0;
-    size_t data_start = 0;             // 8 + header length
+    size_t data_start = 0;             // 8 + header length (0 for an ordered blob)
     bool canonical_order = false;      // data section is byte-identical in layout to the block
+    bool blob = false;                 // the tensors come from an ordered weight blob
+    std::string source;                // the file the tensors are read from
 };
-// Returns 0 or a QWEN_E_* status; err receives a message.
+// Returns 0 or a QWEN_E_* status; err receives a message.  `path` may name a
+// safetensors file or an ordered weight blob (recognised by its exact size and
+// the absence of a safetensors header).  Like the reference's loader
+// (static_loader.hip.h:185-202), a blob named weights_qwen600.bin beside a
+// safetensors file, of the exact size, is read instead of that file once the
+// file's header has been validated.
 int parse_checkpoint(const std::string& path, CheckpointMap& out, std::string& err);
+
+// The reference's ordered weight blob (export.py:80-146): raw bf16 tensors
+// back to back, no header, in the order embed_tokens, lm_head, final norm, then
+// per layer q, k, v, o, q_norm, k_norm, gate, up, down, input_layernorm,
+// post_attention_layernorm.  Indices into canonical_table().
+const std::vector<int>& blob_order();
+// Writes the blob of a (BF16) safetensors checkpoint.
+int write_blob(const std::string& safetensors_path, const std::string& out_path, std::string& err);
 
 // Synthetic checkpoint (see qwen_write_synthetic_checkpoint in qwen_b200.h).
 int write_synthetic(const std::string& path, uint64_t seed, std::string& err);

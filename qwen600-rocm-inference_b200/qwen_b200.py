@@ -43,6 +43,7 @@ _SIGS = {
     "qwen_weights_load": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
     "qwen_weights_free": (_c.c_int, [_P]),
     "qwen_write_synthetic_checkpoint": (_c.c_int, [_c.c_char_p, _c.c_uint64]),
+    "qwen_write_ordered_blob": (_c.c_int, [_c.c_char_p, _c.c_char_p]),
     "qwen_create": (_c.c_int, [_c.c_char_p, _c.c_int, _c.POINTER(_P)]),
     "qwen_destroy": (None, [_P]),
     "qwen_device": (_c.c_int, [_P]),
@@ -144,6 +145,11 @@ def tensor_table():
 
 def checkpoint_validate(path):
     _check(load_library().qwen_checkpoint_validate(path.encode()))
+
+
+def write_ordered_blob(safetensors_path, out_path):
+    """The reference's weights_qwen600.bin (export.py:80-146) of a BF16 safetensors checkpoint."""
+    _check(load_library().qwen_write_ordered_blob(safetensors_path.encode(), out_path.encode()))
 
 
 def write_synthetic_checkpoint(path, seed=0):

@@ -152,3 +152,65 @@ def test_synthetic_checkpoint(qb, checkpoint):
         assert (read("lm_head.weight", 1 << 20) == read("model.embed_tokens.weight", 1 << 20)).all()
         w = (read("model.layers.11.mlp.gate_proj.weight", 1 << 21).astype(np.uint32) << 16).view(np.float32)
         assert abs(float(w.mean())) < 1e-3 and abs(float(w.std()) - 0.02) < 5e-4
+
+
+def _permuted_copy(src, dst):
+    """The same checkpoint with its tensors stored in reverse name order (the
+    header lists them in that order too)."""
+    hl = struct.unpack("<Q", open(src, "rb").read(8))[0]
+    meta = json.loads(open(src, "rb").read(8 + hl)[8:])
+    names = sorted((k for k in meta if k != "__metadata__"), reverse=True)
+    ents, off = {"__metadata__": meta.get("__metadata__", {})}, 0
+    for n in names:
+        a, b = meta[n]["data_offsets"]
+        ents[n] = {"dtype": meta[n]["dtype"], "shape": meta[n]["shape"], "data_offsets": [off, off + b - a]}
+        off += b - a
+    js = json.dumps(ents).encode()
+    with open(src, "rb") as f, open(dst, "wb") as g:
+        g.write(struct.pack("<Q", len(js)) + js)
+        for n in names:
+            a, b = meta[n]["data_offsets"]
+            f.seek(8 + hl + a)
+            g.write(f.read(b - a))
+
+
+def test_ordered_blob_round_trip(qb, checkpoint, tmp_path):
+    """qwen_write_ordered_blob writes export.py:80-146's weights_qwen600.bin: each
+    tensor's bytes at the offset of that order; the loaders accept the blob
+    directly, and prefer one lying beside a safetensors file
+    (static_loader.hip.h:185-202)."""
+    import numpy as np
+    blob = str(tmp_path / "weights_qwen600.bin")
+    qb.write_ordered_blob(checkpoint, blob)
+    assert os.path.getsize(blob) == 1503264768
+    qb.checkpoint_validate(blob)
+    hl = struct.unpack("<Q", open(checkpoint, "rb").read(8))[0]
+    meta = json.loads(open(checkpoint, "rb").read(8 + hl)[8:])
+    order = ["model.embed_tokens.weight", "lm_head.weight", "model.norm.weight"]
+    for i in range(28):
+        p = f"model.layers.{i}."
+        order += [p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight", p + "self_attn.v_proj.weight", p + "self_attn.o_proj.weight",
+                  p + "self_attn.q_norm.weight", p + "self_attn.k_norm.weight", p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight",
+                  p + "mlp.down_proj.weight", p + "input_layernorm.weight", p + "post_attention_layernorm.weight"]
+    assert len(order) == 311
+    b = np.memmap(blob, dtype=np.uint8, mode="r")
+    c = np.memmap(checkpoint, dtype=np.uint8, mode="r")
+    off = 0
+    for n in order:
+        lo, hi = meta[n]["data_offsets"]
+        if n.endswith(("norm.weight", "q_proj.weight")) or n.startswith("model.layers.27"):
+            assert np.array_equal(b[off:off + hi - lo], c[8 + hl + lo:8 + hl + hi]), n
+        off += hi - lo
+    assert off == b.shape[0]
+    # a blob of the wrong size is a (headerless) file the parser rejects
+    bad = str(tmp_path / "short.bin")
+    with open(bad, "wb") as f:
+        f.write(b"\0" * 4096)
+    with pytest.raises(qb.QwenError):
+        qb.checkpoint_validate(bad)
+
+
+def test_permuted_checkpoint_validates(qb, checkpoint, tmp_path):
+    p = str(tmp_path / "permuted.safetensors")
+    _permuted_copy(checkpoint, p)
+    qb.checkpoint_validate(p)

@@ -188,6 +188,37 @@ def test_error_paths(engine, qb):
     assert 0 <= t < VOCAB
 
 
+def test_blob_and_permuted_checkpoints_give_identical_logits(qb, checkpoint, tmp_path):
+    """The canonical safetensors file, the same tensors in reverse order, the
+    ordered blob (export.py:80-146) given directly, and a safetensors file with
+    the blob beside it (static_loader.hip.h:185-202) load the same weights: the
+    logits of a few positions are bit-identical."""
+    import os
+    import shutil
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_cpu_format import _permuted_copy
+    perm = str(tmp_path / "permuted.safetensors")
+    _permuted_copy(checkpoint, perm)
+    blob = str(tmp_path / "blob" / "weights_qwen600.bin")
+    os.makedirs(os.path.dirname(blob))
+    qb.write_ordered_blob(checkpoint, blob)
+    beside = str(tmp_path / "blob" / "model.safetensors")
+    shutil.copyfile(perm, beside)        # its own tensors are those too, but the blob is what is read
+    want = None
+    for path in (checkpoint, perm, blob, beside):
+        eng = qb.Engine(path, 0)
+        try:
+            got = [eng.forward(t, pos).copy() for pos, t in enumerate(PROMPT[:4])]
+        finally:
+            eng.close()
+        if want is None:
+            want = got
+        else:
+            for a, b in zip(got, want):
+                assert np.array_equal(a, b), path
+
+
 def test_ring_accounting(engine):
     engine.prefill(PROMPT, 0)
     engine.decode_step(PROMPT[-1], 16)
