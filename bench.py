@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Batch-1 decode benchmark of the Qwen3-0.6B engine (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference] [--mode replicas|shard]
 
 Workload: Qwen3-0.6B architecture, bf16 weights from the seed-0 synthetic
 checkpoint, a 1024-token seeded prompt, then greedy decode at context 1024-1279
@@ -14,6 +14,10 @@ from HBM every step, far larger than the 126 MB L2.
                   events (max over ranks; N ranks = N independent replicas);
                   e2e = qwen_decode_step per token through the C ABI with the
                   token in and out of pinned host memory.
+--mode shard      the vocabulary-sharded LM head over the N ranks: per-token
+                  decode latency (ms/token, max over ranks) of the device loop
+                  (trunk + shard rows, NCCL all-gather of the shards' top-k,
+                  device merge and sampling), greedy and sampled.
 --impl reference  the reference's path on the host cores: the oracle's
                   restatement of forward() in the reference's own bf16 rounding
                   (qwen_model.cuh:772-851; the reference has no CPU forward) and
@@ -517,15 +521,67 @@ def run_mine(args):
         dist.destroy_process_group()
 
 
+def run_shard(args):
+    """--mode shard: the 151936-row LM head split across the N ranks (rows
+    [r V / N, (r+1) V / N) on rank r), every rank running the same trunk on the
+    same 1024-token prompt, the ranks' top-k exchanged per token by an NCCL
+    all-gather on the engine's stream and merged on the device
+    (sharding.ShardedHead).  value = per-token device latency, max over ranks,
+    greedy and sampled (temperature 0.6, top-p 0.95, top-k 20)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                            device_id=torch.device("cuda", local))
+    qb = load_qb()
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("sharding", os.path.join(REPO, "qwen600-rocm-inference_b200", "sharding.py"))
+    sh = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sh)
+    ck = qb.default_checkpoint(0)
+    eng = qb.Engine(ck, local)
+    eng.set_vocab_shard(*sh.shard_range(rank, world))
+    prompt = np.random.default_rng(1000).integers(0, 151936, PROMPT_LEN).tolist()
+    eng.prefill(prompt, 0)
+    head = sh.ShardedHead(eng)
+    out = {}
+    for name, sp in (("greedy", qb.GREEDY), ("top_k 20", qb.Sampling(0.6, 0.95, 20))):
+        head.generate(prompt[-1], PROMPT_LEN - 1, max(args.warmup, 3), sp, 7)
+        toks, _, ms = head.timed(prompt[-1], PROMPT_LEN - 1, args.steps, sp, 7)
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = float(t.item())
+    if rank == 0:
+        line = {"metric": "vocab-sharded LM head: batch-1 decode latency per token (Qwen3-0.6B bf16)", "value": out["greedy"],
+                "unit": "ms/token", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": dict(CONFIG, parallelism=f"LM head rows split over {world} ranks, top-k all-gather (NCCL) + device merge"),
+                "sampled_top_k20_ms_per_token": out["top_k 20"],
+                "gpu_launches": 2 * args.steps}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2048)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--mode", default="replicas", choices=["replicas", "shard"])
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "shard":
+        run_shard(args)
     else:
         run_mine(args)
 

@@ -191,6 +191,27 @@ int qwen_cached_positions(const qwen_t* ctx);
 int qwen_set_vocab_shard(qwen_t* ctx, int row_begin, int row_end);
 int qwen_shard_topk(qwen_t* ctx, int k, float* values_host, int* ids_host);
 
+/* Device-resident loop of a vocabulary-sharded head (each rank one handle with
+ * qwen_set_vocab_shard, all ranks the same prompt and settings).  Per token:
+ * qwen_shard_decode (the trunk and the shard's rows of the LM head; the shard's
+ * top-k stays on the device), qwen_shard_candidates (copies them, async on
+ * the handle's stream, into the caller's device buffer), an all-gather of
+ * those buffers across the ranks on the handle's stream (NCCL), then
+ * qwen_shard_merge (one small kernel: merges the ranks' candidates in
+ * descending order, ties by id, samples with the shared RNG state and hands the
+ * token to the next qwen_shard_decode).  No host round trip until
+ * qwen_shard_finish, which synchronises and returns the tokens.  Sampling
+ * settings: argmax, or top-p in (0, 1) with 1 <= top_k <= 64.
+ * qwen_shard_begin returns k, the candidates each rank contributes.  No
+ * reference counterpart (the reference runs on one GPU). */
+void* qwen_stream(qwen_t* ctx);
+int qwen_shard_begin(qwen_t* ctx, int token, int pos, const qwen_sampling_t* sp, unsigned long long rng_state);
+int qwen_shard_decode(qwen_t* ctx);
+int qwen_shard_candidates(qwen_t* ctx, float* values_dev, int* ids_dev);
+/* values_dev / ids_dev: rank r's k candidates at + r * stride (elements) */
+int qwen_shard_merge(qwen_t* ctx, const float* values_dev, const int* ids_dev, int n_ranks, int stride);
+int qwen_shard_finish(qwen_t* ctx, int* tokens_host, int n, unsigned long long* rng_state);
+
 /* ---- host sampler (sampler.h) ------------------------------------------- */
 
 /* sampler.h:120-175 on host logits, restated: argmax / top-k (Hoare quickselect)
@@ -285,14 +306,6 @@ int qwen_debug_read(qwen_t* ctx, float* resid, float* qkv);
  * stride and the meaning of each slot are documented in
  * csrc/decode_kernel.cuh (kTraceStride). */
 int qwen_trace_enable(qwen_t* ctx, int enable);
-
-/* The decode launch this handle uses: *layout 0 (exchange words, one CTA per
- * SM), 1 (fused MLP with accumulated hops) or 2 (8-CTA clusters); *grid its
- * CTAs; *clusters the clusters the cluster layout would run (0: not available
- * on this device); *probe the device's answer to the cluster occupancy query
- * (clusters, or minus a CUDA error code).  Any pointer may be NULL.  No
- * reference counterpart. */
-int qwen_decode_info(const qwen_t* ctx, int* layout, int* grid, int* clusters, int* probe);
 
 /* Failure testing without a GPU fault (no reference counterpart; the
  * reference exit()s on errors, static_loader.h:22-30): every later launch

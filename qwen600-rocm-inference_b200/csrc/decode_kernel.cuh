@@ -73,7 +73,6 @@ constexpr int kQKVRows = 2 * HEAD_DIM + 2 * HEAD_DIM;   // 512 rows per group
 constexpr int kCtrStride = 16;              // counters 64 B apart
 constexpr uint64_t kWaitNs = 2000000000ull; // 2 s
 constexpr int kNumCtr = 1;                  // the head's arrival counter
-constexpr int kHopStride = 16;              // hop counters 128 B apart
 // trace slots per CTA: 0 start; 1 + 10l + k for layer l:
 //   k = 0 x ready, 1 QKV done, 2 q/k/v ready, 3 ATT done, 4 partials ready,
 //   5 OPROJ done, 6 y ready, 7 MLP-A done, 8 h ready, 9 MLP-B done;
@@ -88,6 +87,7 @@ constexpr int kTrHead = 1 + 10 * N_LAYERS;
 constexpr int kFlagWriteLogits = 1;   // store all fp32 logits
 constexpr int kFlagNoHead = 2;        // skip the LM head and sampling (prompt positions)
 constexpr int kFlagPromptToken = 4;   // token = prompt[pos] instead of StepIn.token
+constexpr int kFlagCandidatesOnly = 8; // leave the shard's top-K in top_v / top_i; shard_merge_kernel picks the token
 
 struct StepIn {          // host-written before a launch; chained steps update it on device
     int token;
@@ -133,11 +133,6 @@ struct DecodeParams {
     uint64_t* partw;         // [L][8][kMaxGS][kPartStride]
     uint64_t* yw;            // [L][8][DIM]  O-projection partial of each group
     uint64_t* hw;            // [L][HIDDEN]  SwiGLU output
-    // fused-MLP layout (kFused): residual accumulators and arrival counters
-    const uint16_t* wdt[N_LAYERS];   // W_down transposed: [HIDDEN][DIM], row u = column u of W_down
-    float* xacc;             // [2][L+1][DIM]   x_l, accumulated with red.add (index [seq & 1])
-    float* macc;             // [2][L][DIM]     x_mid of layer l
-    unsigned long long* hop; // [2L+1][kHopStride]: arrivals at x_l (l = 1..L) and x_mid_l, monotone
     float* logits;           // [VOCAB]
     float* cand_v;           // [G][kMaxCand]
     int* cand_i;             // [G][kMaxCand]
@@ -152,7 +147,7 @@ struct DecodeParams {
     int* chunk_count;        // [G][2] chunks issued (producer) / consumed (consumers)
     unsigned long long* trace;   // [G][kTraceStride] %globaltimer stamps, or nullptr
     unsigned long long wait_ns;  // limit of each wait on another CTA's values (kWaitNs; shorter for failure tests)
-    int debug_skip;          // >= 0: the CTAs of this group / cluster withhold their layer-0 q|k|v (failure tests)
+    int debug_skip;          // >= 0: the CTAs of this KV-head group withhold their layer-0 q|k|v (failure tests)
     int prefetch_chunks;     // L2 prefetch lead of the producer, in chunks (0 = none)
     int poll_ns;             // back-off between polls of an exchange word
 };
@@ -197,9 +192,7 @@ struct __align__(16) DecodeSmem {
     int ai[kNCW];
     float tv[kMaxCand];      // merged top-K (head)
     int ti[kMaxCand];
-    float hl[kMaxMlpRows];   // fused MLP: this CTA's SwiGLU outputs
     int flag;
-    int hfail;               // a hop-counter wait gave up: every consumer stops waiting
     int abort;               // set after a ring wait expired: stop waiting on the ring
     unsigned int copied;     // chunks the producer has issued (read by the prefetch warp)
     Plan pl;                 // this CTA's share of every stage (one copy, in shared memory)
@@ -277,7 +270,6 @@ constexpr int kWoCols = 256 + kPad / 2;                    // packed Wo row, pad
 constexpr int kStrideWo = 2 * kWoCols;                     // 528 B
 constexpr int kRowsWo = kSlotBytes / kStrideWo;            // 62 rows per chunk
 constexpr int kRowsLM = kSlotBytes / (2 * DIM);            // 16 LM-head rows per chunk (unpadded: FFMA path)
-constexpr int kRowsWdT = kSlotBytes / (2 * DIM);           // 16 rows of W_down^T (2 KB each) per chunk
 constexpr int kKVChunk = 64;                               // positions per K|V chunk
 constexpr int kVOff = kKVChunk * 2 * HEAD_DIM;             // V offset in a K|V chunk
 static_assert(2 * kUnitsGU * kStride1024 <= kSlotBytes && kRowsWd * kStrideWd <= kSlotBytes, "chunks fit a slot");
@@ -311,7 +303,6 @@ struct Seg {            // `rows` copies of `bytes` each: source rows src_stride
 struct ChunkIter {
     int l = 0, st = 0, r = 0;
     int cur_st = 0, cur_l = 0;   // stage and layer of the chunk last returned
-    bool fused = false;          // stage 7 streams W_down^T rows of this CTA's hidden units instead of W_down rows
     // Fills seg[] with the next chunk's copies; returns their count (0 at the end).
     __device__ int next(const DecodeParams& P, const Plan& pl, Seg* seg) {
         for (;;) {
@@ -371,17 +362,10 @@ struct ChunkIter {
                     r += n;
                     return 2;
                 }
-                st = 7; r = fused ? pl.ha : pl.da;
+                st = 7; r = pl.da;
                 break;
             case 7:
-                if (fused) {
-                    if (r < pl.hb) {
-                        const int n = min(kRowsWdT, pl.hb - r);
-                        seg[0] = {(const uint8_t*)(P.wdt[l] + (size_t)r * DIM), (uint32_t)(n * 2 * DIM), 0, 1, 0, 0};
-                        r += n;
-                        return 1;
-                    }
-                } else if (r < pl.db) {
+                if (r < pl.db) {
                     const int n = min(kRowsWd, pl.db - r);
                     seg[0] = {(const uint8_t*)(P.wd[l] + (size_t)r * HIDDEN_DIM), (uint32_t)(2 * HIDDEN_DIM), 0, (uint32_t)n,
                               (uint32_t)(2 * HIDDEN_DIM), (uint32_t)kStrideWd};
@@ -413,12 +397,11 @@ struct ChunkIter {
 // P.prefetch_chunks chunks ahead of the producer; it keeps HBM streaming while
 // the ring is full because consumers wait on another CTA.
 // ---------------------------------------------------------------------------
-template <bool kTr, bool kFused>
+template <bool kTr>
 __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, const Plan& pl) {
     const uint64_t pol = policy_evict_first();
     unsigned long long* tr = (kTr && P.trace) ? P.trace + (size_t)c * kTraceStride : nullptr;
     ChunkIter it;
-    it.fused = kFused;
     Seg seg[3];
     uint32_t k = 0;
     int k13 = -1, last_l = -1;
@@ -455,9 +438,8 @@ __device__ __noinline__ void decode_producer(const DecodeParams& P, uint8_t* rin
     P.chunk_count[2 * c] = (int)k;
 }
 
-__device__ __noinline__ void decode_prefetcher(const DecodeParams& P, DecodeSmem* S, const Plan& pl, bool fused) {
+__device__ __noinline__ void decode_prefetcher(const DecodeParams& P, DecodeSmem* S, const Plan& pl) {
     ChunkIter it;
-    it.fused = fused;
     Seg seg[3];
     uint32_t npf = 0;
     const uint32_t lead = (uint32_t)P.prefetch_chunks;
@@ -563,39 +545,6 @@ struct Consumer {
         }
         #pragma unroll
         for (int i = 0; i < 2 * N; i++) v[i] = 0.f;   // after an error the values are never used for a result
-    }
-    // ---- global hops of the fused layout ----
-    // The CTA's red.add contributions to a hop precede this call: one block
-    // barrier orders them before thread 0's release add on the counter.
-    __device__ __forceinline__ void hop_arrive(unsigned long long* ctr) {
-        bar();
-        if (tid == 0) red_release_add_u64(ctr, 1ull);
-    }
-    // Waits until the counter reaches `target` (every CTA arrived for this
-    // launch: the counters only grow, G per launch).  Thread 0 polls with
-    // acquire loads, bounded by kWaitNs; the block barrier after it hands the
-    // outcome to every consumer thread.
-    __device__ __forceinline__ void hop_wait(const unsigned long long* ctr, unsigned long long target, int where) {
-        if (tid == 0 && !failed && !*(volatile int*)&S->hfail) {
-            if (ld_acquire_u64(ctr) < target) {
-                const uint64_t t0 = global_ns();
-                uint32_t it = 0;
-                while (ld_acquire_u64(ctr) < target) {
-                    if ((++it & 31u) == 0) {
-                        if (ld_volatile(&P->out->err)) { S->hfail = 1; break; }
-                        if (global_ns() - t0 > P->wait_ns) {
-                            atomicOr(&P->out->err, 1u);
-                            atomicExch(&P->out->err_where, where);
-                            S->hfail = 1;
-                            break;
-                        }
-                    }
-                }
-                if (kTr && tr) xw_ns += global_ns() - t0;
-            }
-        }
-        bar();
-        if (*(volatile int*)&S->hfail) failed = true;
     }
     // Sum over the 512 consumer threads.  One barrier: consecutive calls use
     // alternate buffers, and a call's buffer is not written again before every
@@ -769,6 +718,36 @@ struct Consumer {
     }
 };
 
+// sampler.h:137-174 over K candidates already in descending order (values v,
+// ids): argmax when greedy, else temperature softmax, the top-p cut (when 0 <
+// topp < 1), an xorshift64* coin (advancing rng) and the inverse CDF.  prob:
+// K floats of scratch.  Returns the id, or -1 if none is a valid token.
+__device__ __forceinline__ int sample_sorted(const float* v, const int* ids, int K, bool greedy, float T, float topp, unsigned long long& rng,
+                                             float* prob) {
+    int tok;
+    if (greedy) {
+        tok = ids[0];
+    } else {
+        int nc = K;
+        const float mx = v[0];
+        float sum = 0.f;
+        for (int i = 0; i < nc; i++) { const float e = expf((v[i] - mx) / T); prob[i] = e; sum += e; }
+        for (int i = 0; i < nc; i++) prob[i] /= sum;
+        if (topp > 0.0f && topp < 1.0f) {
+            float cum = 0.f; int last = nc - 1;
+            for (int i = 0; i < nc; i++) { cum += prob[i]; if (cum > topp) { last = i; break; } }
+            nc = last + 1; sum = cum;
+        }
+        rng ^= rng >> 12; rng ^= rng << 25; rng ^= rng >> 27;
+        const uint32_t u = (uint32_t)((rng * 0x2545F4914F6CDD1Dull) >> 32);
+        const float coin = ((float)(u >> 8) / 16777216.0f) * sum;
+        float cdf = 0.f;
+        tok = ids[nc - 1];
+        for (int i = 0; i < nc; i++) { cdf += prob[i]; if (coin < cdf) { tok = ids[i]; break; } }
+    }
+    return (tok < 0 || tok >= VOCAB_SIZE) ? -1 : tok;
+}
+
 // The last CTA to finish: merges the G x K candidates of the CTAs (their
 // local top-K of the LM-head rows), samples the next token (argmax, or
 // sampler.h:137-174 over the K candidates in descending order: temperature
@@ -818,33 +797,10 @@ __device__ __noinline__ void decode_merge_sample(const DecodeParams& P, uint8_t*
             }
             C.bar();
         }
-        if (tid == 0) {
-            const int* ids = S->ti;
-            float* prob = S->w.lg;
+        if (tid == 0 && !(flags & kFlagCandidatesOnly)) {
             unsigned long long rng = P.in->rng;
-            if (greedy) {
-                tok = ids[0];
-            } else {
-                // sampler.h:137-174 over the K candidates, scanned in descending order
-                const float T = P.in->temperature, topp = P.in->topp;
-                int nc = K;
-                const float mx = S->tv[0];
-                float sum = 0.f;
-                for (int i = 0; i < nc; i++) { const float e = expf((S->tv[i] - mx) / T); prob[i] = e; sum += e; }
-                for (int i = 0; i < nc; i++) prob[i] /= sum;
-                if (topp > 0.0f && topp < 1.0f) {
-                    float cum = 0.f; int last = nc - 1;
-                    for (int i = 0; i < nc; i++) { cum += prob[i]; if (cum > topp) { last = i; break; } }
-                    nc = last + 1; sum = cum;
-                }
-                rng ^= rng >> 12; rng ^= rng << 25; rng ^= rng >> 27;
-                const uint32_t u = (uint32_t)((rng * 0x2545F4914F6CDD1Dull) >> 32);
-                const float coin = ((float)(u >> 8) / 16777216.0f) * sum;
-                float cdf = 0.f;
-                tok = ids[nc - 1];
-                for (int i = 0; i < nc; i++) { cdf += prob[i]; if (coin < cdf) { tok = ids[i]; break; } }
-            }
-            if (tok < 0 || tok >= VOCAB_SIZE) {   // no finite candidate (NaN logits): report, never hand on
+            tok = sample_sorted(S->tv, S->ti, K, greedy, P.in->temperature, P.in->topp, rng, S->w.lg);
+            if (tok < 0) {   // no finite candidate (NaN logits): report, never hand on
                 atomicOr(&P.out->err, 16u);
                 atomicExch(&P.out->err_where, -201);
                 tok = 0;
@@ -855,7 +811,9 @@ __device__ __noinline__ void decode_merge_sample(const DecodeParams& P, uint8_t*
     }
     if (tid == 0) {
         P.out->out_token = tok;
-        if (head) {
+        if (flags & kFlagCandidatesOnly) {
+            // the token comes from shard_merge_kernel after the candidate exchange
+        } else if (head) {
             const int nd = P.out->n_done;
             if (nd < P.tokens_cap) P.tokens_out[nd] = tok;
             P.out->n_done = nd + 1;
@@ -870,7 +828,7 @@ __device__ __noinline__ void decode_merge_sample(const DecodeParams& P, uint8_t*
     }
 }
 
-template <bool kTr, bool kFused>
+template <bool kTr>
 __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* ring, DecodeSmem* S, int c, int G, const Plan& pl,
                                              int token, int pos, int flags, uint32_t seq) {
     Consumer<kTr> C;
@@ -888,22 +846,6 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
     QB_TRACE(0);
 
     if (tid < HEAD_DIM) S->rope[tid] = __ldg(P.rope + (size_t)pos * HEAD_DIM + tid);
-    // fused layout: this launch accumulates into the buffers of parity seq & 1
-    // (cleared by the previous launch) and clears its share of the other
-    // parity's for the next launch; the hop counters reach G * seq.
-    const uint32_t par = seq & 1u;
-    const unsigned long long hop_target = (unsigned long long)G * seq;
-    constexpr int kAccPer = (2 * N_LAYERS + 1) * DIM;   // floats per parity: x_1..x_L (+ unused x_0), x_mid_0..L-1
-    float* const xacc = P.xacc + (size_t)par * (N_LAYERS + 1) * DIM;
-    float* const macc = P.macc + (size_t)par * N_LAYERS * DIM;
-    if constexpr (kFused) {
-        float* const xq = P.xacc + (size_t)(par ^ 1u) * (N_LAYERS + 1) * DIM;
-        float* const mq = P.macc + (size_t)(par ^ 1u) * N_LAYERS * DIM;
-        for (int i = c * kNCT + tid; i < kAccPer; i += G * kNCT) {
-            if (i < (N_LAYERS + 1) * DIM) xq[i] = 0.f;
-            else mq[i - (N_LAYERS + 1) * DIM] = 0.f;
-        }
-    }
 
     for (int l = 0; l < N_LAYERS; l++) {
         const int TB = 1 + 10 * l;
@@ -917,10 +859,6 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             if (l == 0) {
                 const uint32_t w = __ldg((const uint32_t*)(P.embed + (size_t)token * DIM + j));
                 xv[0] = bf_lo(w); xv[1] = bf_hi(w);
-            } else if constexpr (kFused) {
-                C.hop_wait(P.hop + (size_t)(l - 1) * kHopStride, hop_target, 10 * l);
-                const float2 v = ld_relaxed_f2(xacc + (size_t)l * DIM + j);
-                xv[0] = v.x; xv[1] = v.y;
             } else {
                 const uint64_t* p = P.xw + (size_t)l * DIM + j;
                 C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * l);
@@ -1138,14 +1076,10 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                 if (tid < cnt) {                  // row tid: tile tt, summed over warps tt, tt+4, tt+8, tt+12
                     const int tt = tid >> 4, ri = tid & 15;
                     const float v = ((red[tt * 32 + ri] + red[(tt + 4) * 32 + ri]) + red[(tt + 8) * 32 + ri]) + red[(tt + 12) * 32 + ri];
-                    if constexpr (kFused)   // x_mid = x_l + sum over the 8 groups; group 0 adds the residual
-                        red_add_f32(macc + (size_t)l * DIM + r + tid, g == 0 ? v + S->xres[r + tid] : v);
-                    else
-                        xw_store(y + r + tid, v, seq);
+                    xw_store(y + r + tid, v, seq);
                 }
                 QB_SUB(14);
             }
-            if constexpr (kFused) C.hop_arrive(P.hop + (size_t)(N_LAYERS + l) * kHopStride);
         }
         QB_TRACE(TB + 5);
 
@@ -1156,12 +1090,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
             const uint64_t* yb = P.yw + (size_t)l * kGroups * DIM + j;
             QB_SUB(16);
             float x0 = S->xres[j], x1 = S->xres[j + 1];
-            if constexpr (kFused) {
-                (void)yb;
-                C.hop_wait(P.hop + (size_t)(N_LAYERS + l) * kHopStride, hop_target, 10 * l + 6);
-                const float2 v = ld_relaxed_f2(macc + (size_t)l * DIM + j);
-                x0 = v.x; x1 = v.y;
-            } else {
+            {
                 float yv[2 * kGroups];
                 C.template gather<kGroups>([&](int gg) { return yb + (size_t)gg * DIM; }, (1u << kGroups) - 1u, yv, 10 * l + 6);
                 #pragma unroll
@@ -1199,9 +1128,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
                     #pragma unroll
                     for (int w = 0; w < kNCW; w++) { gt += red[w * 32 + 16 * t + uu]; up += red[w * 32 + 16 * t + kUnitsGU + uu]; }
                     gt *= rn; up *= rn;
-                    const float h = (gt / (1.0f + expf(-gt))) * up;
-                    if constexpr (kFused) S->hl[u + tid - pl.ha] = h;
-                    else xw_store(hw + u + tid, h, seq);
+                    xw_store(hw + u + tid, (gt / (1.0f + expf(-gt))) * up, seq);
                 }
             }
             QB_SUB(22);
@@ -1210,75 +1137,46 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         QB_SUB(35);
 
         // ---------------- MLP-B ----------------
-        if constexpr (kFused) {
-            // x_{l+1} = x_mid + W_down h: this CTA's hidden units u in [ha, hb)
-            // times their columns of W_down (rows of W_down^T, 16 per chunk);
-            // thread t owns outputs 2t, 2t+1.  The partial vectors of all CTAs
-            // add up at L2 (red.add); each CTA adds x_mid for its rows [da, db).
-            C.bar();     // S->hl complete
-            QB_TRACE(TB + 8);
-            float a0 = 0.f, a1 = 0.f;
-            for (int u = pl.ha; u < pl.hb; u += kRowsWdT) {
-                const int n = min(kRowsWdT, pl.hb - u);
-                const uint8_t* ch = C.chunk(0);
-                const float* hs = &S->hl[u - pl.ha];
-                #pragma unroll 4
-                for (int i = 0; i < n; i++) {
-                    const uint32_t w = *(const uint32_t*)(ch + (size_t)i * 2 * DIM + 4 * tid);
-                    const float h = hs[i];
-                    a0 = fmaf(bf_lo(w), h, a0);
-                    a1 = fmaf(bf_hi(w), h, a1);
-                }
-                C.release(1);
-            }
-            const int j = 2 * tid;
-            if (j >= pl.da && j < pl.db) a0 += S->xres[j];
-            if (j + 1 >= pl.da && j + 1 < pl.db) a1 += S->xres[j + 1];
-            const float b0 = __shfl_down_sync(0xffffffffu, a0, 1), b1 = __shfl_down_sync(0xffffffffu, a1, 1);
-            if ((tid & 1) == 0) red_add_v4_f32(xacc + (size_t)(l + 1) * DIM + j, a0, a1, b0, b1);
-            C.hop_arrive(P.hop + (size_t)l * kHopStride);   // also the barrier before S->xres / S->hl are reused
-        } else {
-            {
-                const uint64_t* hb = P.hw + (size_t)l * HIDDEN_DIM + 2 * tid;
-                constexpr int kHP = HIDDEN_DIM / (2 * kNCT);
-                float hv[2 * kHP];
-                QB_SUB(25);
-                C.template gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
-                #pragma unroll
-                for (int i = 0; i < kHP; i++) C.put_pair(&S->w.bh[0][0][0], 2 * tid + 2 * kNCT * i, hv[2 * i], hv[2 * i + 1]);
-            }
-            C.bar();
-            QB_TRACE(TB + 8);
-            {
-                // rows of Wd, two chunks (8 rows) per round as one tile: tile rows
-                // 0..3 = chunk 0, 4..7 = chunk 1; warp w takes k-tiles 12w..12w+11
-                uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
-                const int lr = lane & 15;
-                for (int r = pl.da; r < pl.db; r += 2 * kRowsWd) {
-                    const int n = min(2 * kRowsWd, pl.db - r);
-                    const uint32_t nc = n > kRowsWd ? 2 : 1;
-                    const uint8_t* c0 = C.chunk(0);
-                    const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
-                    QB_SUB(28);
-                    const uint8_t* rp = lr < n ? (lr < kRowsWd ? c0 + (size_t)lr * kStrideWd : c1 + (size_t)(lr - kRowsWd) * kStrideWd) : c0;
-                    uint32_t ta[1] = {smem_addr(rp) + (lane >> 4) * 16};
-                    float d[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-                    C.template mma_tiles<1>(ta, &S->w.bh[0][0][0], 12 * warp, HIDDEN_DIM / 16 / kNCW, d);
-                    float* red = C.next_red();
-                    C.put_red(red, 0, d[0]);
-                    C.release(nc);
-                    C.bar();
-                    QB_SUB(30);
-                    if (tid < n) {
-                        float v = 0.f;
-                        #pragma unroll
-                        for (int w = 0; w < kNCW; w++) v += red[w * 32 + tid];
-                        xw_store(xn + r + tid, S->xres[r + tid] + v, seq);
-                    }
-                }
-            }
-            C.bar();     // S->w.bh and S->xres are reused by the next layer
+        {
+            const uint64_t* hb = P.hw + (size_t)l * HIDDEN_DIM + 2 * tid;
+            constexpr int kHP = HIDDEN_DIM / (2 * kNCT);
+            float hv[2 * kHP];
+            QB_SUB(25);
+            C.template gather<kHP>([&](int i) { return hb + 2 * kNCT * i; }, (1u << kHP) - 1u, hv, 10 * l + 8);
+            #pragma unroll
+            for (int i = 0; i < kHP; i++) C.put_pair(&S->w.bh[0][0][0], 2 * tid + 2 * kNCT * i, hv[2 * i], hv[2 * i + 1]);
         }
+        C.bar();
+        QB_TRACE(TB + 8);
+        {
+            // rows of Wd, two chunks (8 rows) per round as one tile: tile rows
+            // 0..3 = chunk 0, 4..7 = chunk 1; warp w takes k-tiles 12w..12w+11
+            uint64_t* xn = P.xw + (size_t)(l + 1) * DIM;
+            const int lr = lane & 15;
+            for (int r = pl.da; r < pl.db; r += 2 * kRowsWd) {
+                const int n = min(2 * kRowsWd, pl.db - r);
+                const uint32_t nc = n > kRowsWd ? 2 : 1;
+                const uint8_t* c0 = C.chunk(0);
+                const uint8_t* c1 = nc == 2 ? C.chunk(1) : c0;
+                QB_SUB(28);
+                const uint8_t* rp = lr < n ? (lr < kRowsWd ? c0 + (size_t)lr * kStrideWd : c1 + (size_t)(lr - kRowsWd) * kStrideWd) : c0;
+                uint32_t ta[1] = {smem_addr(rp) + (lane >> 4) * 16};
+                float d[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+                C.template mma_tiles<1>(ta, &S->w.bh[0][0][0], 12 * warp, HIDDEN_DIM / 16 / kNCW, d);
+                float* red = C.next_red();
+                C.put_red(red, 0, d[0]);
+                C.release(nc);
+                C.bar();
+                QB_SUB(30);
+                if (tid < n) {
+                    float v = 0.f;
+                    #pragma unroll
+                    for (int w = 0; w < kNCW; w++) v += red[w * 32 + tid];
+                    xw_store(xn + r + tid, S->xres[r + tid] + v, seq);
+                }
+            }
+        }
+        C.bar();     // S->w.bh and S->xres are reused by the next layer
         QB_TRACE(TB + 9);
         QB_SUB(36);
     }
@@ -1295,11 +1193,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
         {
             const int j = tid * 2;
             float xv[2];
-            if constexpr (kFused) {
-                C.hop_wait(P.hop + (size_t)(N_LAYERS - 1) * kHopStride, hop_target, 10 * N_LAYERS);
-                const float2 v = ld_relaxed_f2(xacc + (size_t)N_LAYERS * DIM + j);
-                xv[0] = v.x; xv[1] = v.y;
-            } else {
+            {
                 const uint64_t* p = P.xw + (size_t)N_LAYERS * DIM + j;
                 C.template gather<1>([&](int) { return p; }, 1u, xv, 10 * N_LAYERS);
             }
@@ -1353,7 +1247,7 @@ __device__ __forceinline__ void decode_consumer(const DecodeParams& P, uint8_t* 
 
 // kTr: the tracing build (stage time stamps into P.trace); the other build has
 // no trace code at all.
-template <bool kTr, bool kFused>
+template <bool kTr>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
@@ -1362,7 +1256,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (tid == 0) {
         for (int s = 0; s < kSlots; s++) { mbar_init(&S->full[s], 1); mbar_init(&S->empty[s], kNCW); }
         S->abort = 0;
-        S->hfail = 0;
         S->copied = 0;
         fence_barrier_init();
     }
@@ -1380,14 +1273,71 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     __syncthreads();
     const Plan& pl = S->pl;
     if ((tid >> 5) == kNCW) {
-        if ((tid & 31) == 0) decode_producer<kTr, kFused>(P, ring, S, c, pl);
+        if ((tid & 31) == 0) decode_producer<kTr>(P, ring, S, c, pl);
         return;
     }
     if ((tid >> 5) == kNCW + 1) {
-        if ((tid & 31) == 0) decode_prefetcher(P, S, pl, kFused);
+        if ((tid & 31) == 0) decode_prefetcher(P, S, pl);
         return;
     }
-    decode_consumer<kTr, kFused>(P, ring, S, c, G, pl, token, pos, flags, seq);
+    decode_consumer<kTr>(P, ring, S, c, G, pl, token, pos, flags, seq);
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary-sharded LM head: after every rank's launch left its shard's top K
+// in top_v / top_i (kFlagCandidatesOnly) and the ranks exchanged them (an
+// all-gather on the handle's stream: n_ranks x K values and global ids), this
+// kernel merges them in (value descending, id ascending) order — the order of
+// the one-GPU device sampler — and samples the step's token with the same
+// math and RNG state on every rank, then hands it to the next launch (StepIn)
+// and records it (StepOut, tokens_out).  One CTA of kMergeThreads threads;
+// n_ranks * K <= 2 * kMergeThreads.
+// ---------------------------------------------------------------------------
+constexpr int kMergeThreads = 256;
+
+__global__ void __launch_bounds__(kMergeThreads) shard_merge_kernel(const float* __restrict__ gv, const int* __restrict__ gi, int n_ranks,
+                                                                    int K, int stride, StepIn* in, StepOut* out, int* tokens_out,
+                                                                    int tokens_cap) {
+    __shared__ float sv[2 * kMergeThreads];
+    __shared__ int si[2 * kMergeThreads];
+    __shared__ float prob[kMaxCand];
+    const int n = n_ranks * K, tid = threadIdx.x;
+    // every candidate's rank: the candidates that precede it (NaN counts as -inf;
+    // equal (value, id) pairs, which only padding entries share, by position)
+    // candidate e = (rank e / K, entry e % K) at gv / gi + rank * stride + entry
+    auto at = [&](int e) { return (e / K) * stride + e % K; };
+    for (int e = tid; e < n; e += kMergeThreads) {
+        float v = gv[at(e)];
+        const int id = gi[at(e)];
+        if (v != v) v = -INFINITY;
+        int rank = 0;
+        for (int f = 0; f < n; f++) {
+            float w = gv[at(f)];
+            if (w != w) w = -INFINITY;
+            const int jd = gi[at(f)];
+            rank += (w > v || (w == v && (jd < id || (jd == id && f < e)))) ? 1 : 0;
+        }
+        sv[rank] = v;
+        si[rank] = id;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const bool greedy = in->temperature == 0.0f || in->top_k == 1;
+        unsigned long long rng = in->rng;
+        int tok = sample_sorted(sv, si, greedy ? 1 : K, greedy, in->temperature, in->topp, rng, prob);
+        if (tok < 0) {
+            atomicOr(&out->err, 16u);
+            atomicExch(&out->err_where, -202);
+            tok = 0;
+        }
+        in->rng = rng;
+        out->rng = rng;
+        in->token = tok;
+        out->out_token = tok;
+        const int nd = out->n_done;
+        if (nd < tokens_cap) tokens_out[nd] = tok;
+        out->n_done = nd + 1;
+    }
 }
 
 }  // namespace qb

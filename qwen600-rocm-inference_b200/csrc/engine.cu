@@ -27,7 +27,6 @@
 
 #include "../../include/qwen_b200.h"
 #include "decode_kernel.cuh"
-#include "decode_cluster.cuh"
 #include "gemv_kernel.cuh"
 #include "gemm_tc.cuh"
 #include "prefill_kernels.cuh"
@@ -173,17 +172,6 @@ __global__ void pack_wo_kernel(const uint16_t* __restrict__ wo, uint16_t* __rest
     }
 }
 
-// One layer's W_down [DIM][HIDDEN] -> W_down^T [HIDDEN][DIM]: row u holds the
-// column of hidden unit u, so the decode kernel's fused MLP streams a CTA's
-// units as contiguous 2 KB rows.  32 x 32 tiles through shared memory.
-__global__ void transpose_wd_kernel(const uint16_t* __restrict__ wd, uint16_t* __restrict__ wdt) {
-    __shared__ uint16_t t[32][33];
-    const int u0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) t[i][threadIdx.x] = wd[(size_t)(r0 + i) * HIDDEN_DIM + u0 + threadIdx.x];
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) wdt[(size_t)(u0 + i) * DIM + r0 + threadIdx.x] = t[threadIdx.x][i];
-}
-
 // gate and up rows interleaved in blocks of 128 (block 2j: gate rows 128j ..,
 // block 2j+1: the same up rows), so one 128 x 256 GEMM tile holds both halves
 // of 128 hidden units and its epilogue can apply SwiGLU.
@@ -257,13 +245,7 @@ struct qwen_ctx {
     uint16_t* pf_as = nullptr;
     uint16_t* pf_hs = nullptr;   // SwiGLU output in three bf16 parts (written by the fused gate|up GEMM)
     uint16_t* wgu = nullptr;     // gate|up weights interleaved per 128 rows, all layers
-    uint16_t* wdt = nullptr;     // W_down transposed, all layers (the decode kernel's fused MLP)
-    bool fused = false;          // decode layout: fused MLP with accumulated hops (false: tagged exchange words)
-    bool cluster = false;        // decode layout: 8-CTA clusters (decode_cluster.cuh)
-    int ncl = 0;                 // clusters the cluster layout runs (0: not available on this device)
-    bool cl_coop = true;         // the cluster launch also asks for co-residency (cooperative); dropped if refused
-    int grid = 0;                // CTAs of the decode launch in use
-    int cl_probe = 0;            // clusters the occupancy query reported (or -cudaError_t of the failed query)
+    int shard_pos0 = -1, shard_steps = 0;   // the sharded-head loop in progress (qwen_shard_begin .. _finish)
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
@@ -275,7 +257,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->wdt, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -324,7 +306,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         (HIDDEN_DIM + c->nsm - 1) / c->nsm > kMaxMlpRows) {
         ctx_free(c); return fail(QWEN_E_UNSUPPORTED, "unsupported SM count " + std::to_string(c->nsm));
     }
-    for (auto kern : {decode_kernel<false, false>, decode_kernel<true, false>, decode_kernel<false, true>, decode_kernel<true, true>}) {
+    for (auto kern : {decode_kernel<false>, decode_kernel<true>}) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmemBytes) != cudaSuccess) {
             ctx_free(c); return fail(QWEN_E_CUDA, "cannot reserve " + std::to_string(kDecodeSmemBytes) + " B of shared memory");
         }
@@ -333,34 +315,6 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
             ctx_free(c); return fail(QWEN_E_CUDA, "decode kernel cannot be resident on every SM");
         }
     }
-    // the cluster layout: as many 8-CTA clusters as the device keeps resident at
-    // once (15 on a B200), if that is enough for its shares (8 KV-head clusters,
-    // at most kMaxMlpRows hidden units and kMaxLocalRows LM-head rows per CTA)
-    for (auto kern : {decode_cluster_kernel<false>, decode_cluster_kernel<true>}) {
-        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmemBytes);
-        if (e != cudaSuccess) { c->ncl = -1; c->cl_probe = -(int)e; break; }
-    }
-    if (c->ncl == 0) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)kCl);
-        cfg.blockDim = dim3(kClThreads);
-        cfg.dynamicSmemBytes = kClSmemBytes;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = kCl; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
-        cfg.attrs = at; cfg.numAttrs = 1;
-        int n = 0;
-        const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, decode_cluster_kernel<false>, &cfg);
-        c->cl_probe = e == cudaSuccess ? n : -(int)e;
-        if (e != cudaSuccess) n = 0;
-        n = std::min(n, kClMaxClusters);
-        const int G = n * kCl, mlp_ctas = (n - kGroups) * kCl;
-        const bool ok = n > kGroups && (VOCAB_SIZE + G - 1) / G <= kMaxLocalRows &&
-                        (HIDDEN_DIM - kGroups * kCl * kClAttUnits + mlp_ctas - 1) / std::max(mlp_ctas, 1) <= kMaxMlpRows;
-        c->ncl = ok ? n : 0;
-    }
-    if (c->ncl < 0) c->ncl = 0;
-    cudaGetLastError();
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "stream creation failed"); }
 
     const size_t total = canonical_total_bytes();
@@ -368,18 +322,14 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     TRY(upload_checkpoint(path, m, c->wblock, c->stream));
     TRY(dalloc(&c->wo_g, (size_t)N_LAYERS * kGroups * DIM * kWoCols));
     TRY(dalloc(&c->wgu, (size_t)N_LAYERS * 2 * HIDDEN_DIM * DIM));
-    TRY(dalloc(&c->wdt, (size_t)N_LAYERS * HIDDEN_DIM * DIM));
     const size_t kv = (size_t)N_LAYERS * N_KV_HEADS * SEQ_LEN * HEAD_DIM;
     TRY(dalloc(&c->kc, kv));
     TRY(dalloc(&c->vc, kv));
     TRY(dalloc(&c->rope, (size_t)SEQ_LEN * HEAD_DIM));
-    const size_t n_xw = (size_t)(N_LAYERS + 1) * kClMaxClusters * DIM, n_qkv = (size_t)N_LAYERS * 4096,
+    const size_t n_xw = (size_t)(N_LAYERS + 1) * DIM, n_qkv = (size_t)N_LAYERS * 4096,
                  n_part = (size_t)N_LAYERS * kGroups * kMaxGS * kPartStride, n_y = (size_t)N_LAYERS * kGroups * DIM,
                  n_h = (size_t)N_LAYERS * HIDDEN_DIM;
-    // fused layout: fp32 accumulators of both parities (2 x (2L + 1) x DIM floats,
-    // as 64-bit words) and the hop counters, zeroed with the exchange words
-    const size_t n_acc = (size_t)(2 * N_LAYERS + 1) * DIM, n_hop = (size_t)(2 * N_LAYERS + 1) * kHopStride;
-    c->xchg_words = n_xw + n_qkv + n_part + n_y + n_h + n_acc + n_hop;
+    c->xchg_words = n_xw + n_qkv + n_part + n_y + n_h;
     TRY(dalloc(&c->xchg, c->xchg_words));
     TRY(dalloc(&c->logits, (size_t)VOCAB_SIZE));
     TRY(dalloc(&c->cand_v, (size_t)c->nsm * kMaxCand));
@@ -420,16 +370,11 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
         P.wg[l] = W(li.gate); P.wu[l] = W(li.up); P.wd[l] = W(li.down);
         pack_wo_kernel<<<1024, 256, 0, c->stream>>>(W(li.o_proj), c->wo_g + (size_t)l * kGroups * DIM * kWoCols);
         pack_gu_kernel<<<1024, 256, 0, c->stream>>>(W(li.gate), W(li.up), c->wgu + (size_t)l * 2 * HIDDEN_DIM * DIM);
-        transpose_wd_kernel<<<dim3(HIDDEN_DIM / 32, DIM / 32), dim3(32, 8), 0, c->stream>>>(W(li.down), c->wdt + (size_t)l * HIDDEN_DIM * DIM);
-        P.wdt[l] = c->wdt + (size_t)l * HIDDEN_DIM * DIM;
         c->wo_raw[l] = W(li.o_proj);
     }
     if (cudaGetLastError() != cudaSuccess) { ctx_free(c); return fail(QWEN_E_CUDA, "repack launch failed"); }
     P.wo_g = c->wo_g; P.kc = c->kc; P.vc = c->vc; P.rope = c->rope; P.prompt = c->prompt;
     P.xw = c->xchg; P.qkvw = P.xw + n_xw; P.partw = P.qkvw + n_qkv; P.yw = P.partw + n_part; P.hw = P.yw + n_y;
-    P.xacc = reinterpret_cast<float*>(P.hw + n_h);
-    P.macc = P.xacc + 2 * (size_t)(N_LAYERS + 1) * DIM;
-    P.hop = reinterpret_cast<unsigned long long*>(P.hw + n_h + n_acc);
     P.logits = c->logits;
     P.cand_v = c->cand_v; P.cand_i = c->cand_i; P.top_v = c->top_v; P.top_i = c->top_i; P.ctr = c->ctr;
     P.in = c->d_in; P.out = c->d_out; P.tokens_out = c->tokens; P.tokens_cap = SEQ_LEN;
@@ -442,15 +387,6 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     P.debug_skip = -1;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
-    // decode layout: "cluster" (8-CTA clusters: two L2 hops and three
-    // distributed-shared-memory hops per layer), "fused" (the fused MLP with
-    // accumulated hops, four per layer) or "tagged" (exchange words, five hops
-    // per layer)
-    if (const char* e = getenv("QWEN_B200_DECODE_LAYOUT")) {
-        c->fused = strcmp(e, "fused") == 0;
-        c->cluster = strcmp(e, "cluster") == 0 && c->ncl > 0;
-    }
-    c->grid = c->cluster ? c->ncl * kCl : c->nsm;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -475,33 +411,6 @@ static int count_launch(qwen_t* c) {
 }
 
 static int enqueue_decode(qwen_t* c) {
-    if (c->cluster) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(c->ncl * kCl));
-        cfg.blockDim = dim3(kClThreads);
-        cfg.dynamicSmemBytes = kClSmemBytes;
-        cfg.stream = c->stream;
-        cudaLaunchAttribute at[2];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = kCl; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
-        at[1].id = cudaLaunchAttributeCooperative;
-        at[1].val.cooperative = 1;
-        cfg.attrs = at;
-        cfg.numAttrs = c->cl_coop ? 2 : 1;
-        auto kern = c->params.trace ? decode_cluster_kernel<true> : decode_cluster_kernel<false>;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, c->params);
-        if (e != cudaSuccess && c->cl_coop) {
-            // co-residency is requested where the runtime accepts it with clusters;
-            // the grid is the number of clusters the device keeps resident, so
-            // every CTA runs at once without it too (each wait is bounded)
-            cudaGetLastError();
-            c->cl_coop = false;
-            cfg.numAttrs = 1;
-            e = cudaLaunchKernelEx(&cfg, kern, c->params);
-        }
-        CU(e);
-        return QWEN_OK;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)c->nsm);
     cfg.blockDim = dim3(kThreads);
@@ -512,13 +421,8 @@ static int enqueue_decode(qwen_t* c) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (c->fused) {
-        if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true, true>, c->params));
-        else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false, true>, c->params));
-    } else {
-        if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true, false>, c->params));
-        else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false, false>, c->params));
-    }
+    if (c->params.trace) CU(cudaLaunchKernelEx(&cfg, decode_kernel<true>, c->params));
+    else CU(cudaLaunchKernelEx(&cfg, decode_kernel<false>, c->params));
     return QWEN_OK;
 }
 
@@ -1137,6 +1041,76 @@ extern "C" int qwen_shard_topk(qwen_t* c, int k, float* values_host, int* ids_ho
     return QWEN_OK;
 }
 
+// ---- vocabulary-sharded head, device-resident (no host round trip per token) ----
+extern "C" void* qwen_stream(qwen_t* c) { return c ? (void*)c->stream : nullptr; }
+
+static int shard_k(const qwen_sampling_t* sp) { return is_greedy(sp) ? 1 : sp->top_k; }
+
+extern "C" int qwen_shard_begin(qwen_t* c, int token, int pos, const qwen_sampling_t* sp, unsigned long long rng) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (token < 0 || token >= VOCAB_SIZE) return fail(QWEN_E_ARG, "token out of range");
+    if (pos < 0 || pos >= SEQ_LEN) return fail(QWEN_E_ARG, "pos out of range [0, SEQ_LEN)");
+    if (pos > c->cached) return fail(QWEN_E_STATE, "pos skips uncached positions");
+    int rc = check_sampling(sp);
+    if (rc != QWEN_OK) return rc;
+    if (!device_exact(sp))
+        return fail(QWEN_E_UNSUPPORTED, "the sharded head samples on the device: argmax, or top-p in (0, 1) with 1 <= top_k <= 64");
+    CU(cudaSetDevice(c->device));
+    fill_in(c, token, pos, sp, rng, kFlagCandidatesOnly);
+    CU(cudaMemcpyAsync(c->d_in, c->h_in, sizeof(StepIn), cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemsetAsync(&c->d_out->n_done, 0, sizeof(int), c->stream));
+    c->shard_pos0 = pos;
+    c->shard_steps = 0;
+    c->last_k = shard_k(sp);
+    return c->last_k;
+}
+
+extern "C" int qwen_shard_decode(qwen_t* c) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (c->shard_pos0 < 0) return fail(QWEN_E_STATE, "qwen_shard_begin first");
+    if (c->shard_pos0 + c->shard_steps >= SEQ_LEN) return fail(QWEN_E_ARG, "position reaches SEQ_LEN");
+    CU(cudaSetDevice(c->device));
+    return launch_decode(c);
+}
+
+extern "C" int qwen_shard_candidates(qwen_t* c, float* values_dev, int* ids_dev) {
+    if (!c || !values_dev || !ids_dev) return fail(QWEN_E_ARG, "NULL argument");
+    CU(cudaSetDevice(c->device));
+    CU(cudaMemcpyAsync(values_dev, c->top_v, (size_t)c->last_k * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    CU(cudaMemcpyAsync(ids_dev, c->top_i, (size_t)c->last_k * sizeof(int), cudaMemcpyDeviceToDevice, c->stream));
+    return QWEN_OK;
+}
+
+extern "C" int qwen_shard_merge(qwen_t* c, const float* values_dev, const int* ids_dev, int n_ranks, int stride) {
+    if (!c || !values_dev || !ids_dev) return fail(QWEN_E_ARG, "NULL argument");
+    if (n_ranks < 1 || n_ranks * c->last_k > 2 * kMergeThreads) return fail(QWEN_E_ARG, "n_ranks x k exceeds 512 candidates");
+    if (stride < c->last_k) return fail(QWEN_E_ARG, "stride below k");
+    CU(cudaSetDevice(c->device));
+    shard_merge_kernel<<<1, kMergeThreads, 0, c->stream>>>(values_dev, ids_dev, n_ranks, c->last_k, stride, c->d_in, c->d_out, c->tokens,
+                                                           SEQ_LEN);
+    CU(cudaGetLastError());
+    c->shard_steps++;
+    return QWEN_OK;
+}
+
+extern "C" int qwen_shard_finish(qwen_t* c, int* tokens_host, int n, unsigned long long* rng_state) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (c->shard_pos0 < 0) return fail(QWEN_E_STATE, "qwen_shard_begin first");
+    if (n < 0 || n > c->shard_steps) return fail(QWEN_E_ARG, "more tokens requested than steps merged");
+    CU(cudaSetDevice(c->device));
+    if (n) CU(cudaMemcpyAsync(c->h_tokens, c->tokens, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaMemcpyAsync(c->h_out, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+    const int pos0 = c->shard_pos0, steps = c->shard_steps;
+    c->shard_pos0 = -1;
+    int rc = check_step(c);
+    if (rc != QWEN_OK) return rc;
+    if (tokens_host && n) memcpy(tokens_host, c->h_tokens, (size_t)n * sizeof(int));
+    if (rng_state) *rng_state = c->h_out->rng;
+    c->cached = pos0 + steps;
+    return QWEN_OK;
+}
+
 extern "C" int qwen_debug_capture(qwen_t* c, int enable) {
     // the residual stream and the projections of the last launch stay in the
     // exchange buffers; nothing extra to keep
@@ -1154,28 +1128,10 @@ extern "C" int qwen_debug_read(qwen_t* c, float* resid, float* qkv) {
         for (size_t i = 0; i < n; i++) { const uint32_t u = (uint32_t)w[i]; memcpy(&dst[i], &u, 4); }
         return QWEN_OK;
     };
-    if (c->cluster) return fail(QWEN_E_UNSUPPORTED, "the cluster layout keeps no whole-vector copy of the residual stream");
     int rc = QWEN_OK;
-    if (resid && c->fused) {   // x_1 .. x_L of the last launch (parity of its sequence number)
-        StepOut o{};
-        CU(cudaMemcpy(&o, c->d_out, sizeof(StepOut), cudaMemcpyDeviceToHost));
-        const uint32_t par = (o.seq - 1u) & 1u;
-        CU(cudaMemcpy(resid, c->params.xacc + ((size_t)par * (N_LAYERS + 1) + 1) * DIM, (size_t)N_LAYERS * DIM * sizeof(float),
-                      cudaMemcpyDeviceToHost));
-        resid = nullptr;
-    }
     if (resid) rc = take(c->params.xw + DIM, (size_t)N_LAYERS * DIM, resid);       // residual after layer l = x_{l+1}
     if (rc == QWEN_OK && qkv) rc = take(c->params.qkvw, (size_t)N_LAYERS * 4096, qkv);
     return rc;
-}
-
-extern "C" int qwen_decode_info(const qwen_t* c, int* layout, int* grid, int* clusters, int* probe) {
-    if (!c) return fail(QWEN_E_ARG, "NULL handle");
-    if (layout) *layout = c->cluster ? 2 : (c->fused ? 1 : 0);
-    if (grid) *grid = c->grid;
-    if (clusters) *clusters = c->ncl;
-    if (probe) *probe = c->cl_probe;
-    return QWEN_OK;
 }
 
 extern "C" int qwen_debug_inject_wait(qwen_t* c, unsigned long long wait_ns, int group) {
@@ -1213,10 +1169,10 @@ extern "C" int qwen_trace_read(qwen_t* c, unsigned long long* out, int max_entri
 
 extern "C" int qwen_debug_chunk_counts(qwen_t* c, int* out, int max_ctas) {
     if (!c || !out) return fail(QWEN_E_ARG, "NULL argument");
-    if (max_ctas < c->grid) return fail(QWEN_E_ARG, "buffer too small");
+    if (max_ctas < c->nsm) return fail(QWEN_E_ARG, "buffer too small");
     CU(cudaSetDevice(c->device));
-    CU(cudaMemcpy(out, c->chunk_count, (size_t)2 * c->grid * sizeof(int), cudaMemcpyDeviceToHost));
-    return c->grid;
+    CU(cudaMemcpy(out, c->chunk_count, (size_t)2 * c->nsm * sizeof(int), cudaMemcpyDeviceToHost));
+    return c->nsm;
 }
 
 // ---------------------------------------------------------------------------

@@ -42,7 +42,6 @@ def main():
     spec.loader.exec_module(qb)
     import numpy as np
     eng = qb.Engine(qb.default_checkpoint(0), a.device)
-    print("decode launch:", eng.decode_info())
     if a.batch:
         eng.batch_init(a.batch)
         for slot in range(a.batch):

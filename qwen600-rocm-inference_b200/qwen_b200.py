@@ -60,6 +60,12 @@ _SIGS = {
     "qwen_cached_positions": (_c.c_int, [_P]),
     "qwen_set_vocab_shard": (_c.c_int, [_P, _c.c_int, _c.c_int]),
     "qwen_shard_topk": (_c.c_int, [_P, _c.c_int, _P, _P]),
+    "qwen_stream": (_P, [_P]),
+    "qwen_shard_begin": (_c.c_int, [_P, _c.c_int, _c.c_int, _P, _c.c_ulonglong]),
+    "qwen_shard_decode": (_c.c_int, [_P]),
+    "qwen_shard_candidates": (_c.c_int, [_P, _P, _P]),
+    "qwen_shard_merge": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int]),
+    "qwen_shard_finish": (_c.c_int, [_P, _P, _c.c_int, _c.POINTER(_c.c_ulonglong)]),
     "qwen_sample_host": (_c.c_int, [_P, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _c.POINTER(_c.c_int)]),
     "qwen_sample_candidates": (_c.c_int, [_P, _P, _c.c_int, _P, _c.POINTER(_c.c_ulonglong), _c.POINTER(_c.c_int)]),
     "qwen_debug_chunk_counts": (_c.c_int, [_P, _P, _c.c_int]),
@@ -67,7 +73,6 @@ _SIGS = {
     "qwen_debug_read": (_c.c_int, [_P, _P, _P]),
     "qwen_trace_enable": (_c.c_int, [_P, _c.c_int]),
     "qwen_debug_inject_wait": (_c.c_int, [_P, _c.c_ulonglong, _c.c_int]),
-    "qwen_decode_info": (_c.c_int, [_P, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]),
     "qwen_trace_read": (_c.c_int, [_P, _P, _c.c_int]),
     "qwen_gemv_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
     "qwen_gemv_bf16_static": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _P]),
@@ -364,12 +369,6 @@ class Engine:
 
     TRACE_STRIDE = 576
 
-    def decode_info(self):
-        """{'layout': 'tagged' | 'fused' | 'cluster', 'grid': CTAs, 'clusters': ..., 'probe': ...}"""
-        v = [ctypes.c_int() for _ in range(4)]
-        _check(self._lib.qwen_decode_info(self._h, *[ctypes.byref(x) for x in v]))
-        return {"layout": ["tagged", "fused", "cluster"][v[0].value], "grid": v[1].value, "clusters": v[2].value, "probe": v[3].value}
-
     def debug_inject_wait(self, wait_ns=0, group=-1):
         """Failure testing: wait limit for later launches (0 = default) and a KV
         head whose CTAs withhold their layer-0 q|k|v (-1 = none)."""
@@ -385,6 +384,33 @@ class Engine:
         if n < 0:
             _check(n)
         return out[:n].reshape(-1, self.TRACE_STRIDE)
+
+    # ---- device-resident sharded head (see sharding.py) ----
+    @property
+    def stream(self):
+        """The handle's cudaStream_t (an int), for work that must follow its launches."""
+        return self._lib.qwen_stream(self._h) or 0
+
+    def shard_begin(self, token, pos, sampling=GREEDY, rng=0):
+        k = self._lib.qwen_shard_begin(self._h, int(token), int(pos), ctypes.byref(sampling), int(rng))
+        if k < 0:
+            _check(k)
+        return k
+
+    def shard_decode(self):
+        _check(self._lib.qwen_shard_decode(self._h))
+
+    def shard_candidates(self, values_ptr, ids_ptr):
+        _check(self._lib.qwen_shard_candidates(self._h, ctypes.c_void_p(values_ptr), ctypes.c_void_p(ids_ptr)))
+
+    def shard_merge(self, values_ptr, ids_ptr, n_ranks, stride):
+        _check(self._lib.qwen_shard_merge(self._h, ctypes.c_void_p(values_ptr), ctypes.c_void_p(ids_ptr), int(n_ranks), int(stride)))
+
+    def shard_finish(self, n):
+        toks = np.zeros(max(int(n), 1), dtype=np.int32)
+        r = ctypes.c_ulonglong()
+        _check(self._lib.qwen_shard_finish(self._h, _ptr(toks), int(n), ctypes.byref(r)))
+        return toks[:n].tolist(), r.value
 
     def set_vocab_shard(self, begin, end):
         _check(self._lib.qwen_set_vocab_shard(self._h, int(begin), int(end)))

@@ -1,11 +1,12 @@
 """Two GPUs, one process each, NCCL: the vocabulary-sharded LM head.
 
 Each rank runs the full trunk and half of the 151936 LM-head rows; per token
-the ranks all-gather their shard's top-k (logit, id) lists over NCCL and merge
-them with the same sampler math and RNG state.  The merged token stream must
-equal the single-GPU full-vocabulary stream (the trunk is bit-reproducible for
-a given grid size, so the candidates are exactly the full top-k).  Skipped
-unless two GPUs are visible.
+the ranks all-gather their shard's top-k (logit, id) lists over NCCL on the
+engine's stream and merge them on the device with the same sampler math and
+RNG state (sharding.ShardedHead: no host round trip per token).  The merged
+token stream must equal the single-GPU full-vocabulary stream (the trunk is
+bit-reproducible for a given grid size, so the candidates are exactly the full
+top-k).  Skipped unless two GPUs are visible.
 """
 import datetime
 import importlib.util
@@ -33,19 +34,6 @@ def _load(name):
     return m
 
 
-def _sampled_stream(qb, eng, sp, next_token):
-    """Prefill PROMPT, then N_STEPS sampled tokens chosen by next_token(eng, rng).
-    Each step runs with top_k 20 so the launch keeps its 20 best candidates
-    (the token the launch itself samples is not used)."""
-    eng.prefill(PROMPT[:-1], 0)
-    tok, rng, out = PROMPT[-1], 0x1234, []
-    for i in range(N_STEPS):
-        eng.decode_step(tok, len(PROMPT) - 1 + i, sp, 1)   # trunk + this handle's head rows
-        tok, rng = next_token(eng, rng)
-        out.append(tok)
-    return out
-
-
 def _worker(rank, world, port, ck, q):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -57,13 +45,9 @@ def _worker(rank, world, port, ck, q):
     eng = qb.Engine(ck, rank)
     try:
         eng.set_vocab_shard(*sh.shard_range(rank, world))
-
-        def merged(e, rng):
-            v, i = e.shard_topk(20)
-            gv, gi = sh.gather_candidates(v, i, device=torch.device("cuda", rank))
-            return sh.merge_and_sample(qb, gv, gi, sp, rng)
-
-        out = _sampled_stream(qb, eng, sp, merged)
+        eng.prefill(PROMPT[:-1], 0)
+        head = sh.ShardedHead(eng)
+        out = head.generate(PROMPT[-1], len(PROMPT) - 1, N_STEPS, sp, 0x1234)
     finally:
         eng.close()
     q.put((rank, out))
@@ -92,14 +76,12 @@ def test_vocab_sharded_head_two_gpus(qb, checkpoint):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert got[0] == got[1]
-    # one GPU, full vocabulary, the same candidate merge
+    # one GPU, full vocabulary, the device sampler
     sp = qb.Sampling(0.6, 0.95, 20)
     eng = qb.Engine(checkpoint, 0)
     try:
-        def full(e, rng):
-            v, i = e.shard_topk(20)
-            return qb.sample_candidates(v, i, sp, rng)
-        want = _sampled_stream(qb, eng, sp, full)
+        eng.prefill(PROMPT[:-1], 0)
+        want = eng.generate(PROMPT[-1], len(PROMPT) - 1, N_STEPS, sp, 0x1234)
     finally:
         eng.close()
     assert got[0] == want
