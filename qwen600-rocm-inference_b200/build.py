@@ -19,7 +19,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 CUDA_SOURCES = ["engine.cu"]
 HOST_SOURCES = ["model_format.cpp", "host_sampler.cpp", "tokenizer.cpp"]
-HEADERS = ["decode_kernel.cuh", "gemv_kernel.cuh", "gemm_tc.cuh", "prefill_kernels.cuh", "ptx.cuh", "model_format.h"]
+HEADERS = ["decode_kernel.cuh", "attention_tc5.cuh", "gemv_kernel.cuh", "gemm_tc.cuh", "prefill_kernels.cuh", "ptx.cuh", "model_format.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-Xcompiler", "-fPIC,-fopenmp", "-I", os.path.join(HERE, "..", "include")]
 

@@ -1,0 +1,274 @@
+// attention_tc5.cuh — causal GQA attention of a prompt pass on the sm_100a
+// tensor cores (tcgen05.mma, kind::f16: bf16 operands from shared memory,
+// fp32 accumulators in TMEM).  No reference counterpart: the reference runs
+// its decode attention once per prompt token (main.cu:141-145 over
+// qwen_model.cuh:551-614).
+//
+// One CTA per (64 query positions, KV head hk): the 128 rows of its tiles are
+// the 64 positions of q head 2 hk (rows 0-63) and of q head 2 hk + 1 (rows
+// 64-127), so every K/V tile serves both heads.  Two passes over the key
+// tiles (64 keys each, up to the block's last query; heaviest blocks first):
+//   pass 1  S = Q K^T into TMEM; each softmax thread reads its row (one TMEM
+//           lane) and keeps the row's running max and sum of exp (base 2, the
+//           1/sqrt(d) scale folded into the exponent) — no cross-thread step;
+//   pass 2  S again; P = exp2(S c - max c) / sum, final, written as two bf16
+//           parts into shared memory; O += P V accumulates in TMEM across all
+//           tiles with no rescaling (that is what the first pass buys).
+// Q enters as two bf16 parts side by side along K (K' = 256 against K read
+// twice), P likewise (K' = 128 against V^T read twice): 16 mantissa bits of
+// each fp32 operand, relative error <= 2^-17 (K and V are bf16 in the cache).
+// Both tcgen05 operands are K-major SW128 tiles: Q and P written by threads in
+// the layout the TMA engine produces, K tiles by TMA from the cache
+// ([head][position][dim]), V tiles by TMA from a transposed copy of the
+// layer's V ([head][dim][position], transpose_v_kernel) so that keys are
+// contiguous.  Warps: 0 TMA producer, 1 TMEM allocator and MMA issuer, 2-5
+// softmax and epilogue (warp w reads TMEM lanes 32 (w % 4) ..).  Every wait is
+// bounded: on expiry the thread sets *err and stops waiting; the TMEM
+// allocation is always released.
+#pragma once
+#include "gemm_tc.cuh"
+#include "prefill_kernels.cuh"
+
+namespace qb {
+namespace pf {
+
+constexpr int kA5Keys = 64;                       // keys per tile
+constexpr int kA5Stages = 2;                      // K (and V) tiles in flight
+constexpr int kA5Threads = 192;
+constexpr int kA5QBytes = 4 * 128 * 128;          // Q: 4 SW128 blocks (part, dim half) of 128 rows x 128 B
+constexpr int kA5KBytes = 2 * kA5Keys * 128;      // a K tile: 2 blocks (dim halves) of 64 rows x 128 B
+constexpr int kA5VBytes = HEAD_DIM * 128;         // a V^T tile: 128 rows (dims) x 128 B (64 keys)
+constexpr int kA5PBytes = 2 * 128 * 128;          // a P buffer: 2 blocks (parts) of 128 rows x 128 B
+struct A5Layout {
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kA5QBytes;
+    static constexpr int kV = kK + kA5Stages * kA5KBytes;
+    static constexpr int kP = kV + kA5Stages * kA5VBytes;
+    static constexpr int kBar = kP + 2 * kA5PBytes;   // barriers after the 1024-aligned tiles
+    static constexpr int kSmem = kBar + 32 * 8 + 1024;
+};
+static_assert(A5Layout::kSmem <= 227 * 1024, "attention tiles must fit one CTA's shared memory");
+
+// Byte offset of 16-byte chunk `c` of row `r` in a K-major SW128 tile (rows of
+// 128 B, chunk index XOR row within each 8-row group of 1024 B).
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// V of one layer, [head][position][dim] -> [head][dim][position] for positions
+// [0, n): 64 x 64 tiles through shared memory.  grid (ceil(n / 64), 2, N_KV_HEADS), block (64, 8).
+__global__ void transpose_v_kernel(const uint16_t* __restrict__ vc_l, uint16_t* __restrict__ vt, int n) {
+    __shared__ uint16_t t[64][66];
+    const int p0 = blockIdx.x * 64, d0 = blockIdx.y * 64, hk = blockIdx.z;
+    const uint16_t* src = vc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
+    for (int i = threadIdx.y; i < 64; i += 8) {
+        const int p = p0 + i;
+        t[i][threadIdx.x] = p < n ? src[(size_t)p * HEAD_DIM + d0 + threadIdx.x] : (uint16_t)0;
+    }
+    __syncthreads();
+    uint16_t* dst = vt + ((size_t)hk * HEAD_DIM + d0) * SEQ_LEN;
+    for (int i = threadIdx.y; i < 64; i += 8)
+        if (p0 + threadIdx.x < n) dst[(size_t)i * SEQ_LEN + p0 + threadIdx.x] = t[threadIdx.x][i];
+}
+
+// grid: rows / 64 * N_KV_HEADS CTAs, kA5Threads threads, A5Layout::kSmem bytes.
+// map_k: the layer's K cache as [N_KV_HEADS * SEQ_LEN rows][128], boxes 64 x 64;
+// map_v: the transposed V as [N_KV_HEADS * 128 rows][SEQ_LEN], boxes 128 x 64.
+__global__ void __launch_bounds__(kA5Threads, 1)
+attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v, const float* __restrict__ Q,
+                     int pos0, uint16_t* __restrict__ As, int ld_as, uint32_t* err) {
+    using namespace qb::tc;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + A5Layout::kBar);
+    uint64_t* kfull = bars;            // [kA5Stages]
+    uint64_t* kempty = bars + 2;       // [kA5Stages]
+    uint64_t* vfull = bars + 4;        // [kA5Stages]
+    uint64_t* vempty = bars + 6;       // [kA5Stages]
+    uint64_t* sfull = bars + 8;        // [2] S buffer written (MMA -> softmax)
+    uint64_t* sempty = bars + 10;      // [2] S buffer read (softmax -> MMA), 4 arrivals
+    uint64_t* pfull = bars + 12;       // [2] P buffer written (softmax -> MMA), 4 arrivals
+    uint64_t* pempty = bars + 14;      // [2] P buffer read by the PV MMAs (MMA -> softmax)
+    uint64_t* ofull = bars + 16;       // O complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int nqb = gridDim.x / N_KV_HEADS;
+    const int qb = nqb - 1 - (int)blockIdx.x / N_KV_HEADS, hk = (int)blockIdx.x % N_KV_HEADS;
+    const int q0 = qb * kAttBlock;
+    const int last = min(pos0 + q0 + kAttBlock - 1, SEQ_LEN - 1);
+    const int T = last / kA5Keys + 1;   // key tiles
+
+    if (tid == 0) {
+        for (int s = 0; s < kA5Stages; s++) { mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1); mbar_init(&vfull[s], 1); mbar_init(&vempty[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&sfull[b], 1); mbar_init(&sempty[b], 4); mbar_init(&pfull[b], 4); mbar_init(&pempty[b], 1); }
+        mbar_init(ofull, 1);
+        fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_k) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_v) : "memory");
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 256);   // S[0] cols 0-63, S[1] 64-127, O 128-255
+    // Q of the block's 128 rows, split into hi and mid bf16 parts: block j = part
+    // (j >> 1), dims 64 (j & 1) .. +63
+    for (int e = tid; e < 128 * 16; e += kA5Threads) {
+        const int m = e >> 4, c8 = e & 15;                 // row, 8-dim chunk of the 128 dims
+        const float* src = Q + (size_t)(q0 + (m & 63)) * Q_DIM + 128 * (2 * hk + (m >> 6)) + 8 * c8;
+        const float4 a = *(const float4*)src, b = *(const float4*)(src + 4);
+        uint32_t h[4], md[4], lo[4];
+        split3x2(a.x, a.y, h[0], md[0], lo[0]);
+        split3x2(a.z, a.w, h[1], md[1], lo[1]);
+        split3x2(b.x, b.y, h[2], md[2], lo[2]);
+        split3x2(b.z, b.w, h[3], md[3], lo[3]);
+        const int blk = c8 >> 3, c = c8 & 7;
+        *(uint4*)(smem + A5Layout::kQ + blk * 16384 + sw128(m, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *(uint4*)(smem + A5Layout::kQ + (2 + blk) * 16384 + sw128(m, c)) = make_uint4(md[0], md[1], md[2], md[3]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // K tiles 0..T-1 twice (both passes), V tiles 0..T-1 alongside the second
+            bool ok = true;
+            for (int u = 0; u < 2 * T && ok; u++) {
+                const int t = u < T ? u : u - T;
+                const uint32_t s = (uint32_t)u % kA5Stages;
+                if (u >= kA5Stages && !mbar_wait(&kempty[s], ((u / kA5Stages) - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 16u); ok = false; break; }
+                uint8_t* kd = smem + A5Layout::kK + s * kA5KBytes;
+                mbar_arrive_expect_tx(&kfull[s], kA5KBytes);
+                tma_load_2d(kd, &map_k, 0, hk * SEQ_LEN + t * kA5Keys, &kfull[s]);
+                tma_load_2d(kd + kA5Keys * 128, &map_k, 64, hk * SEQ_LEN + t * kA5Keys, &kfull[s]);
+                if (u >= T) {
+                    const uint32_t sv = (uint32_t)t % kA5Stages;
+                    if (t >= kA5Stages && !mbar_wait(&vempty[sv], ((t / kA5Stages) - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 16u); ok = false; break; }
+                    mbar_arrive_expect_tx(&vfull[sv], kA5VBytes);
+                    tma_load_2d(smem + A5Layout::kV + sv * kA5VBytes, &map_v, t * kA5Keys, hk * HEAD_DIM, &vfull[sv]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t id_s = idesc_bf16_f32(128, kA5Keys), id_o = idesc_bf16_f32(128, HEAD_DIM);
+            bool ok = true;
+            // O += P V for tile t: P buffer t & 1 written by the softmax warps, V^T stage t % kA5Stages
+            auto pv = [&](int t) {
+                const uint32_t pb = (uint32_t)t & 1u, puse = (uint32_t)t >> 1, sv = (uint32_t)t % kA5Stages;
+                if (!mbar_wait(&pfull[pb], puse & 1u, tc::kWaitNs) || !mbar_wait(&vfull[sv], (t / kA5Stages) & 1u, tc::kWaitNs)) {
+                    atomicOr(err, 32u);
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t pa = smem_addr(smem + A5Layout::kP + pb * kA5PBytes), vb = smem_addr(smem + A5Layout::kV + sv * kA5VBytes);
+                #pragma unroll
+                for (int j = 0; j < 2; j++)
+                    #pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(tmem + 128, kmajor_sw128_desc(pa + j * 16384 + kk * 32), kmajor_sw128_desc(vb + kk * 32), id_o,
+                                 (t | j | kk) != 0 ? 1u : 0u);
+                mma_commit(&vempty[sv]);
+                mma_commit(&pempty[pb]);
+                return true;
+            };
+            // S of step u (tiles 0..T-1, then again), and in the second pass the
+            // P V product of the previous tile, so the softmax of one tile
+            // overlaps the S product of the next
+            for (int u = 0; u < 2 * T && ok; u++) {
+                const uint32_t b = (uint32_t)u & 1u, use = (uint32_t)u >> 1, s = (uint32_t)u % kA5Stages;
+                if (use > 0 && !mbar_wait(&sempty[b], (use - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 32u); ok = false; break; }
+                if (!mbar_wait(&kfull[s], (u / kA5Stages) & 1u, tc::kWaitNs)) { atomicOr(err, 32u); ok = false; break; }
+                tc_fence_after();
+                // S[b] = Q K^T: K' = 256 (Q hi | mid) against the K tile read twice
+                const uint32_t qa = smem_addr(smem + A5Layout::kQ), kb = smem_addr(smem + A5Layout::kK + s * kA5KBytes);
+                #pragma unroll
+                for (int j = 0; j < 4; j++)
+                    #pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(tmem + b * kA5Keys, kmajor_sw128_desc(qa + j * 16384 + kk * 32),
+                                 kmajor_sw128_desc(kb + (j & 1) * (kA5Keys * 128) + kk * 32), id_s, (j | kk) != 0 ? 1u : 0u);
+                mma_commit(&kempty[s]);
+                mma_commit(&sfull[b]);
+                if (u - 1 >= T) ok = pv(u - 1 - T);
+            }
+            if (ok && T > 0) pv(T - 1);
+            mma_commit(ofull);   // O complete (or abandoned: *err is set)
+        }
+    } else {
+        // softmax: this thread's row m = TMEM lane 32 q + lane
+        const int q = warp & 3, m = 32 * q + lane;
+        const int qp = pos0 + q0 + (m & 63);               // its query position
+        const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+        const float c2 = 1.4426950408889634f / sqrtf((float)HEAD_DIM);
+        float rmax = -INFINITY, rsum = 0.f, mc = 0.f, inv = 0.f;
+        bool ok = true;
+        for (int u = 0; u < 2 * T; u++) {
+            const int t = u < T ? u : u - T;
+            const uint32_t b = (uint32_t)u & 1u, use = (uint32_t)u >> 1;
+            if (ok && !mbar_wait(&sfull[b], use & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
+            tc_fence_after();
+            float v[64];
+            {
+                float h0[32], h1[32];
+                tmem_ld32(tmem + lane_off + b * kA5Keys, h0);
+                tmem_ld32(tmem + lane_off + b * kA5Keys + 32, h1);
+                #pragma unroll
+                for (int i = 0; i < 32; i++) { v[i] = h0[i]; v[32 + i] = h1[i]; }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sempty[b]);
+            const int k0 = t * kA5Keys;
+            #pragma unroll
+            for (int i = 0; i < 64; i++) if (k0 + i > qp) v[i] = -INFINITY;   // causal mask (also past the block's last key)
+            if (u < T) {
+                float mx = rmax;
+                #pragma unroll
+                for (int i = 0; i < 64; i++) mx = fmaxf(mx, v[i]);
+                float ps = 0.f;
+                const float mcn = mx * c2;
+                #pragma unroll
+                for (int i = 0; i < 64; i++) ps += exp2f(fmaf(v[i], c2, -mcn));
+                rsum = fmaf(rsum, exp2f(fmaf(rmax, c2, -mcn)), ps);   // rmax = -inf on the first tile: factor 0
+                rmax = mx;
+                if (u == T - 1) { mc = rmax * c2; inv = 1.0f / rsum; }
+            } else {
+                // P = exp2(S c - max c) / sum, two bf16 parts, into P buffer t & 1
+                const uint32_t pb = (uint32_t)t & 1u, puse = (uint32_t)t >> 1;
+                if (ok && puse > 0 && !mbar_wait(&pempty[pb], (puse - 1) & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
+                uint8_t* pbuf = smem + A5Layout::kP + pb * kA5PBytes;
+                #pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    uint32_t h[4], md[4], lo[4];
+                    #pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float p0 = exp2f(fmaf(v[8 * c + 2 * j], c2, -mc)) * inv, p1 = exp2f(fmaf(v[8 * c + 2 * j + 1], c2, -mc)) * inv;
+                        split3x2(p0, p1, h[j], md[j], lo[j]);
+                    }
+                    *(uint4*)(pbuf + sw128(m, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+                    *(uint4*)(pbuf + 16384 + sw128(m, c)) = make_uint4(md[0], md[1], md[2], md[3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pfull[pb]);
+            }
+        }
+        // epilogue: O row m (final, normalised) -> the O projection's operand, split
+        if (ok && !mbar_wait(ofull, 0, 2 * tc::kWaitNs)) atomicOr(err, 64u);
+        tc_fence_after();
+        uint16_t* arow = As + (size_t)(q0 + (m & 63)) * ld_as + 128 * (2 * hk + (m >> 6));
+        #pragma unroll 1
+        for (int c = 0; c < HEAD_DIM; c += 32) {
+            float o[32];
+            tmem_ld32(tmem + lane_off + 128 + c, o);
+            #pragma unroll
+            for (int i = 0; i < 32; i += 2) put_split2(arow, c + i, o[i], o[i + 1]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+}  // namespace pf
+}  // namespace qb

@@ -28,6 +28,7 @@
 #include "../../include/qwen_b200.h"
 #include "decode_kernel.cuh"
 #include "gemv_kernel.cuh"
+#include "attention_tc5.cuh"
 #include "gemm_tc.cuh"
 #include "prefill_kernels.cuh"
 #include "model_format.h"
@@ -249,6 +250,8 @@ struct qwen_ctx {
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
+    bool att5 = false;          // prompt-pass attention on tcgen05 (attention_tc5.cuh) instead of mma.sync
+    uint16_t* vt = nullptr;     // the layer's V transposed ([head][dim][position]) for the tcgen05 attention
     int last_k = 0;
 };
 
@@ -257,7 +260,7 @@ static void ctx_free(qwen_t* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->params.trace) cudaFree(c->params.trace);
-    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
+    void* dev[] = {c->pf_x, c->pf_y, c->pf_q, c->pf_xn, c->pf_as, c->pf_hs, c->wgu, c->vt, c->wblock, c->wo_g, c->kc, c->vc, c->rope, c->xchg, c->logits,
                    c->cand_v, c->top_v, c->cand_i, c->top_i, c->prompt, c->tokens, c->ctr, c->d_in, c->d_out, c->chunk_count};
     for (void* p : dev) if (p) cudaFree(p);
     void* host[] = {c->h_in, c->h_out, c->h_logits, c->h_tokens};
@@ -387,6 +390,8 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     P.debug_skip = -1;
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
+    // prompt-pass attention: "tc5" selects the tcgen05 kernel, "mma" the mma.sync one
+    if (const char* e = getenv("QWEN_B200_PREFILL_ATTN")) c->att5 = strcmp(e, "tc5") == 0;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -650,6 +655,7 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
 }
 
 static int gemm_check(qwen_t* c);
+static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, int pos0, int m, int rows, cudaStream_t st);
 static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st, int parts);
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
@@ -671,6 +677,9 @@ static int pf_alloc(qwen_t* c) {
     TRY(dalloc(&c->pf_hs, (size_t)kMaxRows * 3 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_xn, (size_t)DIM));
     CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
+    CU(cudaFuncSetAttribute(attention_tc5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
+    TRY(dalloc(&c->vt, (size_t)N_KV_HEADS * HEAD_DIM * SEQ_LEN));
+    CU(cudaMemset(c->vt, 0, (size_t)N_KV_HEADS * HEAD_DIM * SEQ_LEN * sizeof(uint16_t)));
     return gemm_prepare(c->device);
 }
 
@@ -727,6 +736,8 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
             attention_rows_kernel<<<m * N_KV_HEADS * S, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, S,
                                                                                  c->pf_as, kLdAs, io->part);
             if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_as, kLdAs);
+        } else if (c->att5) {
+            if ((rc = attention_tc5(c, kc_l, vc_l, pos0, m, rows, st)) != QWEN_OK) return rc;
         } else {
             attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_as,
                                                                                                        kLdAs);
@@ -1378,6 +1389,24 @@ static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs
     bm.end[0] = bm.end[1] = bm.end[2] = 2 * HIDDEN_DIM / 256;
     return gemm_launch<256, false, 1>(ma, bm, Hs, ld_hs, M, parts * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev], st,
                                       g_gemm_err[dev]);
+}
+
+// The prompt pass's causal attention on tcgen05 (attention_tc5.cuh): the
+// layer's V for positions [0, pos0 + m) transposed into c->vt, then one CTA
+// per (64 rows, KV head).  Its error word is the GEMMs' (checked after the pass).
+static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, int pos0, int m, int rows, cudaStream_t st) {
+    using namespace qb::pf;
+    const int dev = c->device;
+    const int n = pos0 + m;
+    transpose_v_kernel<<<dim3((n + 63) / 64, 2, N_KV_HEADS), dim3(64, 8), 0, st>>>(vc_l, c->vt, n);
+    CUtensorMap mk, mv;
+    if (!cached_map(&mk, kc_l, (uint64_t)N_KV_HEADS * SEQ_LEN, HEAD_DIM, HEAD_DIM, kA5Keys) ||
+        !cached_map(&mv, c->vt, (uint64_t)N_KV_HEADS * HEAD_DIM, SEQ_LEN, SEQ_LEN, HEAD_DIM))
+        return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    attention_tc5_kernel<<<rows / kAttBlock * N_KV_HEADS, kA5Threads, A5Layout::kSmem, st>>>(mk, mv, c->pf_q, pos0, c->pf_as, 3 * HIDDEN_DIM,
+                                                                                           g_gemm_err[dev]);
+    CU(cudaGetLastError());
+    return QWEN_OK;
 }
 
 // C[M][N] (rows ldc apart) = A[M][K] (rows lda apart) . (B[N][Kb] repeated

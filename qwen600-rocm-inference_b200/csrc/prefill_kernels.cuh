@@ -478,18 +478,20 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_level_kernel(const float
 // accumulate).  One CTA per (64 query rows, KV head): its 8 warps cover both q
 // heads of the group (warp w: head 2 hk + w / 4, rows 16 (w % 4) .. +15), so
 // each K/V tile is loaded once for two heads.  S = Q K^T with Q split into
-// three bf16 parts (K is bf16 in the cache: exact), online softmax on the
+// kAttParts bf16 parts (K is bf16 in the cache: exact), online softmax on the
 // accumulator fragments in base 2 with the 1/sqrt(d) scale folded into the
-// exponent, O += P V with P split into three bf16 parts (V exact) —
-// fp32-level numerics.  K/V tiles are double-buffered (cp.async, 16-byte
+// exponent, O += P V with P split into kAttParts bf16 parts (V exact).  K/V tiles are double-buffered (cp.async, 16-byte
 // row pads: conflict-free ldmatrix, V through .trans); the CTAs with the most
 // causal work are numbered first.
 // ---------------------------------------------------------------------------
 constexpr int kTcRowE = HEAD_DIM + 8;     // padded smem row, elements (272 B)
 constexpr int kTcThreads = 256;
+// bf16 parts of Q and P in the attention products: 2 (hi + mid) keeps 16
+// mantissa bits of each (relative error <= 2^-17); K and V are bf16 already
+constexpr int kAttParts = 2;
 
 struct AttTcSmem {
-    uint16_t q[2][3][kAttBlock][kTcRowE];    // per q head: hi, mid, lo parts of the 64 query rows
+    uint16_t q[2][kAttParts][kAttBlock][kTcRowE];    // per q head: the bf16 parts (hi, mid) of the 64 query rows
     uint16_t k[2][kAttBlock][kTcRowE];       // two K tiles (double buffer)
     uint16_t v[2][kAttBlock][kTcRowE];
 };
@@ -543,7 +545,7 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
         split3x2(v.z, v.w, h1, m1, l1);
         *(uint2*)&S.q[hh][0][r][c] = make_uint2(h0, h1);
         *(uint2*)&S.q[hh][1][r][c] = make_uint2(m0, m1);
-        *(uint2*)&S.q[hh][2][r][c] = make_uint2(l0, l1);
+        if constexpr (kAttParts > 2) *(uint2*)&S.q[hh][kAttParts - 1][r][c] = make_uint2(l0, l1);
     }
     const int rowA = 16 * wr + (lane & 15);                       // ldmatrix row of this lane for A tiles
     const uint32_t qa = smem_addr(&S.q[hl][0][rowA][(lane >> 4) * 8]);
@@ -574,15 +576,15 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
         for (int n = 0; n < 8; n++) { sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f; }
         #pragma unroll
         for (int kt = 0; kt < HEAD_DIM / 16; kt++) {
-            uint32_t a[3][4];
+            uint32_t a[kAttParts][4];
             #pragma unroll
-            for (int p = 0; p < 3; p++) ldsm_x4(qa + p * kQPart + kt * 32, a[p][0], a[p][1], a[p][2], a[p][3]);
+            for (int p = 0; p < kAttParts; p++) ldsm_x4(qa + p * kQPart + kt * 32, a[p][0], a[p][1], a[p][2], a[p][3]);
             #pragma unroll
             for (int np = 0; np < 4; np++) {   // keys 16np .. 16np+15: two n-tiles
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(kbuf + np * 16 * kTcRowE * 2 + kt * 32, b0, b1, b2, b3);
                 #pragma unroll
-                for (int p = 0; p < 3; p++) {
+                for (int p = 0; p < kAttParts; p++) {
                     mma_bf16_16816(sc[2 * np], a[p][0], a[p][1], a[p][2], a[p][3], b0, b1);
                     mma_bf16_16816(sc[2 * np + 1], a[p][0], a[p][1], a[p][2], a[p][3], b2, b3);
                 }
@@ -648,7 +650,7 @@ attention_tc_kernel(const float* __restrict__ Q, int pos0, const uint16_t* __res
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_trans(vbuf + kt * 16 * kTcRowE * 2 + np * 32, b0, b1, b2, b3);
                 #pragma unroll
-                for (int p = 0; p < 3; p++) {
+                for (int p = 0; p < kAttParts; p++) {
                     mma_bf16_16816(o[2 * np], a[p][0], a[p][1], a[p][2], a[p][3], b0, b1);
                     mma_bf16_16816(o[2 * np + 1], a[p][0], a[p][1], a[p][2], a[p][3], b2, b3);
                 }
