@@ -21,8 +21,11 @@
 // the layout the TMA engine produces, K tiles by TMA from the cache
 // ([head][position][dim]), V tiles by TMA from a transposed copy of the
 // layer's V ([head][dim][position], transpose_v_kernel) so that keys are
-// contiguous.  Warps: 0 TMA producer, 1 TMEM allocator and MMA issuer, 2-5
-// softmax and epilogue (warp w reads TMEM lanes 32 (w % 4) ..).  Every wait is
+// contiguous.  Warps: 0 TMA producer, 1 TMEM allocator and MMA issuer, 2-9
+// softmax and epilogue: warp w reads TMEM lanes 32 (w % 4) .. (the rows it may
+// access), warps 2-5 columns 0-31 of each S tile and warps 6-9 columns 32-63,
+// each keeping its half-row's max and sum; the halves combine once, after the
+// first pass, through shared memory.  Every wait is
 // bounded: on expiry the thread sets *err and stops waiting; the TMEM
 // allocation is always released.
 #pragma once
@@ -34,7 +37,7 @@ namespace pf {
 
 constexpr int kA5Keys = 64;                       // keys per tile
 constexpr int kA5Stages = 2;                      // K (and V) tiles in flight
-constexpr int kA5Threads = 192;
+constexpr int kA5Threads = 320;                   // warps 0 producer, 1 MMA, 2-9 softmax (two per TMEM lane quarter)
 constexpr int kA5QBytes = 4 * 128 * 128;          // Q: 4 SW128 blocks (part, dim half) of 128 rows x 128 B
 constexpr int kA5KBytes = 2 * kA5Keys * 128;      // a K tile: 2 blocks (dim halves) of 64 rows x 128 B
 constexpr int kA5VBytes = HEAD_DIM * 128;         // a V^T tile: 128 rows (dims) x 128 B (64 keys)
@@ -45,7 +48,8 @@ struct A5Layout {
     static constexpr int kV = kK + kA5Stages * kA5KBytes;
     static constexpr int kP = kV + kA5Stages * kA5VBytes;
     static constexpr int kBar = kP + 2 * kA5PBytes;   // barriers after the 1024-aligned tiles
-    static constexpr int kSmem = kBar + 32 * 8 + 1024;
+    static constexpr int kStat = kBar + 32 * 8;        // [2 halves][128 rows][max, sum] after the first pass
+    static constexpr int kSmem = kStat + 2 * 128 * 2 * 4 + 1024;
 };
 static_assert(A5Layout::kSmem <= 227 * 1024, "attention tiles must fit one CTA's shared memory");
 
@@ -86,8 +90,8 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
     uint64_t* vfull = bars + 4;        // [kA5Stages]
     uint64_t* vempty = bars + 6;       // [kA5Stages]
     uint64_t* sfull = bars + 8;        // [2] S buffer written (MMA -> softmax)
-    uint64_t* sempty = bars + 10;      // [2] S buffer read (softmax -> MMA), 4 arrivals
-    uint64_t* pfull = bars + 12;       // [2] P buffer written (softmax -> MMA), 4 arrivals
+    uint64_t* sempty = bars + 10;      // [2] S buffer read (softmax -> MMA), 8 arrivals
+    uint64_t* pfull = bars + 12;       // [2] P buffer written (softmax -> MMA), 8 arrivals
     uint64_t* pempty = bars + 14;      // [2] P buffer read by the PV MMAs (MMA -> softmax)
     uint64_t* ofull = bars + 16;       // O complete
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
@@ -100,7 +104,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
 
     if (tid == 0) {
         for (int s = 0; s < kA5Stages; s++) { mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1); mbar_init(&vfull[s], 1); mbar_init(&vempty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&sfull[b], 1); mbar_init(&sempty[b], 4); mbar_init(&pfull[b], 4); mbar_init(&pempty[b], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&sfull[b], 1); mbar_init(&sempty[b], 8); mbar_init(&pfull[b], 8); mbar_init(&pempty[b], 1); }
         mbar_init(ofull, 1);
         fence_barrier_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(&map_k) : "memory");
@@ -195,10 +199,11 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
             mma_commit(ofull);   // O complete (or abandoned: *err is set)
         }
     } else {
-        // softmax: this thread's row m = TMEM lane 32 q + lane
-        const int q = warp & 3, m = 32 * q + lane;
+        // softmax: this thread's row m = TMEM lane 32 q + lane, columns [32 half, +32) of each tile
+        const int q = warp & 3, half = (warp - 2) >> 2, m = 32 * q + lane;
         const int qp = pos0 + q0 + (m & 63);               // its query position
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+        float* stat = reinterpret_cast<float*>(smem + A5Layout::kStat);
         const float c2 = 1.4426950408889634f / sqrtf((float)HEAD_DIM);
         float rmax = -INFINITY, rsum = 0.f, mc = 0.f, inv = 0.f;
         bool ok = true;
@@ -207,44 +212,52 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
             const uint32_t b = (uint32_t)u & 1u, use = (uint32_t)u >> 1;
             if (ok && !mbar_wait(&sfull[b], use & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
             tc_fence_after();
-            float v[64];
-            {
-                float h0[32], h1[32];
-                tmem_ld32(tmem + lane_off + b * kA5Keys, h0);
-                tmem_ld32(tmem + lane_off + b * kA5Keys + 32, h1);
-                #pragma unroll
-                for (int i = 0; i < 32; i++) { v[i] = h0[i]; v[32 + i] = h1[i]; }
-            }
+            float v[32];
+            tmem_ld32(tmem + lane_off + b * kA5Keys + 32 * half, v);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[b]);
-            const int k0 = t * kA5Keys;
+            const int k0 = t * kA5Keys + 32 * half;
             #pragma unroll
-            for (int i = 0; i < 64; i++) if (k0 + i > qp) v[i] = -INFINITY;   // causal mask (also past the block's last key)
+            for (int i = 0; i < 32; i++) if (k0 + i > qp) v[i] = -INFINITY;   // causal mask (also past the block's last key)
             if (u < T) {
                 float mx = rmax;
                 #pragma unroll
-                for (int i = 0; i < 64; i++) mx = fmaxf(mx, v[i]);
-                float ps = 0.f;
-                const float mcn = mx * c2;
-                #pragma unroll
-                for (int i = 0; i < 64; i++) ps += exp2f(fmaf(v[i], c2, -mcn));
-                rsum = fmaf(rsum, exp2f(fmaf(rmax, c2, -mcn)), ps);   // rmax = -inf on the first tile: factor 0
-                rmax = mx;
-                if (u == T - 1) { mc = rmax * c2; inv = 1.0f / rsum; }
+                for (int i = 0; i < 32; i++) mx = fmaxf(mx, v[i]);
+                if (mx != -INFINITY) {   // a half-row whose keys are all masked so far keeps (-inf, 0)
+                    float ps = 0.f;
+                    const float mcn = mx * c2;
+                    #pragma unroll
+                    for (int i = 0; i < 32; i++) ps += exp2f(fmaf(v[i], c2, -mcn));
+                    rsum = fmaf(rsum, exp2f(fmaf(rmax, c2, -mcn)), ps);   // rmax = -inf: factor 0
+                    rmax = mx;
+                }
+                if (u == T - 1) {
+                    // combine the two half-rows: (max, sum) through shared memory, once
+                    stat[(half * 128 + m) * 2] = rmax;
+                    stat[(half * 128 + m) * 2 + 1] = rsum;
+                    named_bar(2, 256);
+                    const float om = stat[((half ^ 1) * 128 + m) * 2], os = stat[((half ^ 1) * 128 + m) * 2 + 1];
+                    const float M = fmaxf(rmax, om);   // finite: key 0 precedes every query
+                    const float L = (rmax == -INFINITY ? 0.f : rsum * exp2f((rmax - M) * c2)) +
+                                    (om == -INFINITY ? 0.f : os * exp2f((om - M) * c2));
+                    mc = M * c2;
+                    inv = 1.0f / L;
+                }
             } else {
-                // P = exp2(S c - max c) / sum, two bf16 parts, into P buffer t & 1
+                // P = exp2(S c - max c) / sum, two bf16 parts, into P buffer t & 1 (this half's 4 chunks of each part)
                 const uint32_t pb = (uint32_t)t & 1u, puse = (uint32_t)t >> 1;
                 if (ok && puse > 0 && !mbar_wait(&pempty[pb], (puse - 1) & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
                 uint8_t* pbuf = smem + A5Layout::kP + pb * kA5PBytes;
                 #pragma unroll
-                for (int c = 0; c < 8; c++) {
+                for (int cc = 0; cc < 4; cc++) {
                     uint32_t h[4], md[4], lo[4];
                     #pragma unroll
                     for (int j = 0; j < 4; j++) {
-                        const float p0 = exp2f(fmaf(v[8 * c + 2 * j], c2, -mc)) * inv, p1 = exp2f(fmaf(v[8 * c + 2 * j + 1], c2, -mc)) * inv;
+                        const float p0 = exp2f(fmaf(v[8 * cc + 2 * j], c2, -mc)) * inv, p1 = exp2f(fmaf(v[8 * cc + 2 * j + 1], c2, -mc)) * inv;
                         split3x2(p0, p1, h[j], md[j], lo[j]);
                     }
+                    const int c = 4 * half + cc;
                     *(uint4*)(pbuf + sw128(m, c)) = make_uint4(h[0], h[1], h[2], h[3]);
                     *(uint4*)(pbuf + 16384 + sw128(m, c)) = make_uint4(md[0], md[1], md[2], md[3]);
                 }
@@ -253,12 +266,12 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
                 if (lane == 0) mbar_arrive(&pfull[pb]);
             }
         }
-        // epilogue: O row m (final, normalised) -> the O projection's operand, split
+        // epilogue: O row m (final, normalised), this half's 64 dims -> the O projection's operand, split
         if (ok && !mbar_wait(ofull, 0, 2 * tc::kWaitNs)) atomicOr(err, 64u);
         tc_fence_after();
         uint16_t* arow = As + (size_t)(q0 + (m & 63)) * ld_as + 128 * (2 * hk + (m >> 6));
         #pragma unroll 1
-        for (int c = 0; c < HEAD_DIM; c += 32) {
+        for (int c = 64 * half; c < 64 * half + 64; c += 32) {
             float o[32];
             tmem_ld32(tmem + lane_off + 128 + c, o);
             #pragma unroll
