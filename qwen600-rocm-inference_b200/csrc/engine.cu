@@ -1017,6 +1017,13 @@ extern "C" int qwen_set_prefill_parts(qwen_t* c, int parts) {
     return QWEN_OK;
 }
 
+extern "C" int qwen_set_prefill_attention(qwen_t* c, int kind) {
+    if (!c) return fail(QWEN_E_ARG, "NULL handle");
+    if (kind != 0 && kind != 1) return fail(QWEN_E_ARG, "kind must be 0 (mma.sync) or 1 (tcgen05)");
+    c->att5 = kind == 1;
+    return QWEN_OK;
+}
+
 extern "C" int qwen_set_prefill_mode(qwen_t* c, int gemm) {
     if (!c) return fail(QWEN_E_ARG, "NULL handle");
     c->gemm_prefill = gemm != 0;

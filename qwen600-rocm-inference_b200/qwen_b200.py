@@ -81,6 +81,7 @@ _SIGS = {
     "qwen_gemm_bf16": (_c.c_int, [_P, _P, _P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P]),
     "qwen_set_prefill_mode": (_c.c_int, [_P, _c.c_int]),
     "qwen_set_prefill_parts": (_c.c_int, [_P, _c.c_int]),
+    "qwen_set_prefill_attention": (_c.c_int, [_P, _c.c_int]),
     "qwen_row_topk": (_c.c_int, [_P, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _P, _P, _P]),
     "qwen_batch_init": (_c.c_int, [_P, _c.c_int]),
     "qwen_batch_prefill": (_c.c_int, [_P, _c.c_int, _P, _c.c_int, _P]),
@@ -339,6 +340,10 @@ class Engine:
     def set_prefill_parts(self, parts=3):
         """bf16 parts per activation in the tensor-core passes (3: fp32-exact, 2, 1)."""
         _check(self._lib.qwen_set_prefill_parts(self._h, int(parts)))
+
+    def set_prefill_attention(self, tcgen05=False):
+        """Prompt-pass attention on the tcgen05/TMEM kernel (True) or mma.sync (False, default)."""
+        _check(self._lib.qwen_set_prefill_attention(self._h, 1 if tcgen05 else 0))
 
     def set_prefill_mode(self, gemm=True):
         """Long prompts on the tensor cores (True, default) or one decode launch per token."""

@@ -11,11 +11,11 @@ checkpoint, one oracle pass over a seeded 4,600-token sequence:
   top-p 0.95) each equal to the oracle sampler, in the reference's candidate
   order, on the device's own logits.
 
-Tolerances, as in test_gpu_decode: max-abs <= 2e-2 at every position; relative
-RMS <= 2.5e-3 per position (the oracle-vs-oracle floor: the oracle with float
-instead of double accumulation differs from itself by up to that much, since
-any round-off difference can move a K/V element across a bf16 rounding
-boundary) and <= 1e-3 averaged over the compared positions."""
+Tolerances: max-abs <= 2e-2 and relative RMS <= 1e-3 at every compared
+position (the stated contract).  At these depths the oracle with float
+instead of double accumulation differs from itself by 1.7-1.9e-4 and the
+engine from the oracle by ~4.5e-4; only the first positions of a sequence sit
+near 2e-3 (see test_gpu_decode, which allows 2.5e-3 per position there)."""
 import numpy as np
 import pytest
 
@@ -46,7 +46,7 @@ def oracle_long(O, checkpoint):
 def _check(got, want, where):
     d, r = float(np.abs(got - want).max()), rel_rms(got, want)
     assert d <= 2e-2, (where, d)
-    assert r <= 2.5e-3, (where, r)
+    assert r <= 1e-3, (where, r)
     assert int(np.argmax(got)) == int(np.argmax(want)), where
     return r
 

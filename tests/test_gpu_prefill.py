@@ -1,7 +1,9 @@
 """qwen_prefill on the tensor cores (whole-prompt passes: tcgen05 GEMMs with the
-activations split into three bf16 parts, fp32 attention over the KV cache)
-against the one-launch-per-token path and the fp32 oracle.  Tolerances as in
-test_gpu_decode: max-abs <= 2e-2 and relative RMS <= 2.5e-3 on the logits."""
+activations split into bf16 parts, causal attention over the KV cache on the
+mma.sync kernel or on the tcgen05/TMEM kernel) against the one-launch-per-token
+path and the fp32 oracle.  Tolerances as in test_gpu_decode: max-abs <= 2e-2
+and relative RMS <= 2.5e-3 on the logits against the other paths; the two
+attention kernels agree to 1e-3."""
 import numpy as np
 import pytest
 
@@ -75,3 +77,62 @@ def test_prefill_edge_lengths(qb, checkpoint, n):
         assert ga == gb
     finally:
         a.close(); b.close()
+
+
+def _pair_attention(qb, checkpoint, chunks):
+    """Prefill the chunks on a handle with the default (mma.sync) prompt-pass
+    attention and on one with the tcgen05/TMEM kernel; returns both final
+    logits and both handles."""
+    a, t = qb.Engine(checkpoint, 0), qb.Engine(checkpoint, 0)
+    a.set_prefill_attention(False)
+    t.set_prefill_attention(True)
+    pos = 0
+    for ch in chunks:
+        la = a.prefill(ch, pos, want_logits=True)
+        lt = t.prefill(ch, pos, want_logits=True)
+        pos += len(ch)
+    return la, lt, a, t, pos
+
+
+def test_prefill_tcgen05_attention_300_against_oracle(qb, O, checkpoint):
+    toks = _prompt(300, 11)
+    la, lt, a, t, pos = _pair_attention(qb, checkpoint, [toks])
+    try:
+        of = O.Oracle(checkpoint, O.FP32, 320)
+        for p, tok in enumerate(toks[:-1]):
+            of.forward(tok, p, want_logits=False)
+        lo = of.forward(toks[-1], len(toks) - 1)
+        assert np.abs(lt - lo).max() <= 2e-2 and rel_rms(lt, lo) <= 2.5e-3, (np.abs(lt - lo).max(), rel_rms(lt, lo))
+        assert rel_rms(lt, la) <= 1e-3 and int(np.argmax(lt)) == int(np.argmax(la))
+        ga, _ = a.generate(int(np.argmax(la)), pos, 8)
+        gt, _ = t.generate(int(np.argmax(lt)), pos, 8)
+        assert ga == gt
+    finally:
+        a.close(); t.close()
+
+
+# 65 and 129: one 128-row pass with 63 / 127 padding rows; 2049: a full pass
+# plus a one-row pass; 2100 + 200: a second prefill call at pos0 = 2100 whose
+# key tiles start in the first call's cache.
+@pytest.mark.parametrize("lens", [(65,), (129,), (2049,), (2100, 200)])
+def test_prefill_tcgen05_attention_matches_mma(qb, checkpoint, lens):
+    chunks = [_prompt(n, 40 + i + n) for i, n in enumerate(lens)]
+    la, lt, a, t, pos = _pair_attention(qb, checkpoint, chunks)
+    try:
+        assert t.cached == sum(lens)
+        assert np.abs(lt - la).max() <= 2e-2 and rel_rms(lt, la) <= 1e-3, (lens, np.abs(lt - la).max(), rel_rms(lt, la))
+        assert int(np.argmax(lt)) == int(np.argmax(la))
+        ga, _ = a.generate(int(np.argmax(la)), pos, 4)
+        gt, _ = t.generate(int(np.argmax(lt)), pos, 4)
+        assert ga == gt
+    finally:
+        a.close(); t.close()
+
+
+def test_prefill_attention_kind_rejects_unknown(qb, checkpoint):
+    e = qb.Engine(checkpoint, 0)
+    try:
+        with pytest.raises(Exception):
+            qb._check(e._lib.qwen_set_prefill_attention(e._h, 2))
+    finally:
+        e.close()
