@@ -336,8 +336,9 @@ def prefill_bench(qb, ck, n_prompt=2048, n_gen=32):
     tokens; prefill time is the wall time of the synchronous call after one
     warm-up call.  Algorithmic FLOPs: the projections (2 x 440,401,920 per
     token) plus causal attention (28 x 16 x 2 x S^2 x 128 for QK^T and P.V
-    over the lower triangle); the passes execute the projections three times
-    (three-part bf16 split of the fp32 activations)."""
+    over the lower triangle); the passes execute both twice (the fp32
+    activations, Q and P enter the bf16 tensor-core products as two bf16
+    parts)."""
     eng = qb.Engine(ck, 0)
     try:
         prompt = np.random.default_rng(2048).integers(0, 151936, n_prompt).tolist()
@@ -352,9 +353,10 @@ def prefill_bench(qb, ck, n_prompt=2048, n_gen=32):
     alg = PREFILL_LINEAR_FLOP * n_prompt + attn
     return {"value": n_prompt / dt, "unit": "tok/s", "prompt_tokens": n_prompt, "ms": dt * 1e3,
             "algorithmic_tflop": alg / 1e12, "achieved_tflops": alg / dt / 1e12,
-            "executed_tensor_tflop": 3 * PREFILL_LINEAR_FLOP * n_prompt / 1e12,
-            "path": "28 layers x (4 persistent tcgen05 GEMM launches over all prompt rows + causal attention on mma.m16n8k16), "
-                    "last position's logits by fp32 RMSNorm + LM-head GEMV",
+            "executed_tensor_tflop": 2 * alg / 1e12,
+            "path": "28 layers x (4 persistent tcgen05 GEMM launches over all prompt rows, 256 x 256 tiles on SM pairs "
+                    "(cta_group::2) + causal attention on tcgen05/TMEM, one pass, online softmax), two bf16 parts per "
+                    "fp32 operand; last position's logits by fp32 RMSNorm + LM-head GEMV",
             "decode_after": {"tokens": n_gen, "tok_s": n_gen / (ms / 1e3)}}
 
 

@@ -180,11 +180,12 @@ int qwen_set_prefill_mode(qwen_t* ctx, int gemm);
  * No reference counterpart (the reference has no prompt pass). */
 int qwen_set_prefill_parts(qwen_t* ctx, int parts);
 
-/* Attention kernel of the tensor-core prompt passes: 0 (the default) the
- * mma.sync kernel, 1 the tcgen05/TMEM kernel (S and O accumulated in tensor
- * memory, K and transposed V tiles by TMA).  Both compute the same causal
- * attention; the environment variable QWEN_B200_PREFILL_ATTN=tc5 selects 1 at
- * qwen_create.  No reference counterpart (the reference has no prompt pass). */
+/* Attention kernel of the tensor-core prompt passes: 1 (the default) the
+ * tcgen05/TMEM kernel (S and O accumulated in tensor memory, K and transposed
+ * V tiles by TMA, one pass over the keys with an online softmax), 0 the
+ * mma.sync kernel.  Both compute the same causal attention; the environment
+ * variable QWEN_B200_PREFILL_ATTN=mma selects 0 at qwen_create.  No reference
+ * counterpart (the reference has no prompt pass). */
 int qwen_set_prefill_attention(qwen_t* ctx, int kind);
 
 /* Number of positions currently held in the KV cache. */

@@ -6,28 +6,33 @@
 //
 // One CTA per (64 query positions, KV head hk): the 128 rows of its tiles are
 // the 64 positions of q head 2 hk (rows 0-63) and of q head 2 hk + 1 (rows
-// 64-127), so every K/V tile serves both heads.  Two passes over the key
-// tiles (64 keys each, up to the block's last query; heaviest blocks first):
-//   pass 1  S = Q K^T into TMEM; each softmax thread reads its row (one TMEM
-//           lane) and keeps the row's running max and sum of exp (base 2, the
-//           1/sqrt(d) scale folded into the exponent) — no cross-thread step;
-//   pass 2  S again; P = exp2(S c - max c) / sum, final, written as two bf16
-//           parts into shared memory; O += P V accumulates in TMEM across all
-//           tiles with no rescaling (that is what the first pass buys).
+// 64-127), so every K/V tile serves both heads.  One pass over the key tiles
+// (64 keys each, up to the block's last query; heaviest blocks first) with an
+// online softmax: S = Q K^T into TMEM (two buffers); each row keeps a running
+// max m and sum l; P = exp2(S c - m c) (the 1/sqrt(d) scale folded into c) is
+// written unnormalised into shared memory and O += P V accumulates in TMEM.
+// When a tile raises a row's max by more than kA5Rescale (base-2 exponent
+// units) the row first scales its O columns and l by exp2((m_old - m_new) c)
+// in tensor memory (after the previous P V product has completed) and adopts
+// the new max; smaller rises keep the old max, so P stays below 2^kA5Rescale
+// and O and l carry the same factor, which the final division by l removes.
 // Q enters as two bf16 parts side by side along K (K' = 256 against K read
 // twice), P likewise (K' = 128 against V^T read twice): 16 mantissa bits of
-// each fp32 operand, relative error <= 2^-17 (K and V are bf16 in the cache).
-// Both tcgen05 operands are K-major SW128 tiles: Q and P written by threads in
-// the layout the TMA engine produces, K tiles by TMA from the cache
-// ([head][position][dim]), V tiles by TMA from a transposed copy of the
-// layer's V ([head][dim][position], transpose_v_kernel) so that keys are
-// contiguous.  Warps: 0 TMA producer, 1 TMEM allocator and MMA issuer, 2-9
-// softmax and epilogue: warp w reads TMEM lanes 32 (w % 4) .. (the rows it may
-// access), warps 2-5 columns 0-31 of each S tile and warps 6-9 columns 32-63,
-// each keeping its half-row's max and sum; the halves combine once, after the
-// first pass, through shared memory.  Every wait is
-// bounded: on expiry the thread sets *err and stops waiting; the TMEM
-// allocation is always released.
+// each fp32 operand, relative error <= 2^-16 (K and V are bf16 in the cache).
+// P's parts are formed with integer arithmetic (split2x2_int) so that the
+// conversion unit only evaluates exp2.  Both tcgen05 operands are K-major
+// SW128 tiles: Q and P written by threads in the layout the TMA engine
+// produces, K tiles by TMA from the cache ([head][position][dim]), V tiles by
+// TMA from a transposed copy of the layer's V ([head][dim][position],
+// transpose_v_kernel) so that keys are contiguous.  Warps: 0 TMA producer
+// (K and V^T tiles in the order the MMAs use them: S of tile t + 1 is issued
+// before P V of tile t, so the softmax of one tile overlaps the S product of
+// the next), 1 TMEM allocator and MMA issuer, 2-9 softmax and epilogue: warp w
+// reads TMEM lanes 32 (w % 4) .. (the rows it may access), warps 2-5 columns
+// 0-31 of each S tile (O columns 0-63) and warps 6-9 columns 32-63 (O columns
+// 64-127); the two warps of a row agree on each tile's max through shared
+// memory, so both halves use the same m.  Every wait is bounded: on expiry the
+// thread sets *err and stops waiting; the TMEM allocation is always released.
 #pragma once
 #include "gemm_tc.cuh"
 #include "prefill_kernels.cuh"
@@ -36,22 +41,11 @@ namespace qb {
 namespace pf {
 
 constexpr int kA5Keys = 64;                       // keys per tile
-constexpr int kA5Stages = 2;                      // K (and V) tiles in flight
 constexpr int kA5Threads = 320;                   // warps 0 producer, 1 MMA, 2-9 softmax (two per TMEM lane quarter)
 constexpr int kA5QBytes = 4 * 128 * 128;          // Q: 4 SW128 blocks (part, dim half) of 128 rows x 128 B
 constexpr int kA5KBytes = 2 * kA5Keys * 128;      // a K tile: 2 blocks (dim halves) of 64 rows x 128 B
 constexpr int kA5VBytes = HEAD_DIM * 128;         // a V^T tile: 128 rows (dims) x 128 B (64 keys)
 constexpr int kA5PBytes = 2 * 128 * 128;          // a P buffer: 2 blocks (parts) of 128 rows x 128 B
-struct A5Layout {
-    static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kA5QBytes;
-    static constexpr int kV = kK + kA5Stages * kA5KBytes;
-    static constexpr int kP = kV + kA5Stages * kA5VBytes;
-    static constexpr int kBar = kP + 2 * kA5PBytes;   // barriers after the 1024-aligned tiles
-    static constexpr int kStat = kBar + 32 * 8;        // [2 halves][128 rows][max, sum] after the first pass
-    static constexpr int kSmem = kStat + 2 * 128 * 2 * 4 + 1024;
-};
-static_assert(A5Layout::kSmem <= 227 * 1024, "attention tiles must fit one CTA's shared memory");
 
 // Byte offset of 16-byte chunk `c` of row `r` in a K-major SW128 tile (rows of
 // 128 B, chunk index XOR row within each 8-row group of 1024 B).
@@ -75,6 +69,50 @@ __global__ void transpose_v_kernel(const uint16_t* __restrict__ vc_l, uint16_t* 
         if (p0 + threadIdx.x < n) dst[(size_t)i * SEQ_LEN + p0 + threadIdx.x] = t[threadIdx.x][i];
 }
 
+constexpr float kA5Rescale = 8.0f;                 // base-2 exponent rise of a row's max that rescales O
+constexpr int kA5KStages = 3;                      // K tiles in flight
+constexpr int kA5VStages = 2;                      // V^T tiles in flight
+struct A5Layout {
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kA5QBytes;
+    static constexpr int kV = kK + kA5KStages * kA5KBytes;
+    static constexpr int kP = kV + kA5VStages * kA5VBytes;
+    static constexpr int kBar = kP + 2 * kA5PBytes;
+    static constexpr int kXm = kBar + 32 * 8;            // [2 tiles][2 halves][128 rows] half-row maxima
+    static constexpr int kLs = kXm + 2 * 2 * 128 * 4;    // [2 halves][128 rows] half-row sums at the end
+    static constexpr int kSmem = kLs + 2 * 128 * 4 + 1024;
+};
+static_assert(A5Layout::kSmem <= 227 * 1024, "attention tiles must fit one CTA's shared memory");
+
+// Two bf16 parts of the non-negative finite values a and b (< 2^127) with
+// integer arithmetic instead of conversion instructions, so the conversion
+// unit is left to exp2: hi = the value rounded to 8 significant bits (adding
+// half a unit of the 16 dropped bits, then truncating), mid = the remainder
+// (exact in fp32) rounded the same way; |a - hi - mid| <= 2^-16 |a|.  Packed
+// like cvt_bf16x2 (a in the low half).
+__device__ __forceinline__ void split2x2_int(float a, float b, uint32_t& h, uint32_t& m) {
+    const uint32_t ra = __float_as_uint(a) + 0x8000u, rb = __float_as_uint(b) + 0x8000u;
+    const float ma = a - __uint_as_float(ra & 0xffff0000u), mb = b - __uint_as_float(rb & 0xffff0000u);
+    h = __byte_perm(ra, rb, 0x7632);
+    m = __byte_perm(__float_as_uint(ma) + 0x8000u, __float_as_uint(mb) + 0x8000u, 0x7632);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+          "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+          "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+          "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+          "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+          "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // grid: rows / 64 * N_KV_HEADS CTAs, kA5Threads threads, A5Layout::kSmem bytes.
 // map_k: the layer's K cache as [N_KV_HEADS * SEQ_LEN rows][128], boxes 64 x 64;
 // map_v: the transposed V as [N_KV_HEADS * 128 rows][SEQ_LEN], boxes 128 x 64.
@@ -85,16 +123,17 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + A5Layout::kBar);
-    uint64_t* kfull = bars;            // [kA5Stages]
-    uint64_t* kempty = bars + 2;       // [kA5Stages]
-    uint64_t* vfull = bars + 4;        // [kA5Stages]
-    uint64_t* vempty = bars + 6;       // [kA5Stages]
-    uint64_t* sfull = bars + 8;        // [2] S buffer written (MMA -> softmax)
-    uint64_t* sempty = bars + 10;      // [2] S buffer read (softmax -> MMA), 8 arrivals
-    uint64_t* pfull = bars + 12;       // [2] P buffer written (softmax -> MMA), 8 arrivals
-    uint64_t* pempty = bars + 14;      // [2] P buffer read by the PV MMAs (MMA -> softmax)
-    uint64_t* ofull = bars + 16;       // O complete
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    uint64_t* kfull = bars;                          // [kA5KStages]
+    uint64_t* kempty = bars + kA5KStages;           // [kA5KStages]
+    uint64_t* vfull = bars + 2 * kA5KStages;        // [kA5VStages]
+    uint64_t* vempty = vfull + kA5VStages;          // [kA5VStages]
+    uint64_t* sfull = vempty + kA5VStages;          // [2] S buffer written (MMA -> softmax)
+    uint64_t* sempty = sfull + 2;                    // [2] S buffer read (softmax -> MMA), 8 arrivals
+    uint64_t* pfull = sfull + 4;                     // [2] P buffer written and O rescaled (softmax -> MMA), 8 arrivals
+    uint64_t* pempty = sfull + 6;                    // [2] P V product of the buffer complete (MMA -> softmax)
+    uint64_t* ofull = sfull + 8;                     // O complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sfull + 9);
+    static_assert((2 * kA5KStages + 2 * kA5VStages + 10) * 8 <= 32 * 8, "barriers fit their 256 bytes");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nqb = gridDim.x / N_KV_HEADS;
     const int qb = nqb - 1 - (int)blockIdx.x / N_KV_HEADS, hk = (int)blockIdx.x % N_KV_HEADS;
@@ -103,7 +142,8 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
     const int T = last / kA5Keys + 1;   // key tiles
 
     if (tid == 0) {
-        for (int s = 0; s < kA5Stages; s++) { mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1); mbar_init(&vfull[s], 1); mbar_init(&vempty[s], 1); }
+        for (int s = 0; s < kA5KStages; s++) { mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1); }
+        for (int s = 0; s < kA5VStages; s++) { mbar_init(&vfull[s], 1); mbar_init(&vempty[s], 1); }
         for (int b = 0; b < 2; b++) { mbar_init(&sfull[b], 1); mbar_init(&sempty[b], 8); mbar_init(&pfull[b], 8); mbar_init(&pempty[b], 1); }
         mbar_init(ofull, 1);
         fence_barrier_init();
@@ -111,10 +151,8 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
         asm volatile("prefetch.tensormap [%0];" ::"l"(&map_v) : "memory");
     }
     if (warp == 1) tmem_alloc(tmem_slot, 256);   // S[0] cols 0-63, S[1] 64-127, O 128-255
-    // Q of the block's 128 rows, split into hi and mid bf16 parts: block j = part
-    // (j >> 1), dims 64 (j & 1) .. +63
     for (int e = tid; e < 128 * 16; e += kA5Threads) {
-        const int m = e >> 4, c8 = e & 15;                 // row, 8-dim chunk of the 128 dims
+        const int m = e >> 4, c8 = e & 15;
         const float* src = Q + (size_t)(q0 + (m & 63)) * Q_DIM + 128 * (2 * hk + (m >> 6)) + 8 * c8;
         const float4 a = *(const float4*)src, b = *(const float4*)(src + 4);
         uint32_t h[4], md[4], lo[4];
@@ -134,32 +172,33 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
 
     if (warp == 0) {
         if (lane == 0) {
-            // K tiles 0..T-1 twice (both passes), V tiles 0..T-1 alongside the second
+            // K(0), K(1), V(0), K(2), V(1), ...: the order the MMAs consume them
             bool ok = true;
-            for (int u = 0; u < 2 * T && ok; u++) {
-                const int t = u < T ? u : u - T;
-                const uint32_t s = (uint32_t)u % kA5Stages;
-                if (u >= kA5Stages && !mbar_wait(&kempty[s], ((u / kA5Stages) - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 16u); ok = false; break; }
+            auto load_v = [&](int t) {
+                const uint32_t sv = (uint32_t)t % kA5VStages;
+                if (t >= kA5VStages && !mbar_wait(&vempty[sv], ((t / kA5VStages) - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 16u); return false; }
+                mbar_arrive_expect_tx(&vfull[sv], kA5VBytes);
+                tma_load_2d(smem + A5Layout::kV + sv * kA5VBytes, &map_v, t * kA5Keys, hk * HEAD_DIM, &vfull[sv]);
+                return true;
+            };
+            for (int t = 0; t < T && ok; t++) {
+                const uint32_t s = (uint32_t)t % kA5KStages;
+                if (t >= kA5KStages && !mbar_wait(&kempty[s], ((t / kA5KStages) - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 16u); ok = false; break; }
                 uint8_t* kd = smem + A5Layout::kK + s * kA5KBytes;
                 mbar_arrive_expect_tx(&kfull[s], kA5KBytes);
                 tma_load_2d(kd, &map_k, 0, hk * SEQ_LEN + t * kA5Keys, &kfull[s]);
                 tma_load_2d(kd + kA5Keys * 128, &map_k, 64, hk * SEQ_LEN + t * kA5Keys, &kfull[s]);
-                if (u >= T) {
-                    const uint32_t sv = (uint32_t)t % kA5Stages;
-                    if (t >= kA5Stages && !mbar_wait(&vempty[sv], ((t / kA5Stages) - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 16u); ok = false; break; }
-                    mbar_arrive_expect_tx(&vfull[sv], kA5VBytes);
-                    tma_load_2d(smem + A5Layout::kV + sv * kA5VBytes, &map_v, t * kA5Keys, hk * HEAD_DIM, &vfull[sv]);
-                }
+                if (t >= 1) ok = load_v(t - 1);
             }
+            if (ok && T > 0) load_v(T - 1);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t id_s = idesc_bf16_f32(128, kA5Keys), id_o = idesc_bf16_f32(128, HEAD_DIM);
             bool ok = true;
-            // O += P V for tile t: P buffer t & 1 written by the softmax warps, V^T stage t % kA5Stages
             auto pv = [&](int t) {
-                const uint32_t pb = (uint32_t)t & 1u, puse = (uint32_t)t >> 1, sv = (uint32_t)t % kA5Stages;
-                if (!mbar_wait(&pfull[pb], puse & 1u, tc::kWaitNs) || !mbar_wait(&vfull[sv], (t / kA5Stages) & 1u, tc::kWaitNs)) {
+                const uint32_t pb = (uint32_t)t & 1u, puse = (uint32_t)t >> 1, sv = (uint32_t)t % kA5VStages;
+                if (!mbar_wait(&pfull[pb], puse & 1u, tc::kWaitNs) || !mbar_wait(&vfull[sv], (t / kA5VStages) & 1u, tc::kWaitNs)) {
                     atomicOr(err, 32u);
                     return false;
                 }
@@ -175,15 +214,11 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
                 mma_commit(&pempty[pb]);
                 return true;
             };
-            // S of step u (tiles 0..T-1, then again), and in the second pass the
-            // P V product of the previous tile, so the softmax of one tile
-            // overlaps the S product of the next
-            for (int u = 0; u < 2 * T && ok; u++) {
-                const uint32_t b = (uint32_t)u & 1u, use = (uint32_t)u >> 1, s = (uint32_t)u % kA5Stages;
+            for (int t = 0; t < T && ok; t++) {
+                const uint32_t b = (uint32_t)t & 1u, use = (uint32_t)t >> 1, s = (uint32_t)t % kA5KStages;
                 if (use > 0 && !mbar_wait(&sempty[b], (use - 1) & 1u, tc::kWaitNs)) { atomicOr(err, 32u); ok = false; break; }
-                if (!mbar_wait(&kfull[s], (u / kA5Stages) & 1u, tc::kWaitNs)) { atomicOr(err, 32u); ok = false; break; }
+                if (!mbar_wait(&kfull[s], (t / kA5KStages) & 1u, tc::kWaitNs)) { atomicOr(err, 32u); ok = false; break; }
                 tc_fence_after();
-                // S[b] = Q K^T: K' = 256 (Q hi | mid) against the K tile read twice
                 const uint32_t qa = smem_addr(smem + A5Layout::kQ), kb = smem_addr(smem + A5Layout::kK + s * kA5KBytes);
                 #pragma unroll
                 for (int j = 0; j < 4; j++)
@@ -193,23 +228,22 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
                                  kmajor_sw128_desc(kb + (j & 1) * (kA5Keys * 128) + kk * 32), id_s, (j | kk) != 0 ? 1u : 0u);
                 mma_commit(&kempty[s]);
                 mma_commit(&sfull[b]);
-                if (u - 1 >= T) ok = pv(u - 1 - T);
+                if (t >= 1) ok = pv(t - 1);
             }
             if (ok && T > 0) pv(T - 1);
-            mma_commit(ofull);   // O complete (or abandoned: *err is set)
+            mma_commit(ofull);
         }
     } else {
-        // softmax: this thread's row m = TMEM lane 32 q + lane, columns [32 half, +32) of each tile
         const int q = warp & 3, half = (warp - 2) >> 2, m = 32 * q + lane;
-        const int qp = pos0 + q0 + (m & 63);               // its query position
+        const int qp = pos0 + q0 + (m & 63);
         const uint32_t lane_off = (uint32_t)(32 * q) << 16;
-        float* stat = reinterpret_cast<float*>(smem + A5Layout::kStat);
+        float* xm = reinterpret_cast<float*>(smem + A5Layout::kXm);
+        float* ls = reinterpret_cast<float*>(smem + A5Layout::kLs);
         const float c2 = 1.4426950408889634f / sqrtf((float)HEAD_DIM);
-        float rmax = -INFINITY, rsum = 0.f, mc = 0.f, inv = 0.f;
+        float mrun = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int u = 0; u < 2 * T; u++) {
-            const int t = u < T ? u : u - T;
-            const uint32_t b = (uint32_t)u & 1u, use = (uint32_t)u >> 1;
+        for (int t = 0; t < T; t++) {
+            const uint32_t b = (uint32_t)t & 1u, use = (uint32_t)t >> 1;
             if (ok && !mbar_wait(&sfull[b], use & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
             tc_fence_after();
             float v[32];
@@ -218,64 +252,70 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[b]);
             const int k0 = t * kA5Keys + 32 * half;
-            #pragma unroll
-            for (int i = 0; i < 32; i++) if (k0 + i > qp) v[i] = -INFINITY;   // causal mask (also past the block's last key)
-            if (u < T) {
-                float mx = rmax;
+            if (k0 + 31 > qp) {   // causal mask (also past the block's last key): the diagonal tiles only
                 #pragma unroll
-                for (int i = 0; i < 32; i++) mx = fmaxf(mx, v[i]);
-                if (mx != -INFINITY) {   // a half-row whose keys are all masked so far keeps (-inf, 0)
-                    float ps = 0.f;
-                    const float mcn = mx * c2;
-                    #pragma unroll
-                    for (int i = 0; i < 32; i++) ps += exp2f(fmaf(v[i], c2, -mcn));
-                    rsum = fmaf(rsum, exp2f(fmaf(rmax, c2, -mcn)), ps);   // rmax = -inf: factor 0
-                    rmax = mx;
-                }
-                if (u == T - 1) {
-                    // combine the two half-rows: (max, sum) through shared memory, once
-                    stat[(half * 128 + m) * 2] = rmax;
-                    stat[(half * 128 + m) * 2 + 1] = rsum;
-                    named_bar(2, 256);
-                    const float om = stat[((half ^ 1) * 128 + m) * 2], os = stat[((half ^ 1) * 128 + m) * 2 + 1];
-                    const float M = fmaxf(rmax, om);   // finite: key 0 precedes every query
-                    const float L = (rmax == -INFINITY ? 0.f : rsum * exp2f((rmax - M) * c2)) +
-                                    (om == -INFINITY ? 0.f : os * exp2f((om - M) * c2));
-                    mc = M * c2;
-                    inv = 1.0f / L;
-                }
-            } else {
-                // P = exp2(S c - max c) / sum, two bf16 parts, into P buffer t & 1 (this half's 4 chunks of each part)
-                const uint32_t pb = (uint32_t)t & 1u, puse = (uint32_t)t >> 1;
-                if (ok && puse > 0 && !mbar_wait(&pempty[pb], (puse - 1) & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
-                uint8_t* pbuf = smem + A5Layout::kP + pb * kA5PBytes;
-                #pragma unroll
-                for (int cc = 0; cc < 4; cc++) {
-                    uint32_t h[4], md[4], lo[4];
-                    #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const float p0 = exp2f(fmaf(v[8 * cc + 2 * j], c2, -mc)) * inv, p1 = exp2f(fmaf(v[8 * cc + 2 * j + 1], c2, -mc)) * inv;
-                        split3x2(p0, p1, h[j], md[j], lo[j]);
-                    }
-                    const int c = 4 * half + cc;
-                    *(uint4*)(pbuf + sw128(m, c)) = make_uint4(h[0], h[1], h[2], h[3]);
-                    *(uint4*)(pbuf + 16384 + sw128(m, c)) = make_uint4(md[0], md[1], md[2], md[3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&pfull[pb]);
+                for (int i = 0; i < 32; i++) if (k0 + i > qp) v[i] = -INFINITY;
             }
+            float mh = -INFINITY;
+            #pragma unroll
+            for (int i = 0; i < 32; i++) mh = fmaxf(mh, v[i]);
+            xm[((t & 1) * 2 + half) * 128 + m] = mh;
+            named_bar(2, 256);
+            const float mnew = fmaxf(mrun, fmaxf(mh, xm[((t & 1) * 2 + (half ^ 1)) * 128 + m]));   // finite: key 0 is in tile 0
+            const bool need = (mnew - mrun) * c2 > kA5Rescale;   // always on tile 0 (mrun = -inf)
+            float f = 1.0f;
+            if (need) { f = exp2f((mrun - mnew) * c2); mrun = mnew; l *= f; }   // f = 0 on tile 0
+            const float mc = mrun * c2;
+            // P (unnormalised), two bf16 parts, into P buffer t & 1 once P V of tile t - 2 is complete
+            if (ok && use > 0 && !mbar_wait(&pempty[b], (use - 1) & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
+            uint8_t* pbuf = smem + A5Layout::kP + b * kA5PBytes;
+            float ps = 0.f;
+            #pragma unroll
+            for (int cc = 0; cc < 4; cc++) {
+                uint32_t h[4], md[4];
+                #pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float p0 = exp2f(fmaf(v[8 * cc + 2 * j], c2, -mc)), p1 = exp2f(fmaf(v[8 * cc + 2 * j + 1], c2, -mc));
+                    ps += p0 + p1;
+                    split2x2_int(p0, p1, h[j], md[j]);
+                }
+                const int c = 4 * half + cc;
+                *(uint4*)(pbuf + sw128(m, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+                *(uint4*)(pbuf + 16384 + sw128(m, c)) = make_uint4(md[0], md[1], md[2], md[3]);
+            }
+            l += ps;
+            // rows whose max moved: scale their O columns (this half's 64) once P V of tile t - 1 is complete
+            if (t > 0 && __any_sync(0xffffffffu, need)) {
+                const uint32_t pb1 = (uint32_t)(t - 1) & 1u, use1 = (uint32_t)(t - 1) >> 1;
+                if (ok && !mbar_wait(&pempty[pb1], use1 & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
+                tc_fence_after();
+                #pragma unroll 1
+                for (int c = 64 * half; c < 64 * half + 64; c += 32) {
+                    float o[32];
+                    tmem_ld32(tmem + lane_off + 128 + c, o);
+                    #pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] *= f;
+                    tmem_st32(tmem + lane_off + 128 + c, o);
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfull[b]);
         }
-        // epilogue: O row m (final, normalised), this half's 64 dims -> the O projection's operand, split
+        // epilogue: O row m / l, this half's 64 dims -> the O projection's operand, split
         if (ok && !mbar_wait(ofull, 0, 2 * tc::kWaitNs)) atomicOr(err, 64u);
         tc_fence_after();
+        ls[half * 128 + m] = l;
+        named_bar(2, 256);
+        const float inv = 1.0f / (l + ls[(half ^ 1) * 128 + m]);
         uint16_t* arow = As + (size_t)(q0 + (m & 63)) * ld_as + 128 * (2 * hk + (m >> 6));
         #pragma unroll 1
         for (int c = 64 * half; c < 64 * half + 64; c += 32) {
             float o[32];
             tmem_ld32(tmem + lane_off + 128 + c, o);
             #pragma unroll
-            for (int i = 0; i < 32; i += 2) put_split2(arow, c + i, o[i], o[i + 1]);
+            for (int i = 0; i < 32; i += 2) put_split2(arow, c + i, o[i] * inv, o[i + 1] * inv);
         }
     }
     tc_fence_before();

@@ -250,7 +250,7 @@ struct qwen_ctx {
     int cached = 0;
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
-    bool att5 = false;          // prompt-pass attention on tcgen05 (attention_tc5.cuh) instead of mma.sync
+    int att5 = 1;               // prompt-pass attention: 1 tcgen05 (attention_tc5.cuh, the default), 0 mma.sync
     uint16_t* vt = nullptr;     // the layer's V transposed ([head][dim][position]) for the tcgen05 attention
     int last_k = 0;
 };
@@ -391,7 +391,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     if (const char* e = getenv("QWEN_B200_PREFETCH")) P.prefetch_chunks = std::max(0, std::min(64, atoi(e)));
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
     // prompt-pass attention: "tc5" selects the tcgen05 kernel, "mma" the mma.sync one
-    if (const char* e = getenv("QWEN_B200_PREFILL_ATTN")) c->att5 = strcmp(e, "tc5") == 0;
+    if (const char* e = getenv("QWEN_B200_PREFILL_ATTN")) c->att5 = strcmp(e, "mma") == 0 ? 0 : 1;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -1020,7 +1020,7 @@ extern "C" int qwen_set_prefill_parts(qwen_t* c, int parts) {
 extern "C" int qwen_set_prefill_attention(qwen_t* c, int kind) {
     if (!c) return fail(QWEN_E_ARG, "NULL handle");
     if (kind != 0 && kind != 1) return fail(QWEN_E_ARG, "kind must be 0 (mma.sync) or 1 (tcgen05)");
-    c->att5 = kind == 1;
+    c->att5 = kind;
     return QWEN_OK;
 }
 
@@ -1338,7 +1338,7 @@ bool cached_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 
 template <int BN, bool F32, int kEpi = 0>
 int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                int m_valid, int nsm, cudaStream_t st, uint32_t* err) {
+                int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -1349,9 +1349,39 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
     }
     const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
     qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi><<<std::min(items, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
-        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err);
+        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts);
     CU(cudaGetLastError());
     return QWEN_OK;
+}
+
+// The pair (2-SM) form: clusters of two CTAs, 256 x BN tiles.
+template <int BN, bool F32, int kEpi = 0>
+int gemm_launch_pair(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
+                     int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3) {
+    static thread_local int attr_dev = -1;
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (attr_dev != dev) {
+        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                qb::tc::PairLayout<BN>::kSmem));
+        attr_dev = dev;
+    }
+    const int items = bm.end[2] * (M / (2 * qb::tc::kBM)) * splits;
+    const int pairs = std::min(items, nsm / 2);
+    qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi><<<2 * pairs, qb::tc::kThreads, qb::tc::PairLayout<BN>::kSmem, st>>>(
+        ma, bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts);
+    CU(cudaGetLastError());
+    return QWEN_OK;
+}
+
+// Whether 256-row GEMMs run in the pair form (QWEN_B200_GEMM_PAIR=0 keeps every
+// GEMM on single-CTA tiles).
+bool pair_gemm_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("QWEN_B200_GEMM_PAIR");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    return on;
 }
 }  // namespace
 
@@ -1373,14 +1403,19 @@ static int gemm_prepare(int dev) {
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             qb::tc::Layout<256>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::PairLayout<256>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::PairLayout<256>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            qb::tc::PairLayout<256>::kSmem));
     done[dev].store(true, std::memory_order_release);
     return QWEN_OK;
 }
 
-// The gate|up projection with SwiGLU in the epilogue: A [M][3 DIM] (three bf16
+// The gate|up projection with SwiGLU in the epilogue: A [M][parts DIM] (bf16
 // parts) against the interleaved gate|up weights wgu [2 HIDDEN_DIM][DIM];
-// writes h = silu(gate) * up as three bf16 parts into Hs (rows ld_hs apart,
-// parts HIDDEN_DIM apart).  Rows m_valid .. M-1 are not written.
+// writes h = silu(gate) * up as `parts` bf16 parts into Hs (rows ld_hs apart,
+// parts HIDDEN_DIM apart), the parts the down projection reads.  Rows
+// m_valid .. M-1 are not written.
 static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st, int parts) {
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -1389,13 +1424,17 @@ static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs
     if (rc != QWEN_OK) return rc;
     CUtensorMap ma;
     qb::tc::BMaps bm;
+    const bool pair = pair_gemm_enabled() && M % (2 * qb::tc::kBM) == 0;
     if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)(3 * DIM), (uint64_t)lda, qb::tc::kBM) ||
-        !cached_map(&bm.map[0], wgu, (uint64_t)(2 * HIDDEN_DIM), (uint64_t)DIM, (uint64_t)DIM, 256))
+        !cached_map(&bm.map[0], wgu, (uint64_t)(2 * HIDDEN_DIM), (uint64_t)DIM, (uint64_t)DIM, pair ? 128 : 256))
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     bm.map[1] = bm.map[2] = bm.map[0];
     bm.end[0] = bm.end[1] = bm.end[2] = 2 * HIDDEN_DIM / 256;
+    if (pair)
+        return gemm_launch_pair<256, false, 1>(ma, bm, Hs, ld_hs, M, parts * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev],
+                                               st, g_gemm_err[dev], parts);
     return gemm_launch<256, false, 1>(ma, bm, Hs, ld_hs, M, parts * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev], st,
-                                      g_gemm_err[dev]);
+                                      g_gemm_err[dev], parts);
 }
 
 // The prompt pass's causal attention on tcgen05 (attention_tc5.cuh): the
@@ -1451,19 +1490,23 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
         CU(cudaMalloc(&g_gemm_err[dev], sizeof(uint32_t)));
         CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
     }
-    const int tiles256 = (N / 256) * (M / qb::tc::kBM);
+    // pair form (256 x 256 tiles on two SMs) for 256-row multiples whose tiles
+    // (or K splits of them) give most of the SM pairs work
+    const bool pair = pair_gemm_enabled() && all256 && M % (2 * qb::tc::kBM) == 0;
+    const int tiles256 = (N / 256) * (M / qb::tc::kBM) / (pair ? 2 : 1);
+    const int slots = pair ? nsm / 2 : nsm;
     int splits = 1;
-    if (split_cols >= N && all256 && 2 * tiles256 <= nsm)
-        for (int s = 2; s * tiles256 <= nsm && (s - 1) * split_cols + N <= ldc; s++)
+    if (split_cols >= N && all256 && 2 * tiles256 <= slots)
+        for (int s = 2; s * tiles256 <= slots && (s - 1) * split_cols + N <= ldc; s++)
             if ((K / qb::tc::kBK) % s == 0) splits = s;   // the largest that divides the K steps
     if (splits_used) *splits_used = splits;
-    const int bn = all256 && (splits > 1 || tiles256 >= nsm) ? 256 : 128;
+    const int bn = all256 && (pair || splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;
     qb::tc::BMaps bm;
     if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     int s = 0, end = 0;
     for (const BSeg& sg : segs) {
-        if (!cached_map(&bm.map[s], sg.B, (uint64_t)sg.rows, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)bn))
+        if (!cached_map(&bm.map[s], sg.B, (uint64_t)sg.rows, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)(pair ? bn / 2 : bn)))
             return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
         end += sg.rows / bn;
         bm.end[s++] = end;
@@ -1472,6 +1515,8 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     const int kb_b = Kb / qb::tc::kBK;
     const int so = splits > 1 ? split_cols : 0;
     const int mv = m_valid > 0 && m_valid < M ? m_valid : M;
+    if (pair) return c_fp32 ? gemm_launch_pair<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
+                            : gemm_launch_pair<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
     if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
                                  : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
     return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])

@@ -154,12 +154,12 @@ struct Layout {
 // kEpi = 1 (BN = 256, no K split): the tile holds the gate and up rows of the
 // same 128 hidden units (columns 0-127 gate, 128-255 up: the weights packed so,
 // n block j covering units 128 j ..); the epilogue writes h = silu(gate) * up as
-// three bf16 parts (C: bf16, rows ldc apart, parts HIDDEN_DIM columns apart),
-// the down projection's A operand.
+// epi_parts (1-3) bf16 parts (C: bf16, rows ldc apart, parts HIDDEN_DIM columns
+// apart), the down projection's A operand.
 template <int BN, bool kOutF32, int kEpi = 0>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
-                        int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err) {
+                        int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts) {
     using L = Layout<BN>;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
     static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
@@ -264,8 +264,8 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
                                              lo[j]);
                                 }
                                 *(uint4*)(row + i) = make_uint4(h[0], h[1], h[2], h[3]);
-                                *(uint4*)(row + HIDDEN_DIM + i) = make_uint4(md[0], md[1], md[2], md[3]);
-                                *(uint4*)(row + 2 * HIDDEN_DIM + i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                                if (epi_parts > 1) *(uint4*)(row + HIDDEN_DIM + i) = make_uint4(md[0], md[1], md[2], md[3]);
+                                if (epi_parts > 2) *(uint4*)(row + 2 * HIDDEN_DIM + i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                             }
                         }
                     }
@@ -286,6 +286,218 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, 2 * BN);
+}
+
+// ---------------------------------------------------------------------------
+// Pair form: a cluster of two CTAs (on two SMs) computes 256 x BN output tiles
+// with tcgen05.mma.cta_group::2.  CTA r of the pair loads rows 128 r .. 128 r +
+// 127 of the tile's A and rows (BN / 2) r .. of its B per K step and receives
+// its 128 rows of D (all BN columns) in its own tensor memory; the leader CTA
+// (rank 0) issues every MMA of the pair, reading both CTAs' shared memory.  Per
+// CTA and K step 16 KB of A and BN x 64 bytes of B cross from L2 for 128 x BN
+// x 64 of MMA work (at BN = 256: 32 KB, against 48 KB for a single-CTA tile),
+// so the L2 -> SM stream that bounds the single-CTA form carries a third less.
+// Both CTAs' TMA loads complete on the leader's stage barrier; the leader's MMA
+// commits arrive on both CTAs' barriers (multicast commit: stage free, tile's
+// accumulator complete); the epilogue warps of both CTAs hand each accumulator
+// back on the leader's barrier.  No TMA multicast: each CTA loads its own
+// boxes into its own shared memory.  Same work items, split K, row padding and
+// epilogues as the single-CTA form, with 256-row m blocks.
+constexpr int kPairStages = 6;
+template <int BN>
+struct PairLayout {
+    static constexpr int kABytes = kBM * kBK * 2;          // this CTA's 128 rows of A
+    static constexpr int kBBytes = (BN / 2) * kBK * 2;     // this CTA's BN / 2 rows of B
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOff = kPairStages * kStageBytes;
+    static constexpr int kSmem = kBarOff + (2 * kPairStages + 4) * 8 + 16 + 1024;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// 2-D tile load into this CTA's shared memory whose completion is counted on
+// the barrier at shared::cluster address `bar` (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on `bar` (the same offset) in both CTAs of the pair once every MMA
+// this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(smem_addr(bar)), "h"((uint16_t)3)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+
+// grid: an even number of CTAs (clusters of two), at most one per SM;
+// m_blocks counts 256-row blocks; B's maps have (BN / 2)-row boxes.
+template <int BN, bool kOutF32, int kEpi = 0>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K, int kb_b,
+                  int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts) {
+    using L = PairLayout<BN>;
+    static_assert(BN == 128 || BN == 256, "pair tiles: 256 x 128 or 256 x 256");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+    uint64_t* empty = full + kPairStages;
+    uint64_t* acc_full = empty + kPairStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int n_blocks = bm.end[2];
+    const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
+    const int nkb = K / kBK / splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 8); }   // 4 epilogue warps x 2 CTAs
+        fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
+        for (int s = 0; s < 3; s++)
+            if (s == 0 || bm.end[s] > bm.end[s - 1]) asm volatile("prefetch.tensormap [%0];" ::"l"(&bm.map[s]) : "memory");
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, 2 * BN);
+    tc_fence_before();
+    cluster_sync_all();   // both CTAs' barriers initialised and tensor memory allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t full0 = map_to_rank(smem_addr(full), 0);          // the leader's stage barriers
+    const uint32_t acc_empty0 = map_to_rank(smem_addr(acc_empty), 0);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int w = pair; w < nitems && ok; w += npairs) {
+                const int t = w % ntiles, kb0 = (w / ntiles) * nkb;
+                const int nb = t % n_blocks, m0 = (t / n_blocks) * 2 * kBM + kBM * (int)rank;
+                const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
+                const CUtensorMap* mb = &bm.map[sg];
+                const int n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN + (BN / 2) * (int)rank;
+                for (int kb = kb0; kb < kb0 + nkb; kb++, it++) {
+                    const uint32_t s = it % kPairStages;
+                    if (it >= (uint32_t)kPairStages && !mbar_wait(&empty[s], ((it / kPairStages) - 1) & 1u, kWaitNs)) {
+                        atomicOr(err, 1u); ok = false; break;
+                    }
+                    uint8_t* st = smem + s * L::kStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);   // both CTAs' bytes
+                    tma_load_2d_pair(st, &map_a, kb * kBK, m0, full0 + 8u * s);
+                    tma_load_2d_pair(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, full0 + 8u * s);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t id = idesc_bf16_f32(2 * kBM, BN);
+            uint32_t it = 0, i = 0;
+            bool ok = true;
+            for (int w = pair; w < nitems; w += npairs, i++) {
+                const uint32_t b = i & 1u, use = i >> 1;
+                if (ok && use > 0 && !mbar_wait(&acc_empty[b], (use - 1) & 1u, kWaitNs)) { atomicOr(err, 8u); ok = false; }
+                tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                for (int kb = 0; kb < nkb && ok; kb++, it++) {
+                    const uint32_t s = it % kPairStages;
+                    if (!mbar_wait(&full[s], (it / kPairStages) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a = smem_addr(smem + s * L::kStageBytes), bb = a + L::kABytes;
+                    #pragma unroll
+                    for (int kk = 0; kk < kBK / kUmmaK; kk++)
+                        mma_bf16_pair(d, kmajor_sw128_desc(a + kk * 32), kmajor_sw128_desc(bb + kk * 32), id, (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit_pair(&empty[s]);
+                }
+                mma_commit_pair(&acc_full[b]);   // complete (or abandoned: *err is set) in both CTAs
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        uint32_t i = 0;
+        for (int w = pair; w < nitems; w += npairs, i++) {
+            const uint32_t b = i & 1u, use = i >> 1;
+            if (!mbar_wait(&acc_full[b], use & 1u, 2 * kWaitNs)) atomicOr(err, 4u);
+            tc_fence_after();
+            const int t = w % ntiles;
+            const int n0 = (t % n_blocks) * BN + (w / ntiles) * c_split_off;
+            const int m_w = (t / n_blocks) * 2 * kBM + kBM * (int)rank + 32 * q, m = m_w + lane;
+            if constexpr (kEpi == 1) {
+                static_assert(kEpi != 1 || BN == 256, "the SwiGLU epilogue pairs 128 gate and 128 up columns");
+                if (m_w < m_valid) {
+                    const int u0 = (t % n_blocks) * 128;
+                    #pragma unroll 1
+                    for (int c = 0; c < 128; c += 32) {
+                        float g[32], u[32];
+                        tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, g);
+                        tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 + c), u);
+                        if (m < m_valid) {
+                            uint16_t* row = static_cast<uint16_t*>(C) + (size_t)m * ldc + u0 + c;
+                            #pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                uint32_t h[4], md[4], lo[4];
+                                #pragma unroll
+                                for (int j = 0; j < 4; j++) {
+                                    const float g0 = g[i + 2 * j], g1 = g[i + 2 * j + 1];
+                                    split3x2((g0 / (1.0f + expf(-g0))) * u[i + 2 * j], (g1 / (1.0f + expf(-g1))) * u[i + 2 * j + 1], h[j], md[j],
+                                             lo[j]);
+                                }
+                                *(uint4*)(row + i) = make_uint4(h[0], h[1], h[2], h[3]);
+                                if (epi_parts > 1) *(uint4*)(row + HIDDEN_DIM + i) = make_uint4(md[0], md[1], md[2], md[3]);
+                                if (epi_parts > 2) *(uint4*)(row + 2 * HIDDEN_DIM + i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            }
+                        }
+                    }
+                }
+            } else if (m_w < m_valid) {
+                #pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+                    if (m < m_valid) store32<kOutF32>(C, ldc, m, n0 + c, v);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acc_empty0 + 8u * b);   // this warp has read its lanes of accumulator b
+        }
+    }
+    tc_fence_before();
+    cluster_sync_all();   // every MMA, commit and remote arrival of the pair has landed
+    if (warp == 1) tmem_dealloc_pair(tmem, 2 * BN);
 }
 
 }  // namespace tc

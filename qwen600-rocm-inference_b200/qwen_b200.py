@@ -341,9 +341,10 @@ class Engine:
         """bf16 parts per activation in the tensor-core passes (3: fp32-exact, 2, 1)."""
         _check(self._lib.qwen_set_prefill_parts(self._h, int(parts)))
 
-    def set_prefill_attention(self, tcgen05=False):
-        """Prompt-pass attention on the tcgen05/TMEM kernel (True) or mma.sync (False, default)."""
-        _check(self._lib.qwen_set_prefill_attention(self._h, 1 if tcgen05 else 0))
+    def set_prefill_attention(self, kind=1):
+        """Prompt-pass attention kernel: 1 tcgen05/TMEM (default, one pass over the
+        keys with an online softmax), 0 mma.sync."""
+        _check(self._lib.qwen_set_prefill_attention(self._h, int(kind)))
 
     def set_prefill_mode(self, gemm=True):
         """Long prompts on the tensor cores (True, default) or one decode launch per token."""

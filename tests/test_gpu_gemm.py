@@ -21,11 +21,13 @@ def _case(qb, M, N, K, c_fp32, seed):
     return C.double(), ref, mag
 
 
-# (2048, 4096), (2048, 6144) and (4096, 4096) have more 128 x 256 tiles than SMs:
-# each CTA of the persistent kernel takes two to four tiles and alternates its
-# two TMEM accumulators; the others run one 128 x 128 tile per CTA.
+# M and N multiples of 256 run in the pair form (256 x 256 tiles on two SMs of a
+# cluster): (2048, 4096), (2048, 6144) and (4096, 4096) give a pair two to four
+# tiles, alternating its two TMEM accumulators.  The others run single-CTA tiles:
+# (1920, 4096) and (1920, 1024) 128 x 256 tiles, several per CTA; the small ones
+# one 128 x 128 tile per CTA.
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 384, 512), (384, 512, 1024), (2048, 4096, 1024), (2048, 1024, 3072),
-                                   (2048, 6144, 1024), (4096, 4096, 256)])
+                                   (2048, 6144, 1024), (4096, 4096, 256), (1920, 4096, 1024), (1920, 1024, 3072)])
 def test_gemm_fp32_out(qb, M, N, K):
     C, ref, mag = _case(qb, M, N, K, True, M + N + K)
     err = ((C - ref).abs() / (mag + 1e-30)).max().item()

@@ -1,6 +1,6 @@
 """qwen_prefill on the tensor cores (whole-prompt passes: tcgen05 GEMMs with the
 activations split into bf16 parts, causal attention over the KV cache on the
-mma.sync kernel or on the tcgen05/TMEM kernel) against the one-launch-per-token
+tcgen05/TMEM kernel or on the mma.sync kernel) against the one-launch-per-token
 path and the fp32 oracle.  Tolerances as in test_gpu_decode: max-abs <= 2e-2
 and relative RMS <= 2.5e-3 on the logits against the other paths; the two
 attention kernels agree to 1e-3."""
@@ -80,12 +80,12 @@ def test_prefill_edge_lengths(qb, checkpoint, n):
 
 
 def _pair_attention(qb, checkpoint, chunks):
-    """Prefill the chunks on a handle with the default (mma.sync) prompt-pass
-    attention and on one with the tcgen05/TMEM kernel; returns both final
+    """Prefill the chunks on a handle with the mma.sync prompt-pass attention
+    and on one with the tcgen05/TMEM kernel (the default); returns both final
     logits and both handles."""
     a, t = qb.Engine(checkpoint, 0), qb.Engine(checkpoint, 0)
-    a.set_prefill_attention(False)
-    t.set_prefill_attention(True)
+    a.set_prefill_attention(0)
+    t.set_prefill_attention(1)
     pos = 0
     for ch in chunks:
         la = a.prefill(ch, pos, want_logits=True)
