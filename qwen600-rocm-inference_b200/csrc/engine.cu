@@ -1450,7 +1450,7 @@ static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, 
         !cached_map(&mv, c->vt, (uint64_t)N_KV_HEADS * HEAD_DIM, SEQ_LEN, SEQ_LEN, HEAD_DIM))
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     attention_tc5_kernel<<<rows / kAttBlock * N_KV_HEADS, kA5Threads, A5Layout::kSmem, st>>>(mk, mv, c->pf_q, pos0, c->pf_as, 3 * HIDDEN_DIM,
-                                                                                           g_gemm_err[dev]);
+                                                                                           c->pf_parts, g_gemm_err[dev]);
     CU(cudaGetLastError());
     return QWEN_OK;
 }
