@@ -723,7 +723,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
-        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, m);
+        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, m, c->pf_parts);
         int sp_q = 1, sp_gu = 1;
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, c->pf_parts * DIM, DIM,
                           true, st, kLdQKV, &sp_q, m)) != QWEN_OK)
@@ -745,7 +745,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, c->pf_parts * Q_DIM, Q_DIM, true, st, DIM, &sp_o, m)) !=
             QWEN_OK)
             return rc;
-        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m);
+        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m, c->pf_parts);
         // gate|up + SwiGLU: fused into the GEMM epilogue when 128 x 256 tiles fill the GPU
         // without splitting K, else GEMM (split K when rows are few) + swiglu_split
         const bool fused = (2 * HIDDEN_DIM / 256) * (rows / tc::kBM) >= c->nsm;
@@ -757,7 +757,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
             if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, c->pf_parts * DIM, DIM, true,
                               st, kLdY, &sp_gu, m)) != QWEN_OK)
                 return rc;
-            swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m);
+            swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m, c->pf_parts);
         }
         if ((rc = gemm_tc(hs, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, c->pf_parts * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
                           &sp_d, m)) != QWEN_OK)
@@ -950,7 +950,7 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
         const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems(), c->b_part};
         int sp_d = 1, ld_d = 0, r2;
         if ((r2 = prefill_pass(c, 0, batch, &sp_d, &io, &ld_d)) != QWEN_OK) return r2;
-        qb::pf::norm_split_kernel<<<batch, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld_d, sp_d, c->params.final_ln, c->pf_as, kLdAs, batch);
+        qb::pf::norm_split_kernel<<<batch, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld_d, sp_d, c->params.final_ln, c->pf_as, kLdAs, batch, 3);
         if ((r2 = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true,
                           c->stream, 0, nullptr, batch)) != QWEN_OK)
             return r2;

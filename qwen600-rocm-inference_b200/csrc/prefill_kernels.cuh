@@ -48,14 +48,15 @@ __device__ __forceinline__ void put_split1(uint16_t* as_row, int col, float v) {
     as_row[Q_DIM + col] = m;
     as_row[2 * Q_DIM + col] = l;
 }
-// v (4 consecutive columns c..c+3 of a K-wide row) -> the three part blocks of As row r
-__device__ __forceinline__ void put_split4(uint16_t* As_row, int K, int c, float4 v) {
+// v (4 consecutive columns c..c+3 of a K-wide row) -> the first `parts` (1-3)
+// part blocks of As row r (the parts the next GEMM reads)
+__device__ __forceinline__ void put_split4(uint16_t* As_row, int K, int c, float4 v, int parts) {
     uint16_t h[4], m[4], l[4];
     split3(v.x, h[0], m[0], l[0]); split3(v.y, h[1], m[1], l[1]);
     split3(v.z, h[2], m[2], l[2]); split3(v.w, h[3], m[3], l[3]);
     *(uint2*)(As_row + c) = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
-    *(uint2*)(As_row + K + c) = make_uint2(m[0] | ((uint32_t)m[1] << 16), m[2] | ((uint32_t)m[3] << 16));
-    *(uint2*)(As_row + 2 * K + c) = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+    if (parts > 1) *(uint2*)(As_row + K + c) = make_uint2(m[0] | ((uint32_t)m[1] << 16), m[2] | ((uint32_t)m[3] << 16));
+    if (parts > 2) *(uint2*)(As_row + 2 * K + c) = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
 }
 
 // X[r] = embed[token[r]] (fp32) for r < m; 0 for m <= r < rows.
@@ -72,11 +73,12 @@ __global__ void embed_kernel(const uint16_t* __restrict__ embed, const int* __re
 
 // One block (256 threads, 4 columns each) per row: X[r] += add[r] (if add),
 // then RMSNorm with `gain` (the decode chain's formula: (x * (1 / sqrt(mean(x^2)
-// + eps))) * g) into As.  `add` may hold n_add partial sums side by side
+// + eps))) * g) into As as `parts` bf16 parts.  `add` may hold n_add partial sums side by side
 // (columns s * DIM ..): a GEMM whose K was split; they are added in order
 // s = 0, 1, ... and then to X.
 __global__ void __launch_bounds__(256) norm_split_kernel(float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
-                                                         const uint16_t* __restrict__ gain, uint16_t* __restrict__ As, int ld_as, int rows) {
+                                                         const uint16_t* __restrict__ gain, uint16_t* __restrict__ As, int ld_as, int rows,
+                                                         int parts) {
     __shared__ float part[8];
     const int r = blockIdx.x, t = threadIdx.x, c = 4 * t;
     if (r >= rows) return;
@@ -101,12 +103,12 @@ __global__ void __launch_bounds__(256) norm_split_kernel(float* __restrict__ X, 
     const float rs = 1.0f / sqrtf(ss * (1.0f / DIM) + EPS);
     const uint2 g = *(const uint2*)(gain + c);
     const float4 y = make_float4((v.x * rs) * bf_lo(g.x), (v.y * rs) * bf_hi(g.x), (v.z * rs) * bf_lo(g.y), (v.w * rs) * bf_hi(g.y));
-    put_split4(As + (size_t)r * ld_as, DIM, c, y);
+    put_split4(As + (size_t)r * ld_as, DIM, c, y, parts);
 }
 
 // Y: gate | up (n_add partial sums of both, part_stride columns apart, added in order)
 __global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, int n_add, int part_stride, uint16_t* __restrict__ As, int ld_as,
-                                    int rows) {
+                                    int rows, int parts) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int q = HIDDEN_DIM / 4;
     if (i >= (size_t)rows * q) return;
@@ -120,7 +122,7 @@ __global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, int n
     }
     const float4 h = make_float4((g.x / (1.0f + expf(-g.x))) * u.x, (g.y / (1.0f + expf(-g.y))) * u.y,
                                  (g.z / (1.0f + expf(-g.z))) * u.z, (g.w / (1.0f + expf(-g.w))) * u.w);
-    put_split4(As + (size_t)r * ld_as, HIDDEN_DIM, c, h);
+    put_split4(As + (size_t)r * ld_as, HIDDEN_DIM, c, h, parts);
 }
 
 // q/k/v of row r (position pos0 + r), one warp per (row, slot): slots 0..15 q
