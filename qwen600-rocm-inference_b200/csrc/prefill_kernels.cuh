@@ -157,12 +157,13 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int n_add
         x[0] = (x[0] * rs) * bf_lo(gn.x); x[1] = (x[1] * rs) * bf_hi(gn.x);
         x[2] = (x[2] * rs) * bf_lo(gn.y); x[3] = (x[3] * rs) * bf_hi(gn.y);
         const float* cs = rope + (size_t)pos * HEAD_DIM;
+        const int j0 = (4 * lane) & 63;   // this lane's 4 rotation angles, cos and sin as one 16-byte load each
+        const float4 c4 = *(const float4*)(cs + j0), s4 = *(const float4*)(cs + 64 + j0);
+        const float cj[4] = {c4.x, c4.y, c4.z, c4.w}, sj[4] = {s4.x, s4.y, s4.z, s4.w};
         #pragma unroll
         for (int e = 0; e < 4; e++) {
             const float pv = __shfl_xor_sync(0xffffffffu, x[e], 16);
-            const int d = 4 * lane + e, j = d & 63;
-            const float cj = cs[j], sj = cs[64 + j];
-            x[e] = d < 64 ? (x[e] * cj - pv * sj) : (pv * sj + x[e] * cj);
+            x[e] = 4 * lane + e < 64 ? (x[e] * cj[e] - pv * sj[e]) : (pv * sj[e] + x[e] * cj[e]);
         }
     }
     if (slot < 16) {
