@@ -90,13 +90,25 @@ static_assert(2 * A5Layout::kSmem > 228 * 1024, "one CTA per SM: the kernel allo
 // integer arithmetic instead of conversion instructions, so the conversion
 // unit is left to exp2: hi = the value rounded to 8 significant bits (adding
 // half a unit of the 16 dropped bits, then truncating), mid = the remainder
-// (exact in fp32) rounded the same way; |a - hi - mid| <= 2^-16 |a|.  Packed
-// like cvt_bf16x2 (a in the low half).
+// (exact in fp32) truncated to 8 significant bits; |a - hi - mid| < 2^-15 |a|.
+// Packed like cvt_bf16x2 (a in the low half).
 __device__ __forceinline__ void split2x2_int(float a, float b, uint32_t& h, uint32_t& m) {
     const uint32_t ra = __float_as_uint(a) + 0x8000u, rb = __float_as_uint(b) + 0x8000u;
     const float ma = a - __uint_as_float(ra & 0xffff0000u), mb = b - __uint_as_float(rb & 0xffff0000u);
     h = __byte_perm(ra, rb, 0x7632);
-    m = __byte_perm(__float_as_uint(ma) + 0x8000u, __float_as_uint(mb) + 0x8000u, 0x7632);
+    m = __byte_perm(__float_as_uint(ma), __float_as_uint(mb), 0x7632);
+}
+// 2^x by the conversion unit's approximation (ex2.approx, subnormal results
+// flushed to zero: a softmax weight below 2^-126 contributes nothing).
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
 
 // 16 or 32 consecutive 32-bit columns of this warp's 32 TMEM lanes (one row per
@@ -289,7 +301,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
             }
             float mh = -INFINITY;
             #pragma unroll
-            for (int i = 0; i < 32; i++) mh = fmaxf(mh, v[i]);
+            for (int i = 0; i < 32; i += 2) mh = max3f(mh, v[i], v[i + 1]);
             xm[((t & 1) * 2 + half) * 128 + m] = mh;
             named_bar(2, 256);
             const float mnew = fmaxf(mrun, fmaxf(mh, xm[((t & 1) * 2 + (half ^ 1)) * 128 + m]));   // finite: key 0 is in tile 0
@@ -305,7 +317,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
                 float ps = 0.f;
                 #pragma unroll
                 for (int j = 0; j < 16; j++) {
-                    const float p0 = exp2f(fmaf(v[2 * j], c2, -mc)), p1 = exp2f(fmaf(v[2 * j + 1], c2, -mc));
+                    const float p0 = ex2_ftz(fmaf(v[2 * j], c2, -mc)), p1 = ex2_ftz(fmaf(v[2 * j + 1], c2, -mc));
                     ps += p0 + p1;
                     split2x2_int(p0, p1, h[j], md[j]);
                 }
