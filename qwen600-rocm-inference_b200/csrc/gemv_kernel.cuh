@@ -6,7 +6,8 @@
 //
 //  gemv_direct_kernel  small and mid-size matrices (the decode chain's 4-13 MB
 //      projections).  No staging ring and no set-up: x is copied to shared
-//      memory once per CTA, and every warp takes (row, 1024-column segment)
+//      memory once per CTA while the first weight loads are already in flight
+//      (the two latencies overlap), and every warp takes (row, 1024-column segment)
 //      work items, loading its whole share of both rows of a pair with 16-byte
 //      streaming loads before the first FMA, so each SM keeps tens of KB of
 //      weight reads in flight.  Small CTAs (up to 8 warps) in a grid sized to
@@ -53,8 +54,7 @@ gemv_direct_kernel(const uint16_t* __restrict__ W, const uint16_t* __restrict__ 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int segs = gemv_direct_segs(K), rows_cta = gemv_direct_rows_cta(K);
     const int nthreads = rows_cta * segs * 32;
-    for (int i = tid; i < K / 8; i += nthreads) *(uint4*)&xs[8 * i] = __ldg((const uint4*)x + i);
-    __syncthreads();
+    bool staged = false;   // x goes to shared memory while the first weight loads are in flight
     const int r_in = warp / segs, seg = warp % segs;
     const int c0 = seg * 1024, c1 = min(K, c0 + 1024);
     const int nvec = (c1 - c0) / 256;   // 16-byte loads per lane per row (<= 4)
@@ -68,6 +68,11 @@ gemv_direct_kernel(const uint16_t* __restrict__ W, const uint16_t* __restrict__ 
         for (int i = 0; i < 4; i++) {
             if (i < nvec && va) wa[i] = ld_stream16(W + (size_t)ra * K + c0 + 256 * i + 8 * lane);
             if (i < nvec && vb) wb[i] = ld_stream16(W + (size_t)rb * K + c0 + 256 * i + 8 * lane);
+        }
+        if (!staged) {   // uniform: the loop bounds depend on the block only
+            for (int i = tid; i < K / 8; i += nthreads) *(uint4*)&xs[8 * i] = __ldg((const uint4*)x + i);
+            __syncthreads();
+            staged = true;
         }
         float sa = 0.f, sb = 0.f;
         #pragma unroll
