@@ -51,6 +51,8 @@ constexpr int kA5VBytes = HEAD_DIM * 128;         // a V^T tile: 128 rows (dims)
 // V of one layer, [head][position][dim] -> [head][dim][position] for positions
 // [0, n): 64 x 64 tiles through shared memory.  grid (ceil(n / 64), 2, N_KV_HEADS), block (64, 8).
 __global__ void transpose_v_kernel(const uint16_t* __restrict__ vc_l, uint16_t* __restrict__ vt, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ uint16_t t[64][66];
     const int p0 = blockIdx.x * 64, d0 = blockIdx.y * 64, hk = blockIdx.z;
     const uint16_t* src = vc_l + (size_t)hk * SEQ_LEN * HEAD_DIM;
@@ -174,6 +176,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
     const int q0 = qb * kAttBlock;
     const int last = min(pos0 + q0 + kAttBlock - 1, SEQ_LEN - 1);
     const int T = last / kA5Keys + 1;   // key tiles
+    pdl_launch_dependents();
 
     if (tid == 0) {
         for (int s = 0; s < kA5KStages; s++) { mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1); }
@@ -189,6 +192,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();   // Q, K and V come from the kernels before this one
 
     if (warp == 0) {
         if (lane == 0) {

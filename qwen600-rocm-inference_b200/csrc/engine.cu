@@ -46,6 +46,33 @@ static int fail(int code, const std::string& msg) { g_err = msg; return code; }
         if (e_ != cudaSuccess) return fail(QWEN_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
     } while (0)
 
+// Kernels of the prompt pass are launched with programmatic stream
+// serialization: each may start (set up barriers and tensor memory, load
+// weights) while the kernel before it finishes, and waits for it with
+// pdl_wait before it reads anything that kernel produced (ptx.cuh).
+// QWEN_B200_PDL=0 launches them normally.
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("QWEN_B200_PDL");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    return on;
+}
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 extern "C" const char* qwen_last_error(void) { return g_err.c_str(); }
 // for the library's host-only files (tokenizer.cpp)
 int qwen_internal_fail(int code, const std::string& msg) { return fail(code, msg); }
@@ -712,7 +739,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     const int* tok = io ? (batch ? io->tokens : io->tokens + pos0) : c->prompt + pos0;
     uint16_t* kc0 = io ? io->kc : c->kc;
     uint16_t* vc0 = io ? io->vc : c->vc;
-    embed_kernel<<<rows, 256, 0, st>>>(P.embed, tok, m, rows, c->pf_x);
+    CU(launch_pdl(embed_kernel, dim3(rows), dim3(256), 0, st, P.embed, tok, m, rows, c->pf_x));
     int rc, sp_o = 1, sp_d = 1;   // K splits of the O and down GEMMs: partial sums side by side in pf_y
     // with few rows pf_y also has room for split-K partials of the q|k|v and
     // gate|up GEMMs (their row strides widened to hold up to 4 / 6 of them)
@@ -723,13 +750,14 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
-        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, l ? c->pf_y : nullptr, ld_od, sp_d, P.in_ln[l], c->pf_as, kLdAs, m, c->pf_parts);
+        CU(launch_pdl(norm_split_kernel, dim3(m), dim3(256), 0, st, c->pf_x, (const float*)(l ? c->pf_y : nullptr), ld_od, sp_d, P.in_ln[l],
+                      c->pf_as, kLdAs, m, c->pf_parts));
         int sp_q = 1, sp_gu = 1;
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, c->pf_parts * DIM, DIM,
                           true, st, kLdQKV, &sp_q, m)) != QWEN_OK)
             return rc;
-        qkv_post_kernel<<<m * 4, 256, 0, st>>>(c->pf_y, ld_qkv, sp_q, kLdQKV, m, m, pos0, P.qn[l], P.kn[l], P.rope, c->pf_q, kc_l, vc_l,
-                                                  batch ? io->pos_rows : nullptr, batch ? io->row_stride : 0);
+        CU(launch_pdl(qkv_post_kernel, dim3(m * 4), dim3(256), 0, st, (const float*)c->pf_y, ld_qkv, sp_q, kLdQKV, m, m, pos0, P.qn[l], P.kn[l],
+                      (const float*)P.rope, c->pf_q, kc_l, vc_l, (const int*)(batch ? io->pos_rows : nullptr), (size_t)(batch ? io->row_stride : 0)));
         if (batch) {
             // key ranges per (row, KV head): enough blocks for two per SM
             const int S = std::max(1, std::min(kMaxKeySplits, (2 * c->nsm + m * N_KV_HEADS - 1) / (m * N_KV_HEADS)));
@@ -745,7 +773,8 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         if ((rc = gemm_tc(c->pf_as, kLdAs, {{c->wo_raw[l], DIM}}, Q_DIM, c->pf_y, ld_od, rows, c->pf_parts * Q_DIM, Q_DIM, true, st, DIM, &sp_o, m)) !=
             QWEN_OK)
             return rc;
-        norm_split_kernel<<<m, 256, 0, st>>>(c->pf_x, c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m, c->pf_parts);
+        CU(launch_pdl(norm_split_kernel, dim3(m), dim3(256), 0, st, c->pf_x, (const float*)c->pf_y, ld_od, sp_o, P.post_ln[l], c->pf_as, kLdAs, m,
+                      c->pf_parts));
         // gate|up + SwiGLU: fused into the GEMM epilogue when 128 x 256 tiles fill the GPU
         // without splitting K, else GEMM (split K when rows are few) + swiglu_split
         const bool fused = (2 * HIDDEN_DIM / 256) * (rows / tc::kBM) >= c->nsm;
@@ -757,7 +786,8 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
             if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wg[l], HIDDEN_DIM}, {P.wu[l], HIDDEN_DIM}}, DIM, c->pf_y, ld_gu, rows, c->pf_parts * DIM, DIM, true,
                               st, kLdY, &sp_gu, m)) != QWEN_OK)
                 return rc;
-            swiglu_split_kernel<<<(m * (HIDDEN_DIM / 4) + 255) / 256, 256, 0, st>>>(c->pf_y, ld_gu, sp_gu, kLdY, c->pf_as, kLdAs, m, c->pf_parts);
+            CU(launch_pdl(swiglu_split_kernel, dim3((m * (HIDDEN_DIM / 4) + 255) / 256), dim3(256), 0, st, (const float*)c->pf_y, ld_gu, sp_gu, kLdY,
+                          c->pf_as, kLdAs, m, c->pf_parts));
         }
         if ((rc = gemm_tc(hs, kLdAs, {{P.wd[l], DIM}}, HIDDEN_DIM, c->pf_y, ld_od, rows, c->pf_parts * HIDDEN_DIM, HIDDEN_DIM, true, st, DIM,
                           &sp_d, m)) != QWEN_OK)
@@ -792,8 +822,10 @@ extern "C" int qwen_prefill(qwen_t* c, const int* tokens, int n, int pos0, float
             if ((rc = prefill_pass(c, pos0 + s, m, &sp, nullptr, &ld)) != QWEN_OK) return rc;
         }
         const int last_row = m - 1;
-        qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld, sp, c->params.final_ln, last_row, c->pf_xn);
-        qb::pf::lm_head_f32_kernel<<<c->nsm * 8, 256, 0, c->stream>>>(c->params.lm, c->pf_xn, 0, VOCAB_SIZE, c->logits);
+        CU(launch_pdl(qb::pf::final_norm_row_kernel, dim3(1), dim3(256), 0, c->stream, (const float*)c->pf_x, (const float*)c->pf_y, ld, sp,
+                      c->params.final_ln, last_row, c->pf_xn));
+        CU(launch_pdl(qb::pf::lm_head_f32_kernel, dim3(c->nsm * 8), dim3(256), 0, c->stream, c->params.lm, (const float*)c->pf_xn, 0, (int)VOCAB_SIZE,
+                      c->logits));
         CU(cudaGetLastError());
         if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
         CU(cudaStreamSynchronize(c->stream));
@@ -912,8 +944,10 @@ extern "C" int qwen_batch_prefill(qwen_t* c, int slot, const int* tokens, int n,
         m = std::min(qb::pf::kMaxRows, n - s);
         if ((rc = prefill_pass(c, s, m, &sp, &io, &ld)) != QWEN_OK) return rc;
     }
-    qb::pf::final_norm_row_kernel<<<1, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld, sp, c->params.final_ln, m - 1, c->pf_xn);
-    qb::pf::lm_head_f32_kernel<<<c->nsm * 8, 256, 0, c->stream>>>(c->params.lm, c->pf_xn, 0, VOCAB_SIZE, c->logits);
+    CU(launch_pdl(qb::pf::final_norm_row_kernel, dim3(1), dim3(256), 0, c->stream, (const float*)c->pf_x, (const float*)c->pf_y, ld, sp,
+                  c->params.final_ln, m - 1, c->pf_xn));
+    CU(launch_pdl(qb::pf::lm_head_f32_kernel, dim3(c->nsm * 8), dim3(256), 0, c->stream, c->params.lm, (const float*)c->pf_xn, 0, (int)VOCAB_SIZE,
+                  c->logits));
     CU(cudaGetLastError());
     if (logits_host) CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)VOCAB_SIZE * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     CU(cudaStreamSynchronize(c->stream));
@@ -950,7 +984,8 @@ extern "C" int qwen_batch_step(qwen_t* c, int batch, const int* tokens, const in
         const PassIO io{c->b_tokens, c->bkc, c->bvc, c->b_pos, slot_elems(), c->b_part};
         int sp_d = 1, ld_d = 0, r2;
         if ((r2 = prefill_pass(c, 0, batch, &sp_d, &io, &ld_d)) != QWEN_OK) return r2;
-        qb::pf::norm_split_kernel<<<batch, 256, 0, c->stream>>>(c->pf_x, c->pf_y, ld_d, sp_d, c->params.final_ln, c->pf_as, kLdAs, batch, 3);
+        CU(launch_pdl(qb::pf::norm_split_kernel, dim3(batch), dim3(256), 0, c->stream, c->pf_x, (const float*)c->pf_y, ld_d, sp_d,
+                      c->params.final_ln, c->pf_as, kLdAs, batch, 3));
         if ((r2 = gemm_tc(c->pf_as, kLdAs, {{c->params.lm, VOCAB_SIZE}}, DIM, c->b_logits, VOCAB_SIZE, rows, 3 * DIM, DIM, true,
                           c->stream, 0, nullptr, batch)) != QWEN_OK)
             return r2;
@@ -1348,9 +1383,8 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
         attr_dev = dev;
     }
     const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
-    qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi><<<std::min(items, nsm), qb::tc::kThreads, qb::tc::Layout<BN>::kSmem, st>>>(
-        ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts);
-    CU(cudaGetLastError());
+    CU(launch_pdl(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi>, dim3(std::min(items, nsm)), dim3(qb::tc::kThreads),
+                  (size_t)qb::tc::Layout<BN>::kSmem, st, ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts));
     return QWEN_OK;
 }
 
@@ -1368,9 +1402,8 @@ int gemm_launch_pair(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, in
     }
     const int items = bm.end[2] * (M / (2 * qb::tc::kBM)) * splits;
     const int pairs = std::min(items, nsm / 2);
-    qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi><<<2 * pairs, qb::tc::kThreads, qb::tc::PairLayout<BN>::kSmem, st>>>(
-        ma, bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts);
-    CU(cudaGetLastError());
+    CU(launch_pdl(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi>, dim3(2 * pairs), dim3(qb::tc::kThreads), (size_t)qb::tc::PairLayout<BN>::kSmem, st, ma,
+                  bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts));
     return QWEN_OK;
 }
 
@@ -1444,14 +1477,13 @@ static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, 
     using namespace qb::pf;
     const int dev = c->device;
     const int n = pos0 + m;
-    transpose_v_kernel<<<dim3((n + 63) / 64, 2, N_KV_HEADS), dim3(64, 8), 0, st>>>(vc_l, c->vt, n);
+    CU(launch_pdl(transpose_v_kernel, dim3((n + 63) / 64, 2, N_KV_HEADS), dim3(64, 8), 0, st, vc_l, c->vt, n));
     CUtensorMap mk, mv;
     if (!cached_map(&mk, kc_l, (uint64_t)N_KV_HEADS * SEQ_LEN, HEAD_DIM, HEAD_DIM, kA5Keys) ||
         !cached_map(&mv, c->vt, (uint64_t)N_KV_HEADS * HEAD_DIM, SEQ_LEN, SEQ_LEN, HEAD_DIM))
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
-    attention_tc5_kernel<<<rows / kAttBlock * N_KV_HEADS, kA5Threads, A5Layout::kSmem, st>>>(mk, mv, c->pf_q, pos0, c->pf_as, 3 * HIDDEN_DIM,
-                                                                                           c->pf_parts, g_gemm_err[dev]);
-    CU(cudaGetLastError());
+    CU(launch_pdl(attention_tc5_kernel, dim3(rows / kAttBlock * N_KV_HEADS), dim3(kA5Threads), (size_t)A5Layout::kSmem, st, mk, mv,
+                  (const float*)c->pf_q, pos0, c->pf_as, 3 * HIDDEN_DIM, c->pf_parts, g_gemm_err[dev]));
     return QWEN_OK;
 }
 

@@ -11,7 +11,11 @@
 //   warp 0, one thread: TMA producer — 2-D tiled bulk tensor loads of a
 //           128 x 64 A box and a BN x 64 B box per K step, 128-byte swizzle,
 //           into a kStages-deep ring (mbarrier complete_tx) that runs on
-//           across tile boundaries; no multicast;
+//           across tile boundaries; no multicast.  Launched with programmatic
+//           stream serialization, the kernel starts while the kernel before it
+//           finishes: the producer loads the B (weight) boxes of the ring's
+//           first stages, then waits for that kernel (pdl_wait), then loads
+//           the A (activation) boxes;
 //   warp 1: allocates 2 x BN TMEM columns (two fp32 accumulators, 128 lanes =
 //           the tile's rows); one thread issues four 128 x BN x 16 MMAs per K
 //           step from shared-memory descriptors, commits each stage back to
@@ -174,6 +178,7 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
     const int n_blocks = bm.end[2];
     const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
     const int nkb = K / kBK / splits;   // K steps per work item
+    pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -191,24 +196,39 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
 
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t it = 0;   // stage-ring position across tiles
-            bool ok = true;
-            for (int w = blockIdx.x; w < nitems && ok; w += gridDim.x) {
-                const int t = w % ntiles, kb0 = (w / ntiles) * nkb;
-                const int nb = t % n_blocks, m0 = (t / n_blocks) * kBM;
+            // step `it` of the stage ring: work item blockIdx.x + (it / nkb) * gridDim.x, its K step it % nkb
+            auto step = [&](uint32_t it, int& m0, int& n0, int& kb, const CUtensorMap*& mb) {
+                const int w = blockIdx.x + (int)(it / (uint32_t)nkb) * (int)gridDim.x;
+                if (w >= nitems) return false;
+                const int t = w % ntiles, nb = t % n_blocks;
+                kb = (w / ntiles) * nkb + (int)(it % (uint32_t)nkb);
+                m0 = (t / n_blocks) * kBM;
                 const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
-                const CUtensorMap* mb = &bm.map[sg];
-                const int n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN;   // row in matrix sg
-                for (int kb = kb0; kb < kb0 + nkb; kb++, it++) {
-                    const uint32_t s = it % kStages;
-                    if (it >= (uint32_t)kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) {
-                        atomicOr(err, 1u); ok = false; break;
-                    }
-                    uint8_t* st = smem + s * L::kStageBytes;
-                    mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-                    tma_load_2d(st, &map_a, kb * kBK, m0, &full[s]);
-                    tma_load_2d(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, &full[s]);
-                }
+                mb = &bm.map[sg];
+                n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN;   // row in matrix sg
+                return true;
+            };
+            int m0, n0, kb;
+            const CUtensorMap* mb;
+            // the ring's first stages: weight boxes while the previous kernel may still run
+            // (no kernel writes the weights), activation boxes once it has finished
+            uint32_t npre = 0;
+            for (; npre < (uint32_t)kStages && step(npre, m0, n0, kb, mb); npre++) {
+                mbar_arrive_expect_tx(&full[npre], L::kStageBytes);
+                tma_load_2d(smem + npre * L::kStageBytes + L::kABytes, mb, (kb % kb_b) * kBK, n0, &full[npre]);
+            }
+            pdl_wait();
+            for (uint32_t it = 0; it < npre; it++) {
+                step(it, m0, n0, kb, mb);
+                tma_load_2d(smem + it * L::kStageBytes, &map_a, kb * kBK, m0, &full[it]);
+            }
+            for (uint32_t it = npre; step(it, m0, n0, kb, mb); it++) {   // it >= kStages here
+                const uint32_t s = it % kStages;
+                if (!mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); break; }
+                uint8_t* st = smem + s * L::kStageBytes;
+                mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                tma_load_2d(st, &map_a, kb * kBK, m0, &full[s]);
+                tma_load_2d(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -383,6 +403,7 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
     const int n_blocks = bm.end[2];
     const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
     const int nkb = K / kBK / splits;
+    pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPairStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -402,24 +423,39 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
 
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t it = 0;
-            bool ok = true;
-            for (int w = pair; w < nitems && ok; w += npairs) {
-                const int t = w % ntiles, kb0 = (w / ntiles) * nkb;
-                const int nb = t % n_blocks, m0 = (t / n_blocks) * 2 * kBM + kBM * (int)rank;
+            // step `it` of the stage ring: work item pair + (it / nkb) * npairs, its K step it % nkb
+            auto step = [&](uint32_t it, int& m0, int& n0, int& kb, const CUtensorMap*& mb) {
+                const int w = pair + (int)(it / (uint32_t)nkb) * npairs;
+                if (w >= nitems) return false;
+                const int t = w % ntiles, nb = t % n_blocks;
+                kb = (w / ntiles) * nkb + (int)(it % (uint32_t)nkb);
+                m0 = (t / n_blocks) * 2 * kBM + kBM * (int)rank;
                 const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
-                const CUtensorMap* mb = &bm.map[sg];
-                const int n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN + (BN / 2) * (int)rank;
-                for (int kb = kb0; kb < kb0 + nkb; kb++, it++) {
-                    const uint32_t s = it % kPairStages;
-                    if (it >= (uint32_t)kPairStages && !mbar_wait(&empty[s], ((it / kPairStages) - 1) & 1u, kWaitNs)) {
-                        atomicOr(err, 1u); ok = false; break;
-                    }
-                    uint8_t* st = smem + s * L::kStageBytes;
-                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);   // both CTAs' bytes
-                    tma_load_2d_pair(st, &map_a, kb * kBK, m0, full0 + 8u * s);
-                    tma_load_2d_pair(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, full0 + 8u * s);
-                }
+                mb = &bm.map[sg];
+                n0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN + (BN / 2) * (int)rank;
+                return true;
+            };
+            int m0, n0, kb;
+            const CUtensorMap* mb;
+            // the ring's first stages: weight boxes while the previous kernel may still run
+            // (no kernel writes the weights), activation boxes once it has finished
+            uint32_t npre = 0;
+            for (; npre < (uint32_t)kPairStages && step(npre, m0, n0, kb, mb); npre++) {
+                if (rank == 0) mbar_arrive_expect_tx(&full[npre], 2 * L::kStageBytes);   // both CTAs' bytes
+                tma_load_2d_pair(smem + npre * L::kStageBytes + L::kABytes, mb, (kb % kb_b) * kBK, n0, full0 + 8u * npre);
+            }
+            pdl_wait();
+            for (uint32_t it = 0; it < npre; it++) {
+                step(it, m0, n0, kb, mb);
+                tma_load_2d_pair(smem + it * L::kStageBytes, &map_a, kb * kBK, m0, full0 + 8u * it);
+            }
+            for (uint32_t it = npre; step(it, m0, n0, kb, mb); it++) {   // it >= kPairStages here
+                const uint32_t s = it % kPairStages;
+                if (!mbar_wait(&empty[s], ((it / kPairStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); break; }
+                uint8_t* st = smem + s * L::kStageBytes;
+                if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+                tma_load_2d_pair(st, &map_a, kb * kBK, m0, full0 + 8u * s);
+                tma_load_2d_pair(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, full0 + 8u * s);
             }
         }
     } else if (warp == 1) {

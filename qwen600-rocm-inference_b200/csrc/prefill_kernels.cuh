@@ -61,6 +61,8 @@ __device__ __forceinline__ void put_split4(uint16_t* As_row, int K, int c, float
 
 // X[r] = embed[token[r]] (fp32) for r < m; 0 for m <= r < rows.
 __global__ void embed_kernel(const uint16_t* __restrict__ embed, const int* __restrict__ tokens, int m, int rows, float* __restrict__ X) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int r = blockIdx.x, t = threadIdx.x;   // 256 threads x 4 columns
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < m) {
@@ -79,6 +81,8 @@ __global__ void embed_kernel(const uint16_t* __restrict__ embed, const int* __re
 __global__ void __launch_bounds__(256) norm_split_kernel(float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
                                                          const uint16_t* __restrict__ gain, uint16_t* __restrict__ As, int ld_as, int rows,
                                                          int parts) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float part[8];
     const int r = blockIdx.x, t = threadIdx.x, c = 4 * t;
     if (r >= rows) return;
@@ -109,6 +113,8 @@ __global__ void __launch_bounds__(256) norm_split_kernel(float* __restrict__ X, 
 // Y: gate | up (n_add partial sums of both, part_stride columns apart, added in order)
 __global__ void swiglu_split_kernel(const float* __restrict__ Y, int ld_y, int n_add, int part_stride, uint16_t* __restrict__ As, int ld_as,
                                     int rows, int parts) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int q = HIDDEN_DIM / 4;
     if (i >= (size_t)rows * q) return;
@@ -138,6 +144,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int n_add
                                 const uint16_t* __restrict__ qn, const uint16_t* __restrict__ kn, const float* __restrict__ rope,
                                 float* __restrict__ Q, uint16_t* __restrict__ kc_l, uint16_t* __restrict__ vc_l,
                                 const int* __restrict__ pos_rows, size_t row_cache_stride) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int r = w >> 5, slot = w & 31;
     if (r >= rows) return;
@@ -181,6 +189,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ Y, int ld_y, int n_add
 // formula, qwen_model.cuh:836-839) into xn (fp32).  One block of 256 threads.
 __global__ void final_norm_row_kernel(const float* __restrict__ X, const float* __restrict__ add, int ld_add, int n_add,
                                       const uint16_t* __restrict__ gain, int row, float* __restrict__ xn) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float part[8];
     const int t = threadIdx.x, c = 4 * t;
     float4 v = *(const float4*)(X + (size_t)row * DIM + c);
@@ -207,6 +217,8 @@ __global__ void final_norm_row_kernel(const float* __restrict__ X, const float* 
 // row, two rows in flight per warp; lane l holds xn[8 (l + 32 i) .. +7].
 __global__ void __launch_bounds__(256) lm_head_f32_kernel(const uint16_t* __restrict__ lm, const float* __restrict__ xn, int r0, int r1,
                                                           float* __restrict__ logits) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     float xr[4][8];
     #pragma unroll

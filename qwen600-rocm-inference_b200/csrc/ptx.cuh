@@ -11,6 +11,17 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it in the stream is still
+// running, once every CTA of that kernel has called pdl_launch_dependents (or
+// exited); pdl_wait then blocks until the earlier kernel has completed and its
+// memory operations are visible.  So a kernel does only work that needs nothing
+// from earlier kernels (barrier set-up, tensor-memory allocation, loads of
+// weights no kernel writes) before pdl_wait, and writes nothing global before
+// it.  For a normally launched kernel both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
