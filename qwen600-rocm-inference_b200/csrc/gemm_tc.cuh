@@ -222,13 +222,25 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
                 step(it, m0, n0, kb, mb);
                 tma_load_2d(smem + it * L::kStageBytes, &map_a, kb * kBK, m0, &full[it]);
             }
-            for (uint32_t it = npre; step(it, m0, n0, kb, mb); it++) {   // it >= kStages here
-                const uint32_t s = it % kStages;
-                if (!mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); break; }
-                uint8_t* st = smem + s * L::kStageBytes;
-                mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-                tma_load_2d(st, &map_a, kb * kBK, m0, &full[s]);
-                tma_load_2d(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, &full[s]);
+            // the rest: coordinates once per work item (a division per step would slow this thread
+            // below the MMA rate)
+            uint32_t it = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; w < nitems && ok; w += gridDim.x) {
+                const int t = w % ntiles, kb0 = (w / ntiles) * nkb;
+                const int nb = t % n_blocks, mi0 = (t / n_blocks) * kBM;
+                const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
+                const CUtensorMap* mbi = &bm.map[sg];
+                const int ni0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN;   // row in matrix sg
+                for (int k = kb0; k < kb0 + nkb; k++, it++) {
+                    if (it < npre) continue;   // loaded above
+                    const uint32_t s = it % kStages;
+                    if (!mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); ok = false; break; }
+                    uint8_t* st = smem + s * L::kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                    tma_load_2d(st, &map_a, k * kBK, mi0, &full[s]);
+                    tma_load_2d(st + L::kABytes, mbi, (k % kb_b) * kBK, ni0, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
@@ -449,13 +461,25 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                 step(it, m0, n0, kb, mb);
                 tma_load_2d_pair(smem + it * L::kStageBytes, &map_a, kb * kBK, m0, full0 + 8u * it);
             }
-            for (uint32_t it = npre; step(it, m0, n0, kb, mb); it++) {   // it >= kPairStages here
-                const uint32_t s = it % kPairStages;
-                if (!mbar_wait(&empty[s], ((it / kPairStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); break; }
-                uint8_t* st = smem + s * L::kStageBytes;
-                if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
-                tma_load_2d_pair(st, &map_a, kb * kBK, m0, full0 + 8u * s);
-                tma_load_2d_pair(st + L::kABytes, mb, (kb % kb_b) * kBK, n0, full0 + 8u * s);
+            // the rest: coordinates once per work item (a division per step would slow this thread
+            // below the MMA rate)
+            uint32_t it = 0;
+            bool ok = true;
+            for (int w = pair; w < nitems && ok; w += npairs) {
+                const int t = w % ntiles, kb0 = (w / ntiles) * nkb;
+                const int nb = t % n_blocks, mi0 = (t / n_blocks) * 2 * kBM + kBM * (int)rank;
+                const int sg = nb < bm.end[0] ? 0 : (nb < bm.end[1] ? 1 : 2);
+                const CUtensorMap* mbi = &bm.map[sg];
+                const int ni0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN + (BN / 2) * (int)rank;
+                for (int k = kb0; k < kb0 + nkb; k++, it++) {
+                    if (it < npre) continue;   // loaded above
+                    const uint32_t s = it % kPairStages;
+                    if (!mbar_wait(&empty[s], ((it / kPairStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); ok = false; break; }
+                    uint8_t* st = smem + s * L::kStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);   // both CTAs' bytes
+                    tma_load_2d_pair(st, &map_a, k * kBK, mi0, full0 + 8u * s);
+                    tma_load_2d_pair(st + L::kABytes, mbi, (k % kb_b) * kBK, ni0, full0 + 8u * s);
+                }
             }
         }
     } else if (warp == 1) {
