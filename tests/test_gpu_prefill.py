@@ -136,3 +136,39 @@ def test_prefill_attention_kind_rejects_unknown(qb, checkpoint):
             qb._check(e._lib.qwen_set_prefill_attention(e._h, 2))
     finally:
         e.close()
+
+
+def test_prefill_programmatic_launch_matches_normal_launch(qb, checkpoint, tmp_path):
+    """The prompt pass's kernels start early under programmatic dependent launch
+    and wait for their predecessors on the device; launched normally
+    (QWEN_B200_PDL=0, read once per process, so in a child process) the same
+    kernels must give bit-identical logits, over two passes (2100 + 200 tokens)."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG
+    chunks = [_prompt(2100, 61), _prompt(200, 62)]
+    script = (
+        "import importlib.util, sys, numpy as np\n"
+        f"spec = importlib.util.spec_from_file_location('qwen_b200', {os.path.join(PKG, 'qwen_b200.py')!r})\n"
+        "qb = importlib.util.module_from_spec(spec); spec.loader.exec_module(qb)\n"
+        f"e = qb.Engine({checkpoint!r}, 0)\n"
+        f"chunks = {chunks!r}\n"
+        "pos = 0\n"
+        "for ch in chunks:\n"
+        "    lg = e.prefill(ch, pos, want_logits=True); pos += len(ch)\n"
+        f"np.save({str(tmp_path / 'normal.npy')!r}, lg)\n"
+        "e.close()\n")
+    env = dict(os.environ, QWEN_B200_PDL="0")
+    r = subprocess.run([sys.executable, "-c", script], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    e = qb.Engine(checkpoint, 0)
+    try:
+        pos = 0
+        for ch in chunks:
+            lg = e.prefill(ch, pos, want_logits=True)
+            pos += len(ch)
+    finally:
+        e.close()
+    normal = np.load(tmp_path / "normal.npy")
+    assert np.array_equal(lg, normal), np.abs(lg.astype(np.float64) - normal).max()
