@@ -278,6 +278,7 @@ struct qwen_ctx {
     bool gemm_prefill = true;   // qwen_prefill uses prefill_pass for long prompts
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
     int att5 = 1;               // prompt-pass attention: 1 tcgen05 (attention_tc5.cuh, the default), 0 mma.sync
+    bool qkv_epi = true;        // QK-norm, RoPE and the K/V append in the q|k|v GEMM's epilogue where it applies
     uint16_t* vt = nullptr;     // the layer's V transposed ([head][dim][position]) for the tcgen05 attention
     int last_k = 0;
 };
@@ -419,6 +420,8 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     if (const char* e = getenv("QWEN_B200_POLL_NS")) P.poll_ns = std::max(0, std::min(2000, atoi(e)));
     // prompt-pass attention: "tc5" selects the tcgen05 kernel, "mma" the mma.sync one
     if (const char* e = getenv("QWEN_B200_PREFILL_ATTN")) c->att5 = strcmp(e, "mma") == 0 ? 0 : 1;
+    // "0": q|k|v GEMM with fp32 output, then qkv_post_kernel, in every prompt pass
+    if (const char* e = getenv("QWEN_B200_QKV_EPILOGUE")) c->qkv_epi = strcmp(e, "0") != 0;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -682,7 +685,12 @@ extern "C" int qwen_generate_timed(qwen_t* c, int token, int pos, int n_steps, c
 }
 
 static int gemm_check(qwen_t* c);
-static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, int pos0, int m, int rows, cudaStream_t st);
+static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, int pos0, int m, int rows, int vt_n, cudaStream_t st);
+static int gemm_qkv_rope(const void* A, int lda, const DecodeParams& P, int l, const qb::tc::QkvOut& qo, int M, int m_valid, cudaStream_t st,
+                         int parts);
+namespace {
+bool pair_gemm_enabled();
+}
 static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs, int ld_hs, int M, int m_valid, cudaStream_t st, int parts);
 struct BSeg { const void* B; int rows; };   // one weight matrix [rows][Kb] of a grouped GEMM
 static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int ldb, void* C, int ldc, int M, int K, int Kb, bool c_fp32,
@@ -747,17 +755,29 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
     const int ld_qkv = kLdQKV * (int)std::max<size_t>(1, std::min<size_t>(8, ycap / ((size_t)rows * kLdQKV)));
     const int ld_gu = kLdY * (int)std::max<size_t>(1, std::min<size_t>(6, ycap / ((size_t)rows * kLdY)));
     const int ld_od = std::max(kLdY, DIM * (int)std::min<size_t>(24, ycap / ((size_t)rows * DIM)));   // O and down partials
+    // QK-norm, RoPE, the K/V append and V's transposed copy in the q|k|v GEMM's
+    // epilogue when that GEMM runs on SM pairs without splitting K (its 256 x
+    // 256 tiles give more than half the pairs two tiles) and attention is the
+    // tcgen05 kernel (the reader of the transposed copy); else qkv_post_kernel
+    const bool fuse_qkv = !batch && c->att5 && c->qkv_epi && pair_gemm_enabled() && rows % (2 * tc::kBM) == 0 &&
+                          2 * (kLdQKV / 256) * (rows / (2 * tc::kBM)) > c->nsm / 2;
     for (int l = 0; l < N_LAYERS; l++) {
         uint16_t* kc_l = kc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         uint16_t* vc_l = vc0 + (size_t)l * kGroups * SEQ_LEN * HEAD_DIM;
         CU(launch_pdl(norm_split_kernel, dim3(m), dim3(256), 0, st, c->pf_x, (const float*)(l ? c->pf_y : nullptr), ld_od, sp_d, P.in_ln[l],
                       c->pf_as, kLdAs, m, c->pf_parts));
         int sp_q = 1, sp_gu = 1;
-        if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, c->pf_parts * DIM, DIM,
-                          true, st, kLdQKV, &sp_q, m)) != QWEN_OK)
-            return rc;
-        CU(launch_pdl(qkv_post_kernel, dim3(m * 4), dim3(256), 0, st, (const float*)c->pf_y, ld_qkv, sp_q, kLdQKV, m, m, pos0, P.qn[l], P.kn[l],
-                      (const float*)P.rope, c->pf_q, kc_l, vc_l, (const int*)(batch ? io->pos_rows : nullptr), (size_t)(batch ? io->row_stride : 0)));
+        if (fuse_qkv) {
+            const qb::tc::QkvOut qo{c->pf_q, kc_l, vc_l, c->vt, P.qn[l], P.kn[l], (const float*)P.rope, pos0};
+            if ((rc = gemm_qkv_rope(c->pf_as, kLdAs, P, l, qo, rows, m, st, c->pf_parts)) != QWEN_OK) return rc;
+        } else {
+            if ((rc = gemm_tc(c->pf_as, kLdAs, {{P.wq[l], Q_DIM}, {P.wk[l], KV_DIM}, {P.wv[l], KV_DIM}}, DIM, c->pf_y, ld_qkv, rows, c->pf_parts * DIM,
+                              DIM, true, st, kLdQKV, &sp_q, m)) != QWEN_OK)
+                return rc;
+            CU(launch_pdl(qkv_post_kernel, dim3(m * 4), dim3(256), 0, st, (const float*)c->pf_y, ld_qkv, sp_q, kLdQKV, m, m, pos0, P.qn[l], P.kn[l],
+                          (const float*)P.rope, c->pf_q, kc_l, vc_l, (const int*)(batch ? io->pos_rows : nullptr),
+                          (size_t)(batch ? io->row_stride : 0)));
+        }
         if (batch) {
             // key ranges per (row, KV head): enough blocks for two per SM
             const int S = std::max(1, std::min(kMaxKeySplits, (2 * c->nsm + m * N_KV_HEADS - 1) / (m * N_KV_HEADS)));
@@ -765,7 +785,7 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
                                                                                  c->pf_as, kLdAs, io->part);
             if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_as, kLdAs);
         } else if (c->att5) {
-            if ((rc = attention_tc5(c, kc_l, vc_l, pos0, m, rows, st)) != QWEN_OK) return rc;
+            if ((rc = attention_tc5(c, kc_l, vc_l, pos0, m, rows, fuse_qkv ? pos0 : pos0 + m, st)) != QWEN_OK) return rc;
         } else {
             attention_tc_kernel<<<rows / kAttBlock * N_KV_HEADS, kTcThreads, sizeof(AttTcSmem), st>>>(c->pf_q, pos0, kc_l, vc_l, c->pf_as,
                                                                                                        kLdAs);
@@ -1391,7 +1411,7 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
 // The pair (2-SM) form: clusters of two CTAs, 256 x BN tiles.
 template <int BN, bool F32, int kEpi = 0>
 int gemm_launch_pair(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                     int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3) {
+                     int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3, const qb::tc::QkvOut& qo = qb::tc::QkvOut{}) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -1403,7 +1423,7 @@ int gemm_launch_pair(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, in
     const int items = bm.end[2] * (M / (2 * qb::tc::kBM)) * splits;
     const int pairs = std::min(items, nsm / 2);
     CU(launch_pdl(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi>, dim3(2 * pairs), dim3(qb::tc::kThreads), (size_t)qb::tc::PairLayout<BN>::kSmem, st, ma,
-                  bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts));
+                  bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts, qo));
     return QWEN_OK;
 }
 
@@ -1440,6 +1460,8 @@ static int gemm_prepare(int dev) {
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::PairLayout<256>::kSmem));
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             qb::tc::PairLayout<256>::kSmem));
+    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            qb::tc::PairLayout<256>::kSmem));
     done[dev].store(true, std::memory_order_release);
     return QWEN_OK;
 }
@@ -1470,14 +1492,40 @@ static int gemm_swiglu(const void* A, int lda, const uint16_t* wgu, uint16_t* Hs
                                       g_gemm_err[dev], parts);
 }
 
+// The q|k|v projection of the prompt rows with QK-norm, RoPE, the K/V cache
+// append and the transposed copy of V in its epilogue (QkvOut): A [M][parts
+// DIM] (bf16 parts) against wq | wk | wv; rows m_valid .. M-1 are padding.
+// Pair form only (M a multiple of 256), K not split.
+static int gemm_qkv_rope(const void* A, int lda, const DecodeParams& P, int l, const qb::tc::QkvOut& qo, int M, int m_valid, cudaStream_t st,
+                         int parts) {
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev >= 64) return fail(QWEN_E_UNSUPPORTED, "device index >= 64");
+    const int rc = gemm_prepare(dev);
+    if (rc != QWEN_OK) return rc;
+    if (M % (2 * qb::tc::kBM)) return fail(QWEN_E_ARG, "the q|k|v epilogue runs on 256-row blocks");
+    CUtensorMap ma;
+    qb::tc::BMaps bm;
+    if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)(parts * DIM), (uint64_t)lda, qb::tc::kBM) ||
+        !cached_map(&bm.map[0], P.wq[l], (uint64_t)Q_DIM, (uint64_t)DIM, (uint64_t)DIM, 128) ||
+        !cached_map(&bm.map[1], P.wk[l], (uint64_t)KV_DIM, (uint64_t)DIM, (uint64_t)DIM, 128) ||
+        !cached_map(&bm.map[2], P.wv[l], (uint64_t)KV_DIM, (uint64_t)DIM, (uint64_t)DIM, 128))
+        return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    bm.end[0] = Q_DIM / 256;
+    bm.end[1] = bm.end[0] + KV_DIM / 256;
+    bm.end[2] = bm.end[1] + KV_DIM / 256;
+    return gemm_launch_pair<256, true, 2>(ma, bm, nullptr, 0, M, parts * DIM, DIM / qb::tc::kBK, 1, 0, m_valid > 0 ? m_valid : M, g_nsm[dev], st,
+                                          g_gemm_err[dev], parts, qo);
+}
+
 // The prompt pass's causal attention on tcgen05 (attention_tc5.cuh): the
-// layer's V for positions [0, pos0 + m) transposed into c->vt, then one CTA
+// layer's V for positions [0, vt_n) transposed into c->vt (positions vt_n ..
+// pos0 + m - 1 are there already: the q|k|v epilogue wrote them), then one CTA
 // per (64 rows, KV head).  Its error word is the GEMMs' (checked after the pass).
-static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, int pos0, int m, int rows, cudaStream_t st) {
+static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, int pos0, int m, int rows, int vt_n, cudaStream_t st) {
     using namespace qb::pf;
     const int dev = c->device;
-    const int n = pos0 + m;
-    CU(launch_pdl(transpose_v_kernel, dim3((n + 63) / 64, 2, N_KV_HEADS), dim3(64, 8), 0, st, vc_l, c->vt, n));
+    if (vt_n > 0) CU(launch_pdl(transpose_v_kernel, dim3((vt_n + 63) / 64, 2, N_KV_HEADS), dim3(64, 8), 0, st, vc_l, c->vt, vt_n));
     CUtensorMap mk, mv;
     if (!cached_map(&mk, kc_l, (uint64_t)N_KV_HEADS * SEQ_LEN, HEAD_DIM, HEAD_DIM, kA5Keys) ||
         !cached_map(&mv, c->vt, (uint64_t)N_KV_HEADS * HEAD_DIM, SEQ_LEN, SEQ_LEN, HEAD_DIM))

@@ -147,6 +147,23 @@ struct BMaps {
     CUtensorMap map[3];
     int end[3];   // cumulative n-block counts; end[2] = total n blocks
 };
+// Outputs of the q|k|v epilogue (pair form, kEpi 2): the GEMM's N columns are
+// the 16 q heads, then the 8 k heads, then the 8 v heads (128 each) of rows at
+// positions pos0 + m.  q and k heads are RMS-normalised over their 128 values,
+// scaled by qn / kn and rotated (RoPE: value j < 64 pairs with j + 64 at angle
+// j, the table's row `pos` holding cos in columns 0-63 and sin in 64-127); q
+// goes to q (fp32, rows Q_DIM apart), k and v to the layer's caches
+// ([kv head][SEQ_LEN][128], bf16) and v also to vt ([kv head][128][SEQ_LEN]).
+struct QkvOut {
+    float* q;
+    uint16_t* kc;
+    uint16_t* vc;
+    uint16_t* vt;
+    const uint16_t* qn;
+    const uint16_t* kn;
+    const float* rope;
+    int pos0;
+};
 template <int BN>
 struct Layout {
     static constexpr int kABytes = kBM * kBK * 2;
@@ -394,12 +411,125 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
 
+// The q|k|v epilogue (QkvOut) of one row m (position qo.pos0 + m) and one
+// head: ta addresses the head's 128 fp32 accumulator columns of this warp's
+// TMEM lanes; hd is the head's 128-column block of the GEMM (0-15 q, 16-23 k,
+// 24-31 v).  row_ok: the row is valid (rows at m_valid and beyond are padding
+// and stored nowhere); pair_ok: so is the other row of this lane's pair (lanes
+// 2i, 2i + 1) and the pair's first position is even.  Warp-collective (TMEM
+// loads; the v^T stores pair adjacent positions by a shuffle).  q and k heads
+// are read twice (sum of squares, then 32 + 32 rotation partners at a time) so
+// that at most 64 values are live.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const float (&v)[32]);
+template <>
+__device__ __forceinline__ void store_row32<float>(float* dst, const float (&v)[32]) {
+    float4* d = reinterpret_cast<float4*>(dst);
+    #pragma unroll
+    for (int i = 0; i < 8; i++) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+template <>
+__device__ __forceinline__ void store_row32<uint16_t>(uint16_t* dst, const float (&v)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    #pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint32_t w[4];
+        #pragma unroll
+        for (int e = 0; e < 4; e++) w[e] = (uint32_t)f2bf(v[8 * i + 2 * e]) | ((uint32_t)f2bf(v[8 * i + 2 * e + 1]) << 16);
+        d[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ __forceinline__ void qkv_head_out(const QkvOut& qo, int hd, int m, bool row_ok, bool pair_ok, uint32_t ta) {
+    const int pos = qo.pos0 + m;
+    const bool is_q = hd < N_HEADS, is_v = hd >= N_HEADS + N_KV_HEADS;
+    const int h = is_q ? hd : hd - N_HEADS - (is_v ? N_KV_HEADS : 0);
+    if (!is_v) {   // QK-norm, then RoPE (rotate-half pairs j, j + 64 at angle j)
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        #pragma unroll 1
+        for (int c = 0; c < HEAD_DIM; c += 32) {
+            float v[32];
+            tmem_ld32(ta + (uint32_t)c, v);
+            #pragma unroll
+            for (int j = 0; j < 32; j++) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
+        }
+        const float rs = 1.0f / sqrtf(((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / HEAD_DIM) + EPS);
+        const uint4* g4 = reinterpret_cast<const uint4*>(is_q ? qo.qn : qo.kn);
+        const float4* cs = reinterpret_cast<const float4*>(qo.rope + (size_t)(row_ok ? pos : 0) * HEAD_DIM);
+        float* qd = qo.q + (size_t)m * Q_DIM + h * HEAD_DIM;
+        uint16_t* kd = qo.kc + ((size_t)h * SEQ_LEN + pos) * HEAD_DIM;
+        #pragma unroll 1
+        for (int c = 0; c < HEAD_DIM / 2; c += 32) {
+            float a[32], b[32];
+            tmem_ld32(ta + (uint32_t)c, a);
+            tmem_ld32(ta + (uint32_t)(c + HEAD_DIM / 2), b);
+            #pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint4 ga = __ldg(g4 + c / 8 + i), gb = __ldg(g4 + (c + HEAD_DIM / 2) / 8 + i);
+                const uint32_t wa[4] = {ga.x, ga.y, ga.z, ga.w}, wb[4] = {gb.x, gb.y, gb.z, gb.w};
+                #pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    a[8 * i + 2 * e] = (a[8 * i + 2 * e] * rs) * bf_lo(wa[e]);
+                    a[8 * i + 2 * e + 1] = (a[8 * i + 2 * e + 1] * rs) * bf_hi(wa[e]);
+                    b[8 * i + 2 * e] = (b[8 * i + 2 * e] * rs) * bf_lo(wb[e]);
+                    b[8 * i + 2 * e + 1] = (b[8 * i + 2 * e + 1] * rs) * bf_hi(wb[e]);
+                }
+            }
+            #pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 co = __ldg(cs + c / 4 + i), si = __ldg(cs + (c + HEAD_DIM / 2) / 4 + i);
+                const float cj[4] = {co.x, co.y, co.z, co.w}, sj[4] = {si.x, si.y, si.z, si.w};
+                #pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float x0 = a[4 * i + e], x1 = b[4 * i + e];
+                    a[4 * i + e] = x0 * cj[e] - x1 * sj[e];
+                    b[4 * i + e] = x0 * sj[e] + x1 * cj[e];
+                }
+            }
+            if (row_ok) {
+                if (is_q) {
+                    store_row32(qd + c, a);
+                    store_row32(qd + c + HEAD_DIM / 2, b);
+                } else {
+                    store_row32(kd + c, a);
+                    store_row32(kd + c + HEAD_DIM / 2, b);
+                }
+            }
+        }
+        return;
+    }
+    uint16_t* vd = qo.vc + ((size_t)h * SEQ_LEN + pos) * HEAD_DIM;
+    uint16_t* t = qo.vt + (size_t)h * HEAD_DIM * SEQ_LEN;
+    const bool odd = (threadIdx.x & 1) != 0;
+    #pragma unroll 1
+    for (int c = 0; c < HEAD_DIM; c += 32) {
+        float v[32];
+        tmem_ld32(ta + (uint32_t)c, v);
+        if (row_ok) store_row32(vd + c, v);
+        // v^T: for each dim, consecutive lanes' positions are consecutive
+        #pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+            if (pair_ok) {   // even lane: dim c + j of positions pos, pos + 1; odd lane: dim c + j + 1 of pos - 1, pos
+                if (!odd)
+                    *reinterpret_cast<uint32_t*>(t + (size_t)(c + j) * SEQ_LEN + pos) = (uint32_t)f2bf(v[j]) | ((uint32_t)f2bf(recv) << 16);
+                else
+                    *reinterpret_cast<uint32_t*>(t + (size_t)(c + j + 1) * SEQ_LEN + pos - 1) =
+                        (uint32_t)f2bf(recv) | ((uint32_t)f2bf(v[j + 1]) << 16);
+            } else if (row_ok) {
+                t[(size_t)(c + j) * SEQ_LEN + pos] = f2bf(v[j]);
+                t[(size_t)(c + j + 1) * SEQ_LEN + pos] = f2bf(v[j + 1]);
+            }
+        }
+    }
+}
+
 // grid: an even number of CTAs (clusters of two), at most one per SM;
 // m_blocks counts 256-row blocks; B's maps have (BN / 2)-row boxes.
 template <int BN, bool kOutF32, int kEpi = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K, int kb_b,
-                  int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts) {
+                  int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts, const QkvOut qo) {
     using L = PairLayout<BN>;
     static_assert(BN == 128 || BN == 256, "pair tiles: 256 x 128 or 256 x 256");
     extern __shared__ uint8_t smem_raw[];
@@ -541,6 +671,15 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                             }
                         }
                     }
+                }
+            } else if constexpr (kEpi == 2) {
+                static_assert(kEpi != 2 || BN == 256, "the q|k|v epilogue takes two heads per tile");
+                if (m_w < m_valid) {
+                    const bool row_ok = m < m_valid, pair_ok = (qo.pos0 & 1) == 0 && (m | 1) < m_valid;
+                    #pragma unroll 1
+                    for (int hh = 0; hh < 2; hh++)
+                        qkv_head_out(qo, (t % n_blocks) * 2 + hh, m, row_ok, pair_ok,
+                                     tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)(HEAD_DIM * hh));
                 }
             } else if (m_w < m_valid) {
                 #pragma unroll 1

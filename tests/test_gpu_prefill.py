@@ -172,3 +172,34 @@ def test_prefill_programmatic_launch_matches_normal_launch(qb, checkpoint, tmp_p
         e.close()
     normal = np.load(tmp_path / "normal.npy")
     assert np.array_equal(lg, normal), np.abs(lg.astype(np.float64) - normal).max()
+
+
+def test_prefill_qkv_epilogue_matches_separate_kernel(qb, checkpoint, monkeypatch):
+    """QK-norm, RoPE, the K/V append and V's transposed copy in the q|k|v GEMM's
+    epilogue (passes of 768 rows and more) against the fp32-output GEMM plus
+    qkv_post_kernel (QWEN_B200_QKV_EPILOGUE=0, read when a handle is created)
+    and against the per-token path.  Chunks: 1000 rows at position 0, 1001 rows
+    at 1000 (an odd last row), 999 rows at 2001 (an odd first position: the
+    transposed-V stores go one position at a time)."""
+    chunks = [_prompt(1000, 71), _prompt(1001, 72), _prompt(999, 73)]
+    fused = qb.Engine(checkpoint, 0)
+    monkeypatch.setenv("QWEN_B200_QKV_EPILOGUE", "0")
+    sep = qb.Engine(checkpoint, 0)
+    monkeypatch.delenv("QWEN_B200_QKV_EPILOGUE")
+    tok = qb.Engine(checkpoint, 0)
+    tok.set_prefill_mode(False)
+    try:
+        pos = 0
+        for ch in chunks:
+            lf = fused.prefill(ch, pos, want_logits=True)
+            ls = sep.prefill(ch, pos, want_logits=True)
+            lt = tok.prefill(ch, pos, want_logits=True)
+            pos += len(ch)
+            assert np.abs(lf - ls).max() <= 2e-2 and rel_rms(lf, ls) <= 1e-3, (pos, np.abs(lf - ls).max(), rel_rms(lf, ls))
+            assert np.abs(lf - lt).max() <= 2e-2 and rel_rms(lf, lt) <= 2.5e-3, (pos, np.abs(lf - lt).max(), rel_rms(lf, lt))
+            assert int(np.argmax(lf)) == int(np.argmax(ls)) == int(np.argmax(lt))
+        gf, _ = fused.generate(int(np.argmax(lf)), pos, 8)
+        gs, _ = sep.generate(int(np.argmax(ls)), pos, 8)
+        assert gf == gs
+    finally:
+        fused.close(); sep.close(); tok.close()
