@@ -781,9 +781,11 @@ static int prefill_pass(qwen_t* c, int pos0, int m, int* down_splits = nullptr, 
         if (batch) {
             // key ranges per (row, KV head): enough blocks for two per SM
             const int S = std::max(1, std::min(kMaxKeySplits, (2 * c->nsm + m * N_KV_HEADS - 1) / (m * N_KV_HEADS)));
-            attention_rows_kernel<<<m * N_KV_HEADS * S, kDecAttThreads, 0, st>>>(c->pf_q, io->pos_rows, kc_l, vc_l, io->row_stride, S,
-                                                                                 c->pf_as, kLdAs, io->part);
-            if (S > 1) attention_combine_kernel<<<m * N_KV_HEADS, kDecAttThreads, 0, st>>>(io->part, S, c->pf_as, kLdAs);
+            CU(launch_pdl(attention_rows_kernel, dim3(m * N_KV_HEADS * S), dim3(kDecAttThreads), 0, st, (const float*)c->pf_q,
+                          (const int*)io->pos_rows, (const uint16_t*)kc_l, (const uint16_t*)vc_l, io->row_stride, S, c->pf_as, kLdAs, io->part));
+            if (S > 1)
+                CU(launch_pdl(attention_combine_kernel, dim3(m * N_KV_HEADS), dim3(kDecAttThreads), 0, st, (const float*)io->part, S, c->pf_as,
+                              kLdAs));
         } else if (c->att5) {
             if ((rc = attention_tc5(c, kc_l, vc_l, pos0, m, rows, fuse_qkv ? pos0 : pos0 + m, st)) != QWEN_OK) return rc;
         } else {
@@ -1408,23 +1410,46 @@ int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc
     return QWEN_OK;
 }
 
-// The pair (2-SM) form: clusters of two CTAs, 256 x BN tiles.
-template <int BN, bool F32, int kEpi = 0>
-int gemm_launch_pair(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                     int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3, const qb::tc::QkvOut& qo = qb::tc::QkvOut{}) {
+// The pair (2-SM) form: clusters of two CTAs, 256 x BN tiles; A holds P =
+// K / (kb_b 64) parts side by side, all P loaded in one stage.
+template <int BN, bool F32, int kEpi, int P>
+int gemm_launch_pair_p(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
+                       int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts, const qb::tc::QkvOut& qo) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
     if (attr_dev != dev) {
-        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                qb::tc::PairLayout<BN>::kSmem));
+        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                qb::tc::PairLayout<BN, P>::kSmem));
         attr_dev = dev;
     }
     const int items = bm.end[2] * (M / (2 * qb::tc::kBM)) * splits;
     const int pairs = std::min(items, nsm / 2);
-    CU(launch_pdl(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi>, dim3(2 * pairs), dim3(qb::tc::kThreads), (size_t)qb::tc::PairLayout<BN>::kSmem, st, ma,
-                  bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts, qo));
+    CU(launch_pdl(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, P>, dim3(2 * pairs), dim3(qb::tc::kThreads), (size_t)qb::tc::PairLayout<BN, P>::kSmem,
+                  st, ma, bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts, qo));
     return QWEN_OK;
+}
+template <int BN, bool F32, int kEpi = 0>
+int gemm_launch_pair(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
+                     int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3, const qb::tc::QkvOut& qo = qb::tc::QkvOut{}) {
+    switch (K / (kb_b * qb::tc::kBK)) {
+        case 1: return gemm_launch_pair_p<BN, F32, kEpi, 1>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts, qo);
+        case 2: return gemm_launch_pair_p<BN, F32, kEpi, 2>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts, qo);
+        case 3: return gemm_launch_pair_p<BN, F32, kEpi, 3>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts, qo);
+        default: return fail(QWEN_E_ARG, "the pair GEMM takes one to three activation parts");
+    }
+}
+template <int BN, bool F32, int kEpi>
+cudaError_t pair_smem_attrs() {
+    cudaError_t e = cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         qb::tc::PairLayout<BN, 1>::kSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 qb::tc::PairLayout<BN, 2>::kSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 qb::tc::PairLayout<BN, 3>::kSmem);
+    return e;
 }
 
 // Whether 256-row GEMMs run in the pair form (QWEN_B200_GEMM_PAIR=0 keeps every
@@ -1456,12 +1481,10 @@ static int gemm_prepare(int dev) {
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
     CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             qb::tc::Layout<256>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::PairLayout<256>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::PairLayout<256>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            qb::tc::PairLayout<256>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_pair<256, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            qb::tc::PairLayout<256>::kSmem));
+    CU((pair_smem_attrs<256, true, 0>()));
+    CU((pair_smem_attrs<256, false, 0>()));
+    CU((pair_smem_attrs<256, false, 1>()));
+    CU((pair_smem_attrs<256, true, 2>()));
     done[dev].store(true, std::memory_order_release);
     return QWEN_OK;
 }
@@ -1572,13 +1595,13 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     }
     // pair form (256 x 256 tiles on two SMs) for 256-row multiples whose tiles
     // (or K splits of them) give most of the SM pairs work
-    const bool pair = pair_gemm_enabled() && all256 && M % (2 * qb::tc::kBM) == 0;
+    const bool pair = pair_gemm_enabled() && all256 && M % (2 * qb::tc::kBM) == 0 && K / Kb <= 3;
     const int tiles256 = (N / 256) * (M / qb::tc::kBM) / (pair ? 2 : 1);
     const int slots = pair ? nsm / 2 : nsm;
     int splits = 1;
     if (split_cols >= N && all256 && 2 * tiles256 <= slots)
         for (int s = 2; s * tiles256 <= slots && (s - 1) * split_cols + N <= ldc; s++)
-            if ((K / qb::tc::kBK) % s == 0) splits = s;   // the largest that divides the K steps
+            if (((pair ? Kb : K) / qb::tc::kBK) % s == 0) splits = s;   // the largest that divides the K steps (of one part in the pair form)
     if (splits_used) *splits_used = splits;
     const int bn = all256 && (pair || splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;

@@ -352,14 +352,23 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
 // back on the leader's barrier.  No TMA multicast: each CTA loads its own
 // boxes into its own shared memory.  Same work items, split K, row padding and
 // epilogues as the single-CTA form, with 256-row m blocks.
-constexpr int kPairStages = 6;
-template <int BN>
+//
+// A that holds P bf16 parts of each activation side by side (A = [part 0 |
+// part 1 | ..], each Kb = K / P columns wide, against one B of Kb columns): a
+// stage holds the P A boxes of one K step and the B box once, and the MMA
+// thread issues the P products of each 16-wide K slice against the same B
+// slice, so B crosses from L2 once per K step instead of once per part (two
+// parts: 48 KB per stage and CTA for 2 x 128 x BN x 64 of MMA work instead of
+// 64 KB).
+template <int BN, int P>
 struct PairLayout {
-    static constexpr int kABytes = kBM * kBK * 2;          // this CTA's 128 rows of A
+    static_assert(P >= 1 && P <= 3, "one to three activation parts");
+    static constexpr int kABytes = kBM * kBK * 2;          // this CTA's 128 rows of one part of A
     static constexpr int kBBytes = (BN / 2) * kBK * 2;     // this CTA's BN / 2 rows of B
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarOff = kPairStages * kStageBytes;
-    static constexpr int kSmem = kBarOff + (2 * kPairStages + 4) * 8 + 16 + 1024;
+    static constexpr int kStageBytes = P * kABytes + kBBytes;
+    static constexpr int kStages = (192 * 1024 / kStageBytes) < 8 ? (192 * 1024 / kStageBytes) : 8;
+    static constexpr int kBarOff = kStages * kStageBytes;
+    static constexpr int kSmem = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -526,17 +535,18 @@ __device__ __forceinline__ void qkv_head_out(const QkvOut& qo, int hd, int m, bo
 
 // grid: an even number of CTAs (clusters of two), at most one per SM;
 // m_blocks counts 256-row blocks; B's maps have (BN / 2)-row boxes.
-template <int BN, bool kOutF32, int kEpi = 0>
+template <int BN, bool kOutF32, int kEpi = 0, int kParts = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K, int kb_b,
                   int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts, const QkvOut qo) {
-    using L = PairLayout<BN>;
+    using L = PairLayout<BN, kParts>;
+    constexpr int kSt = L::kStages;
     static_assert(BN == 128 || BN == 256, "pair tiles: 256 x 128 or 256 x 256");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-    uint64_t* empty = full + kPairStages;
-    uint64_t* acc_full = empty + kPairStages;
+    uint64_t* empty = full + kSt;
+    uint64_t* acc_full = empty + kSt;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -544,11 +554,11 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int n_blocks = bm.end[2];
     const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
-    const int nkb = K / kBK / splits;
+    const int nkb = K / kParts / kBK / splits;   // K steps per work item, each covering every part
     pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPairStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < kSt; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; b++) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 8); }   // 4 epilogue warps x 2 CTAs
         fence_barrier_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
@@ -582,14 +592,16 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
             // the ring's first stages: weight boxes while the previous kernel may still run
             // (no kernel writes the weights), activation boxes once it has finished
             uint32_t npre = 0;
-            for (; npre < (uint32_t)kPairStages && step(npre, m0, n0, kb, mb); npre++) {
+            for (; npre < (uint32_t)kSt && step(npre, m0, n0, kb, mb); npre++) {
                 if (rank == 0) mbar_arrive_expect_tx(&full[npre], 2 * L::kStageBytes);   // both CTAs' bytes
-                tma_load_2d_pair(smem + npre * L::kStageBytes + L::kABytes, mb, (kb % kb_b) * kBK, n0, full0 + 8u * npre);
+                tma_load_2d_pair(smem + npre * L::kStageBytes + kParts * L::kABytes, mb, kb * kBK, n0, full0 + 8u * npre);
             }
             pdl_wait();
             for (uint32_t it = 0; it < npre; it++) {
                 step(it, m0, n0, kb, mb);
-                tma_load_2d_pair(smem + it * L::kStageBytes, &map_a, kb * kBK, m0, full0 + 8u * it);
+                #pragma unroll
+                for (int p = 0; p < kParts; p++)
+                    tma_load_2d_pair(smem + it * L::kStageBytes + p * L::kABytes, &map_a, (p * kb_b + kb) * kBK, m0, full0 + 8u * it);
             }
             // the rest: coordinates once per work item (a division per step would slow this thread
             // below the MMA rate)
@@ -603,12 +615,13 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                 const int ni0 = (nb - (sg == 0 ? 0 : bm.end[sg - 1])) * BN + (BN / 2) * (int)rank;
                 for (int k = kb0; k < kb0 + nkb; k++, it++) {
                     if (it < npre) continue;   // loaded above
-                    const uint32_t s = it % kPairStages;
-                    if (!mbar_wait(&empty[s], ((it / kPairStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); ok = false; break; }
+                    const uint32_t s = it % kSt;
+                    if (!mbar_wait(&empty[s], ((it / kSt) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); ok = false; break; }
                     uint8_t* st = smem + s * L::kStageBytes;
                     if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);   // both CTAs' bytes
-                    tma_load_2d_pair(st, &map_a, k * kBK, mi0, full0 + 8u * s);
-                    tma_load_2d_pair(st + L::kABytes, mbi, (k % kb_b) * kBK, ni0, full0 + 8u * s);
+                    #pragma unroll
+                    for (int p = 0; p < kParts; p++) tma_load_2d_pair(st + p * L::kABytes, &map_a, (p * kb_b + k) * kBK, mi0, full0 + 8u * s);
+                    tma_load_2d_pair(st + kParts * L::kABytes, mbi, k * kBK, ni0, full0 + 8u * s);
                 }
             }
         }
@@ -623,13 +636,16 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                 tc_fence_after();
                 const uint32_t d = tmem + b * BN;
                 for (int kb = 0; kb < nkb && ok; kb++, it++) {
-                    const uint32_t s = it % kPairStages;
-                    if (!mbar_wait(&full[s], (it / kPairStages) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
+                    const uint32_t s = it % kSt;
+                    if (!mbar_wait(&full[s], (it / kSt) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a = smem_addr(smem + s * L::kStageBytes), bb = a + L::kABytes;
+                    const uint32_t a = smem_addr(smem + s * L::kStageBytes), bb = a + kParts * L::kABytes;
                     #pragma unroll
                     for (int kk = 0; kk < kBK / kUmmaK; kk++)
-                        mma_bf16_pair(d, kmajor_sw128_desc(a + kk * 32), kmajor_sw128_desc(bb + kk * 32), id, (kb | kk) != 0 ? 1u : 0u);
+                        #pragma unroll
+                        for (int p = 0; p < kParts; p++)
+                            mma_bf16_pair(d, kmajor_sw128_desc(a + p * L::kABytes + kk * 32), kmajor_sw128_desc(bb + kk * 32), id,
+                                          (kb | kk | p) != 0 ? 1u : 0u);
                     mma_commit_pair(&empty[s]);
                 }
                 mma_commit_pair(&acc_full[b]);   // complete (or abandoned: *err is set) in both CTAs

@@ -275,6 +275,8 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
                                                                         const uint16_t* __restrict__ kc_l, const uint16_t* __restrict__ vc_l,
                                                                         size_t row_cache_stride, int S, uint16_t* __restrict__ As,
                                                                         int ld_as, float* __restrict__ part) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float qs[2][HEAD_DIM];
     __shared__ float wm[8][2], wl[8][2];
     __shared__ __align__(16) float wacc[8][2][HEAD_DIM];
@@ -372,6 +374,8 @@ __global__ void __launch_bounds__(kDecAttThreads) attention_rows_kernel(const fl
 // thread (h, d) -> As.  An empty range (max -inf) contributes nothing.
 __global__ void __launch_bounds__(kDecAttThreads) attention_combine_kernel(const float* __restrict__ part, int S, uint16_t* __restrict__ As,
                                                                            int ld_as) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int r = blockIdx.x / N_KV_HEADS, hk = blockIdx.x % N_KV_HEADS, h = threadIdx.x >> 7, d = threadIdx.x & 127;
     const float* pb = part + (size_t)blockIdx.x * S * kPartFloats + h * (HEAD_DIM + 2);
     float M = -INFINITY;
