@@ -279,6 +279,7 @@ struct qwen_ctx {
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
     int att5 = 1;               // prompt-pass attention: 1 tcgen05 (attention_tc5.cuh, the default), 0 mma.sync
     bool qkv_epi = true;        // QK-norm, RoPE and the K/V append in the q|k|v GEMM's epilogue where it applies
+    int att_pp = 2;             // bf16 parts of the tcgen05 attention's P operand (1 or 2)
     uint16_t* vt = nullptr;     // the layer's V transposed ([head][dim][position]) for the tcgen05 attention
     int last_k = 0;
 };
@@ -422,6 +423,7 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     if (const char* e = getenv("QWEN_B200_PREFILL_ATTN")) c->att5 = strcmp(e, "mma") == 0 ? 0 : 1;
     // "0": q|k|v GEMM with fp32 output, then qkv_post_kernel, in every prompt pass
     if (const char* e = getenv("QWEN_B200_QKV_EPILOGUE")) c->qkv_epi = strcmp(e, "0") != 0;
+    if (const char* e = getenv("QWEN_B200_ATTN_P_PARTS")) c->att_pp = strcmp(e, "1") == 0 ? 1 : 2;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -712,7 +714,8 @@ static int pf_alloc(qwen_t* c) {
     TRY(dalloc(&c->pf_hs, (size_t)kMaxRows * 3 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_xn, (size_t)DIM));
     CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
-    CU(cudaFuncSetAttribute(attention_tc5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
+    CU(cudaFuncSetAttribute(attention_tc5_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
+    CU(cudaFuncSetAttribute(attention_tc5_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
     TRY(dalloc(&c->vt, (size_t)N_KV_HEADS * HEAD_DIM * SEQ_LEN));
     CU(cudaMemset(c->vt, 0, (size_t)N_KV_HEADS * HEAD_DIM * SEQ_LEN * sizeof(uint16_t)));
     return gemm_prepare(c->device);
@@ -1393,21 +1396,45 @@ bool cached_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
     return true;
 }
 
-template <int BN, bool F32, int kEpi = 0>
-int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3) {
+// The single-CTA form, 128 x BN tiles; A holds P = K / (kb_b 64) parts side
+// by side, all P loaded in one stage.
+template <int BN, bool F32, int kEpi, int P>
+int gemm_launch_p(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
+                  int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
     if (attr_dev != dev) {
-        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                qb::tc::Layout<BN>::kSmem));
+        CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                qb::tc::Layout<BN, P>::kSmem));
         attr_dev = dev;
     }
     const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
-    CU(launch_pdl(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi>, dim3(std::min(items, nsm)), dim3(qb::tc::kThreads),
-                  (size_t)qb::tc::Layout<BN>::kSmem, st, ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts));
+    CU(launch_pdl(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi, P>, dim3(std::min(items, nsm)), dim3(qb::tc::kThreads),
+                  (size_t)qb::tc::Layout<BN, P>::kSmem, st, ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts));
     return QWEN_OK;
+}
+template <int BN, bool F32, int kEpi = 0>
+int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
+                int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3) {
+    switch (K / (kb_b * qb::tc::kBK)) {
+        case 1: return gemm_launch_p<BN, F32, kEpi, 1>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts);
+        case 2: return gemm_launch_p<BN, F32, kEpi, 2>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts);
+        case 3: return gemm_launch_p<BN, F32, kEpi, 3>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts);
+        default: return fail(QWEN_E_ARG, "the GEMM takes one to three activation parts");
+    }
+}
+template <int BN, bool F32, int kEpi>
+cudaError_t single_smem_attrs() {
+    cudaError_t e = cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         qb::tc::Layout<BN, 1>::kSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 qb::tc::Layout<BN, 2>::kSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 qb::tc::Layout<BN, 3>::kSmem);
+    return e;
 }
 
 // The pair (2-SM) form: clusters of two CTAs, 256 x BN tiles; A holds P =
@@ -1475,12 +1502,11 @@ static int gemm_prepare(int dev) {
         CU(cudaMemset(g_gemm_err[dev], 0, sizeof(uint32_t)));
     }
     if (!g_nsm[dev]) CU(cudaDeviceGetAttribute(&g_nsm[dev], cudaDevAttrMultiProcessorCount, dev));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<256>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<256>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, qb::tc::Layout<128>::kSmem));
-    CU(cudaFuncSetAttribute(qb::tc::gemm_bf16_tc_persistent<256, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            qb::tc::Layout<256>::kSmem));
+    CU((single_smem_attrs<256, true, 0>()));
+    CU((single_smem_attrs<256, false, 0>()));
+    CU((single_smem_attrs<128, true, 0>()));
+    CU((single_smem_attrs<128, false, 0>()));
+    CU((single_smem_attrs<256, false, 1>()));
     CU((pair_smem_attrs<256, true, 0>()));
     CU((pair_smem_attrs<256, false, 0>()));
     CU((pair_smem_attrs<256, false, 1>()));
@@ -1553,7 +1579,7 @@ static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, 
     if (!cached_map(&mk, kc_l, (uint64_t)N_KV_HEADS * SEQ_LEN, HEAD_DIM, HEAD_DIM, kA5Keys) ||
         !cached_map(&mv, c->vt, (uint64_t)N_KV_HEADS * HEAD_DIM, SEQ_LEN, SEQ_LEN, HEAD_DIM))
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
-    CU(launch_pdl(attention_tc5_kernel, dim3(rows / kAttBlock * N_KV_HEADS), dim3(kA5Threads), (size_t)A5Layout::kSmem, st, mk, mv,
+    CU(launch_pdl(c->att_pp == 1 ? attention_tc5_kernel<1> : attention_tc5_kernel<2>, dim3(rows / kAttBlock * N_KV_HEADS), dim3(kA5Threads), (size_t)A5Layout::kSmem, st, mk, mv,
                   (const float*)c->pf_q, pos0, c->pf_as, 3 * HIDDEN_DIM, c->pf_parts, g_gemm_err[dev]));
     return QWEN_OK;
 }
@@ -1595,13 +1621,14 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     }
     // pair form (256 x 256 tiles on two SMs) for 256-row multiples whose tiles
     // (or K splits of them) give most of the SM pairs work
-    const bool pair = pair_gemm_enabled() && all256 && M % (2 * qb::tc::kBM) == 0 && K / Kb <= 3;
+    if (K / Kb > 3) return fail(QWEN_E_ARG, "K must be one to three times B's K extent");
+    const bool pair = pair_gemm_enabled() && all256 && M % (2 * qb::tc::kBM) == 0;
     const int tiles256 = (N / 256) * (M / qb::tc::kBM) / (pair ? 2 : 1);
     const int slots = pair ? nsm / 2 : nsm;
     int splits = 1;
     if (split_cols >= N && all256 && 2 * tiles256 <= slots)
         for (int s = 2; s * tiles256 <= slots && (s - 1) * split_cols + N <= ldc; s++)
-            if (((pair ? Kb : K) / qb::tc::kBK) % s == 0) splits = s;   // the largest that divides the K steps (of one part in the pair form)
+            if ((Kb / qb::tc::kBK) % s == 0) splits = s;   // the largest that divides the K steps (each step covers every part)
     if (splits_used) *splits_used = splits;
     const int bn = all256 && (pair || splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;

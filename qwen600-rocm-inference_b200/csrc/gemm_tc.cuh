@@ -10,7 +10,7 @@
 // 192 threads; CTA b takes output tiles b, b + grid, ... (128 x BN each):
 //   warp 0, one thread: TMA producer — 2-D tiled bulk tensor loads of a
 //           128 x 64 A box and a BN x 64 B box per K step, 128-byte swizzle,
-//           into a kStages-deep ring (mbarrier complete_tx) that runs on
+//           into a ring of stages (mbarrier complete_tx) that runs on
 //           across tile boundaries; no multicast.  Launched with programmatic
 //           stream serialization, the kernel starts while the kernel before it
 //           finishes: the producer loads the B (weight) boxes of the ring's
@@ -38,7 +38,6 @@ namespace tc {
 
 constexpr int kBM = 128;            // tile rows (TMEM lanes)
 constexpr int kBK = 64;             // K per stage: one 128-byte swizzle row
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kUmmaK = 16;          // K of one tcgen05.mma for 16-bit inputs
 constexpr uint64_t kWaitNs = 2000000000ull;
@@ -134,15 +133,18 @@ __device__ __forceinline__ void store32(void* C, int ldc, int m, int n, const fl
 // contiguous (n block j writes columns j * BN ..).
 //
 // Split K: with splits > 1 every tile is `splits` work items, item s taking
-// K steps [s, s + 1) * K / (64 splits) and writing its partial sum at column
+// K steps [s, s + 1) * kb_b / splits and writing its partial sum at column
 // offset s * c_split_off of C (the caller adds the partials).
 //
 // Rows m_valid .. M-1 of C are not written (padding rows of a short pass).
 //
-// K a multiple of 64 * splits; ldc in elements.  B's K extent may be a divisor
-// kb_b * 64 of K: K step kb reads B columns (kb mod kb_b) * 64, so
-// A = [a_1 | a_2 | a_3] (each K/3 wide) against B gives sum_i a_i . B^T — the
-// three-part bf16 split of fp32 activations in one accumulation.
+// ldc in elements.  B's K extent may be a divisor kb_b * 64 of K (K = P kb_b
+// 64, P = 1-3, the kernel's kParts): A = [a_1 | .. | a_P] (each kb_b * 64
+// wide) against B gives sum_i a_i . B^T — the bf16 parts of fp32 activations
+// in one accumulation.  A K step covers 64 columns of B and the same 64
+// columns of every a_i (one stage: the P A boxes and the B box once), and
+// the MMA thread issues the P products of each 16-wide slice in turn; kb_b is
+// a multiple of splits.
 struct BMaps {
     CUtensorMap map[3];
     int end[3];   // cumulative n-block counts; end[2] = total n blocks
@@ -164,11 +166,15 @@ struct QkvOut {
     const float* rope;
     int pos0;
 };
-template <int BN>
+// P = the activation parts of A (see PairLayout): a stage holds the P A boxes
+// of one K step and its B box once.
+template <int BN, int P>
 struct Layout {
+    static_assert(P >= 1 && P <= 3, "one to three activation parts");
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStageBytes = P * kABytes + kBBytes;
+    static constexpr int kStages = (192 * 1024 / kStageBytes) < 8 ? (192 * 1024 / kStageBytes) : 8;
     static constexpr int kBarOff = kStages * kStageBytes;   // full[S], empty[S], acc_full[2], acc_empty[2], tmem slot
     static constexpr int kSmem = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
 };
@@ -177,11 +183,12 @@ struct Layout {
 // n block j covering units 128 j ..); the epilogue writes h = silu(gate) * up as
 // epi_parts (1-3) bf16 parts (C: bf16, rows ldc apart, parts HIDDEN_DIM columns
 // apart), the down projection's A operand.
-template <int BN, bool kOutF32, int kEpi = 0>
+template <int BN, bool kOutF32, int kEpi = 0, int kParts = 1>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
                         int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts) {
-    using L = Layout<BN>;
+    using L = Layout<BN, kParts>;
+    constexpr int kStages = L::kStages;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
     static_assert(2 * BN <= 512, "two accumulators must fit the 512 TMEM columns");
     extern __shared__ uint8_t smem_raw[];
@@ -194,7 +201,7 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_blocks = bm.end[2];
     const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
-    const int nkb = K / kBK / splits;   // K steps per work item
+    const int nkb = K / kParts / kBK / splits;   // K steps per work item, each covering every part
     pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
@@ -232,12 +239,14 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
             uint32_t npre = 0;
             for (; npre < (uint32_t)kStages && step(npre, m0, n0, kb, mb); npre++) {
                 mbar_arrive_expect_tx(&full[npre], L::kStageBytes);
-                tma_load_2d(smem + npre * L::kStageBytes + L::kABytes, mb, (kb % kb_b) * kBK, n0, &full[npre]);
+                tma_load_2d(smem + npre * L::kStageBytes + kParts * L::kABytes, mb, kb * kBK, n0, &full[npre]);
             }
             pdl_wait();
             for (uint32_t it = 0; it < npre; it++) {
                 step(it, m0, n0, kb, mb);
-                tma_load_2d(smem + it * L::kStageBytes, &map_a, kb * kBK, m0, &full[it]);
+                #pragma unroll
+                for (int p = 0; p < kParts; p++)
+                    tma_load_2d(smem + it * L::kStageBytes + p * L::kABytes, &map_a, (p * kb_b + kb) * kBK, m0, &full[it]);
             }
             // the rest: coordinates once per work item (a division per step would slow this thread
             // below the MMA rate)
@@ -255,8 +264,9 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
                     if (!mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); ok = false; break; }
                     uint8_t* st = smem + s * L::kStageBytes;
                     mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-                    tma_load_2d(st, &map_a, k * kBK, mi0, &full[s]);
-                    tma_load_2d(st + L::kABytes, mbi, (k % kb_b) * kBK, ni0, &full[s]);
+                    #pragma unroll
+                    for (int p = 0; p < kParts; p++) tma_load_2d(st + p * L::kABytes, &map_a, (p * kb_b + k) * kBK, mi0, &full[s]);
+                    tma_load_2d(st + kParts * L::kABytes, mbi, k * kBK, ni0, &full[s]);
                 }
             }
         }
@@ -274,10 +284,13 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
                     const uint32_t s = it % kStages;
                     if (!mbar_wait(&full[s], (it / kStages) & 1u, kWaitNs)) { atomicOr(err, 2u); ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a = smem_addr(smem + s * L::kStageBytes), bb = a + L::kABytes;
+                    const uint32_t a = smem_addr(smem + s * L::kStageBytes), bb = a + kParts * L::kABytes;
                     #pragma unroll
                     for (int kk = 0; kk < kBK / kUmmaK; kk++)
-                        mma_bf16(d, kmajor_sw128_desc(a + kk * 32), kmajor_sw128_desc(bb + kk * 32), id, (kb | kk) != 0 ? 1u : 0u);
+                        #pragma unroll
+                        for (int p = 0; p < kParts; p++)
+                            mma_bf16(d, kmajor_sw128_desc(a + p * L::kABytes + kk * 32), kmajor_sw128_desc(bb + kk * 32), id,
+                                     (kb | kk | p) != 0 ? 1u : 0u);
                     mma_commit(&empty[s]);
                 }
                 mma_commit(&acc_full[b]);   // the accumulator is complete (or abandoned: *err is set)
