@@ -93,10 +93,7 @@ static_assert(2 * A5Layout::kSmem > 228 * 1024, "one CTA per SM: the kernel allo
 // unit is left to exp2: hi = the value rounded to 8 significant bits (adding
 // half a unit of the 16 dropped bits, then truncating), mid = the remainder
 // (exact in fp32) truncated to 8 significant bits; |a - hi - mid| < 2^-15 |a|.
-// Packed like cvt_bf16x2 (a in the low half).  round2_int: hi alone.
-__device__ __forceinline__ uint32_t round2_int(float a, float b) {
-    return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
-}
+// Packed like cvt_bf16x2 (a in the low half).
 __device__ __forceinline__ void split2x2_int(float a, float b, uint32_t& h, uint32_t& m) {
     const uint32_t ra = __float_as_uint(a) + 0x8000u, rb = __float_as_uint(b) + 0x8000u;
     const float ma = a - __uint_as_float(ra & 0xffff0000u), mb = b - __uint_as_float(rb & 0xffff0000u);
@@ -155,9 +152,6 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
 // map_v: the transposed V as [N_KV_HEADS * 128 rows][SEQ_LEN], boxes 128 x 64.
 // Output: the O projection's A operand, `parts` (1-3) bf16 parts of each value,
 // Q_DIM columns apart, in rows of As (ld_as apart).
-// kPParts: bf16 parts of P (2: |p - hi - mid| < 2^-15 p; 1: p rounded to 8
-// significant bits, half the P V products and fewer softmax instructions).
-template <int kPParts>
 __global__ void __launch_bounds__(kA5Threads, 1)
 attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v, const float* __restrict__ Q,
                      int pos0, uint16_t* __restrict__ As, int ld_as, int parts, uint32_t* err) {
@@ -238,7 +232,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
                 tc_fence_after();
                 const uint32_t vb = smem_addr(smem + A5Layout::kV + sv * kA5VBytes);
                 #pragma unroll
-                for (int j = 0; j < kPParts; j++)
+                for (int j = 0; j < 2; j++)
                     #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
                         mma_bf16_ts(tmem + kTmO, tmem + kTmP + 64 * pb + 32 * j + 8 * kk, kmajor_sw128_desc(vb + kk * 32), id_o,
@@ -322,7 +316,7 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
             // P (unnormalised), two bf16 parts, into P buffer t & 1 once P V of tile t - 2 is complete
             if (ok && use > 0 && !mbar_wait(&pempty[b], (use - 1) & 1u, 2 * tc::kWaitNs)) { atomicOr(err, 64u); ok = false; }
             tc_fence_after();
-            if constexpr (kPParts == 2) {
+            {
                 uint32_t h[16], md[16];
                 float ps = 0.f;
                 #pragma unroll
@@ -334,17 +328,6 @@ attention_tc5_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_con
                 l += ps;
                 tmem_st16(tmem + lane_off + kTmP + 64 * b + 16 * half, h);
                 tmem_st16(tmem + lane_off + kTmP + 64 * b + 32 + 16 * half, md);
-            } else {
-                uint32_t h[16];
-                float ps = 0.f;
-                #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const float p0 = ex2_ftz(fmaf(v[2 * j], c2, -mc)), p1 = ex2_ftz(fmaf(v[2 * j + 1], c2, -mc));
-                    ps += p0 + p1;
-                    h[j] = round2_int(p0, p1);
-                }
-                l += ps;
-                tmem_st16(tmem + lane_off + kTmP + 64 * b + 16 * half, h);
             }
             // rows whose max moved: scale their O columns (this half's 64) once P V of tile t - 1 is complete
             if (t > 0 && __any_sync(0xffffffffu, need)) {

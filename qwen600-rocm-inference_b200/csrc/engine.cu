@@ -279,7 +279,6 @@ struct qwen_ctx {
     int pf_parts = 2;           // bf16 parts of the activations the pass's projections read (3: fp32-exact, 2, 1)
     int att5 = 1;               // prompt-pass attention: 1 tcgen05 (attention_tc5.cuh, the default), 0 mma.sync
     bool qkv_epi = true;        // QK-norm, RoPE and the K/V append in the q|k|v GEMM's epilogue where it applies
-    int att_pp = 2;             // bf16 parts of the tcgen05 attention's P operand (1 or 2)
     uint16_t* vt = nullptr;     // the layer's V transposed ([head][dim][position]) for the tcgen05 attention
     int last_k = 0;
 };
@@ -423,7 +422,6 @@ extern "C" int qwen_create(const char* path, int device, qwen_t** out) {
     if (const char* e = getenv("QWEN_B200_PREFILL_ATTN")) c->att5 = strcmp(e, "mma") == 0 ? 0 : 1;
     // "0": q|k|v GEMM with fp32 output, then qkv_post_kernel, in every prompt pass
     if (const char* e = getenv("QWEN_B200_QKV_EPILOGUE")) c->qkv_epi = strcmp(e, "0") != 0;
-    if (const char* e = getenv("QWEN_B200_ATTN_P_PARTS")) c->att_pp = strcmp(e, "1") == 0 ? 1 : 2;
     P.chunk_count = c->chunk_count;
     TRY(reset_device_state(c));
     *out = c;
@@ -714,8 +712,7 @@ static int pf_alloc(qwen_t* c) {
     TRY(dalloc(&c->pf_hs, (size_t)kMaxRows * 3 * HIDDEN_DIM));
     TRY(dalloc(&c->pf_xn, (size_t)DIM));
     CU(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttTcSmem)));
-    CU(cudaFuncSetAttribute(attention_tc5_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
-    CU(cudaFuncSetAttribute(attention_tc5_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
+    CU(cudaFuncSetAttribute(attention_tc5_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)A5Layout::kSmem));
     TRY(dalloc(&c->vt, (size_t)N_KV_HEADS * HEAD_DIM * SEQ_LEN));
     CU(cudaMemset(c->vt, 0, (size_t)N_KV_HEADS * HEAD_DIM * SEQ_LEN * sizeof(uint16_t)));
     return gemm_prepare(c->device);
@@ -1579,7 +1576,7 @@ static int attention_tc5(qwen_t* c, const uint16_t* kc_l, const uint16_t* vc_l, 
     if (!cached_map(&mk, kc_l, (uint64_t)N_KV_HEADS * SEQ_LEN, HEAD_DIM, HEAD_DIM, kA5Keys) ||
         !cached_map(&mv, c->vt, (uint64_t)N_KV_HEADS * HEAD_DIM, SEQ_LEN, SEQ_LEN, HEAD_DIM))
         return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
-    CU(launch_pdl(c->att_pp == 1 ? attention_tc5_kernel<1> : attention_tc5_kernel<2>, dim3(rows / kAttBlock * N_KV_HEADS), dim3(kA5Threads), (size_t)A5Layout::kSmem, st, mk, mv,
+    CU(launch_pdl(attention_tc5_kernel, dim3(rows / kAttBlock * N_KV_HEADS), dim3(kA5Threads), (size_t)A5Layout::kSmem, st, mk, mv,
                   (const float*)c->pf_q, pos0, c->pf_as, 3 * HIDDEN_DIM, c->pf_parts, g_gemm_err[dev]));
     return QWEN_OK;
 }
