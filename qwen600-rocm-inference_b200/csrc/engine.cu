@@ -1449,7 +1449,7 @@ int gemm_launch_pair_p(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, 
     }
     const int items = bm.end[2] * (M / (2 * qb::tc::kBM)) * splits;
     const int pairs = std::min(items, nsm / 2);
-    CU(launch_pdl(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, P>, dim3(2 * pairs), dim3(qb::tc::kThreads), (size_t)qb::tc::PairLayout<BN, P>::kSmem,
+    CU(launch_pdl(qb::tc::gemm_bf16_tc_pair<BN, F32, kEpi, P>, dim3(2 * pairs), dim3(qb::tc::kPairThreads), (size_t)qb::tc::PairLayout<BN, P>::kSmem,
                   st, ma, bm, C, ldc, K, kb_b, M / (2 * qb::tc::kBM), splits, c_split_off, m_valid, err, epi_parts, qo));
     return QWEN_OK;
 }

@@ -39,6 +39,7 @@ namespace tc {
 constexpr int kBM = 128;            // tile rows (TMEM lanes)
 constexpr int kBK = 64;             // K per stage: one 128-byte swizzle row
 constexpr int kThreads = 192;
+constexpr int kPairThreads = 320;   // pair form: producer, MMA, 8 epilogue warps (two per TMEM lane quarter)
 constexpr int kUmmaK = 16;          // K of one tcgen05.mma for 16-bit inputs
 constexpr uint64_t kWaitNs = 2000000000ull;
 
@@ -364,7 +365,10 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
 // accumulator complete); the epilogue warps of both CTAs hand each accumulator
 // back on the leader's barrier.  No TMA multicast: each CTA loads its own
 // boxes into its own shared memory.  Same work items, split K, row padding and
-// epilogues as the single-CTA form, with 256-row m blocks.
+// epilogues as the single-CTA form, with 256-row m blocks, but eight epilogue
+// warps (kPairThreads): two per TMEM lane quarter, each draining half of the
+// tile's columns, so the last tile's epilogue, which no MMA work hides, takes
+// half as long.
 //
 // A that holds P bf16 parts of each activation side by side (A = [part 0 |
 // part 1 | ..], each Kb = K / P columns wide, against one B of Kb columns): a
@@ -549,7 +553,7 @@ __device__ __forceinline__ void qkv_head_out(const QkvOut& qo, int hd, int m, bo
 // grid: an even number of CTAs (clusters of two), at most one per SM;
 // m_blocks counts 256-row blocks; B's maps have (BN / 2)-row boxes.
 template <int BN, bool kOutF32, int kEpi = 0, int kParts = 1>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K, int kb_b,
                   int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts, const QkvOut qo) {
     using L = PairLayout<BN, kParts>;
@@ -572,7 +576,7 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSt; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 8); }   // 4 epilogue warps x 2 CTAs
+        for (int b = 0; b < 2; b++) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 16); }   // 8 epilogue warps x 2 CTAs
         fence_barrier_init();
         asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a) : "memory");
         for (int s = 0; s < 3; s++)
@@ -665,7 +669,9 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
             }
         }
     } else {
-        const int q = warp & 3;
+        // warps 2-9: warp w reads TMEM lanes 32 (w % 4) .. + 31 (the rows it may access) and
+        // half eh of the tile's columns (for the q|k|v epilogue: head eh of the tile)
+        const int q = warp & 3, eh = (warp - 2) >> 2;
         uint32_t i = 0;
         for (int w = pair; w < nitems; w += npairs, i++) {
             const uint32_t b = i & 1u, use = i >> 1;
@@ -679,7 +685,7 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                 if (m_w < m_valid) {
                     const int u0 = (t % n_blocks) * 128;
                     #pragma unroll 1
-                    for (int c = 0; c < 128; c += 32) {
+                    for (int c = 64 * eh; c < 64 * eh + 64; c += 32) {
                         float g[32], u[32];
                         tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, g);
                         tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 + c), u);
@@ -705,14 +711,12 @@ gemm_bf16_tc_pair(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                 static_assert(kEpi != 2 || BN == 256, "the q|k|v epilogue takes two heads per tile");
                 if (m_w < m_valid) {
                     const bool row_ok = m < m_valid, pair_ok = (qo.pos0 & 1) == 0 && (m | 1) < m_valid;
-                    #pragma unroll 1
-                    for (int hh = 0; hh < 2; hh++)
-                        qkv_head_out(qo, (t % n_blocks) * 2 + hh, m, row_ok, pair_ok,
-                                     tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)(HEAD_DIM * hh));
+                    qkv_head_out(qo, (t % n_blocks) * 2 + eh, m, row_ok, pair_ok,
+                                 tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)(HEAD_DIM * eh));
                 }
             } else if (m_w < m_valid) {
                 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = eh * BN / 2; c < (eh + 1) * BN / 2; c += 32) {
                     float v[32];
                     tmem_ld32(tmem + b * BN + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
                     if (m < m_valid) store32<kOutF32>(C, ldc, m, n0 + c, v);
