@@ -296,10 +296,16 @@ def gemm_sweep(qb, peak_tflops):
 def long_context(qb, ck, n_prompt=4096, n_gen=512):
     """4096 seeded prompt tokens, then 512 sampled tokens (temperature 0.6,
     top-k 20, top-p 0.95, seeded xorshift64*), KV cache sized 8192: decode
-    tok/s from the device time of the 512 chained launches."""
+    tok/s from the device time of the 512 chained launches.  The prompt is
+    prefilled twice (the second call writes the same cache): prefill_tok_s is
+    the second, synchronous call's wall time; the first call, which also sets
+    up the handle's prompt-pass buffers and tensor maps, is reported beside it."""
     eng = qb.Engine(ck, 0)
     try:
         prompt = np.random.default_rng(4096).integers(0, 151936, n_prompt).tolist()
+        t0 = time.perf_counter()
+        eng.prefill(prompt, 0)
+        first_s = time.perf_counter() - t0
         t0 = time.perf_counter()
         eng.prefill(prompt, 0)
         pre_s = time.perf_counter() - t0
@@ -309,7 +315,7 @@ def long_context(qb, ck, n_prompt=4096, n_gen=512):
         eng.close()
     return {"value": n_gen / (ms / 1e3), "unit": "tok/s", "prompt_tokens": n_prompt, "sampled_tokens": n_gen,
             "sampling": {"temperature": 0.6, "top_k": 20, "top_p": 0.95}, "ms_per_token": ms / n_gen,
-            "prefill_tok_s": n_prompt / pre_s}
+            "prefill_tok_s": n_prompt / pre_s, "prefill_first_call_tok_s": n_prompt / first_s}
 
 
 def batched_decode(qb, ck, batches=(8, 32, 128), n_prompt=1024, n_steps=24, warmup=3, sampled=(32,)):
