@@ -203,3 +203,24 @@ def test_prefill_qkv_epilogue_matches_separate_kernel(qb, checkpoint, monkeypatc
         assert gf == gs
     finally:
         fused.close(); sep.close(); tok.close()
+
+
+@pytest.mark.parametrize("parts,tol,abs_tol", [(3, 2.5e-3, 2e-2), (1, 1e-2, 1e-1)])
+def test_prefill_activation_parts(qb, checkpoint, parts, tol, abs_tol):
+    """The tensor-core passes with three bf16 parts per activation (fp32-exact
+    operands: one GEMM stage holds three A boxes and the B box) and with one
+    (plain bf16 activations, ~5e-3 relative RMS from the fp32 chain, hence the
+    looser bound) against the per-token path: a 2048-row pass (SM-pair GEMMs,
+    the q|k|v epilogue) and a 300-row pass (single-CTA GEMMs)."""
+    for n, seed in ((2048, 81), (300, 82)):
+        toks = _prompt(n, seed)
+        a, b = qb.Engine(checkpoint, 0), qb.Engine(checkpoint, 0)
+        a.set_prefill_parts(parts)
+        b.set_prefill_mode(False)
+        try:
+            la = a.prefill(toks, 0, want_logits=True)
+            lb = b.prefill(toks, 0, want_logits=True)
+            assert np.abs(la - lb).max() <= abs_tol and rel_rms(la, lb) <= tol, (parts, n, np.abs(la - lb).max(), rel_rms(la, lb))
+            assert int(np.argmax(la)) == int(np.argmax(lb))
+        finally:
+            a.close(); b.close()
