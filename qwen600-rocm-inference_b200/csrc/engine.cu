@@ -1397,7 +1397,7 @@ bool cached_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, 
 // by side, all P loaded in one stage.
 template <int BN, bool F32, int kEpi, int P>
 int gemm_launch_p(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                  int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts) {
+                  int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts, int a_rows) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     CU(cudaGetDevice(&dev));
@@ -1408,16 +1408,19 @@ int gemm_launch_p(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int l
     }
     const int items = bm.end[2] * (M / qb::tc::kBM) * splits;
     CU(launch_pdl(qb::tc::gemm_bf16_tc_persistent<BN, F32, kEpi, P>, dim3(std::min(items, nsm)), dim3(qb::tc::kThreads),
-                  (size_t)qb::tc::Layout<BN, P>::kSmem, st, ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts));
+                  (size_t)qb::tc::Layout<BN, P>::kSmem, st, ma, bm, C, ldc, K, kb_b, M / qb::tc::kBM, splits, c_split_off, m_valid, err, epi_parts,
+                  a_rows));
     return QWEN_OK;
 }
+// a_rows: the height of ma's box (qb::tc::kBM, or fewer rows when M is one
+// 128-row block of which only those are valid).
 template <int BN, bool F32, int kEpi = 0>
 int gemm_launch(const CUtensorMap& ma, const qb::tc::BMaps& bm, void* C, int ldc, int M, int K, int kb_b, int splits, int c_split_off,
-                int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3) {
+                int m_valid, int nsm, cudaStream_t st, uint32_t* err, int epi_parts = 3, int a_rows = qb::tc::kBM) {
     switch (K / (kb_b * qb::tc::kBK)) {
-        case 1: return gemm_launch_p<BN, F32, kEpi, 1>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts);
-        case 2: return gemm_launch_p<BN, F32, kEpi, 2>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts);
-        case 3: return gemm_launch_p<BN, F32, kEpi, 3>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts);
+        case 1: return gemm_launch_p<BN, F32, kEpi, 1>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts, a_rows);
+        case 2: return gemm_launch_p<BN, F32, kEpi, 2>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts, a_rows);
+        case 3: return gemm_launch_p<BN, F32, kEpi, 3>(ma, bm, C, ldc, M, K, kb_b, splits, c_split_off, m_valid, nsm, st, err, epi_parts, a_rows);
         default: return fail(QWEN_E_ARG, "the GEMM takes one to three activation parts");
     }
 }
@@ -1630,7 +1633,11 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     const int bn = all256 && (pair || splits > 1 || tiles256 >= nsm) ? 256 : 128;
     CUtensorMap ma;
     qb::tc::BMaps bm;
-    if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, qb::tc::kBM)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
+    const int mv = m_valid > 0 && m_valid < M ? m_valid : M;
+    // one 128-row block with few valid rows (a batched decode step): A boxes of only
+    // those rows (rounded up to 8), so the padding rows do not cross from L2
+    const int a_rows = !pair && M == qb::tc::kBM ? (mv + 7) / 8 * 8 : qb::tc::kBM;
+    if (!cached_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, (uint32_t)a_rows)) return fail(QWEN_E_CUDA, "cuTensorMapEncodeTiled failed");
     int s = 0, end = 0;
     for (const BSeg& sg : segs) {
         if (!cached_map(&bm.map[s], sg.B, (uint64_t)sg.rows, (uint64_t)Kb, (uint64_t)ldb, (uint32_t)(pair ? bn / 2 : bn)))
@@ -1641,13 +1648,12 @@ static int gemm_tc(const void* A, int lda, std::initializer_list<BSeg> segs, int
     for (; s < 3; s++) { bm.map[s] = bm.map[0]; bm.end[s] = end; }
     const int kb_b = Kb / qb::tc::kBK;
     const int so = splits > 1 ? split_cols : 0;
-    const int mv = m_valid > 0 && m_valid < M ? m_valid : M;
     if (pair) return c_fp32 ? gemm_launch_pair<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
                             : gemm_launch_pair<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
-    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
-                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
-    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev])
-                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev]);
+    if (bn == 256) return c_fp32 ? gemm_launch<256, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev], 3, a_rows)
+                                 : gemm_launch<256, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev], 3, a_rows);
+    return c_fp32 ? gemm_launch<128, true>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev], 3, a_rows)
+                  : gemm_launch<128, false>(ma, bm, C, ldc, M, K, kb_b, splits, so, mv, nsm, st, g_gemm_err[dev], 3, a_rows);
 }
 
 // The GEMM kernel's error word for the handle's device (a bounded wait ran out

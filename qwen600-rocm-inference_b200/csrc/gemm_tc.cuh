@@ -187,7 +187,7 @@ struct Layout {
 template <int BN, bool kOutF32, int kEpi = 0, int kParts = 1>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ BMaps bm, void* C, int ldc, int K,
-                        int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts) {
+                        int kb_b, int m_blocks, int splits, int c_split_off, int m_valid, uint32_t* err, int epi_parts, int a_rows) {
     using L = Layout<BN, kParts>;
     constexpr int kStages = L::kStages;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256 && (BN & (BN - 1)) == 0, "tcgen05 M=128 tile: N a power of two in [32, 256]");
@@ -203,6 +203,10 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
     const int n_blocks = bm.end[2];
     const int ntiles = n_blocks * m_blocks, nitems = ntiles * splits;
     const int nkb = K / kParts / kBK / splits;   // K steps per work item, each covering every part
+    // A boxes of a_rows rows (the map's box height: 128, or fewer when one m block holds
+    // only that many valid rows; the rest of the A slot keeps stale data, which only
+    // reaches padding rows of the result, never stored)
+    const uint32_t stage_tx = (uint32_t)(kParts * a_rows * kBK * 2 + L::kBBytes);
     pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
@@ -239,7 +243,7 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
             // (no kernel writes the weights), activation boxes once it has finished
             uint32_t npre = 0;
             for (; npre < (uint32_t)kStages && step(npre, m0, n0, kb, mb); npre++) {
-                mbar_arrive_expect_tx(&full[npre], L::kStageBytes);
+                mbar_arrive_expect_tx(&full[npre], stage_tx);
                 tma_load_2d(smem + npre * L::kStageBytes + kParts * L::kABytes, mb, kb * kBK, n0, &full[npre]);
             }
             pdl_wait();
@@ -264,7 +268,7 @@ gemm_bf16_tc_persistent(const __grid_constant__ CUtensorMap map_a, const __grid_
                     const uint32_t s = it % kStages;
                     if (!mbar_wait(&empty[s], ((it / kStages) - 1) & 1u, kWaitNs)) { atomicOr(err, 1u); ok = false; break; }
                     uint8_t* st = smem + s * L::kStageBytes;
-                    mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
                     #pragma unroll
                     for (int p = 0; p < kParts; p++) tma_load_2d(st + p * L::kABytes, &map_a, (p * kb_b + k) * kBK, mi0, &full[s]);
                     tma_load_2d(st + kParts * L::kABytes, mbi, k * kBK, ni0, &full[s]);
