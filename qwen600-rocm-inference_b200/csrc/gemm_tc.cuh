@@ -392,6 +392,14 @@ struct PairLayout {
     static constexpr int kSmem = kBarOff + (2 * kStages + 4) * 8 + 16 + 1024;
 };
 
+// Every layout the host instantiates fits one CTA's shared memory (227 KB).
+static_assert(Layout<256, 3>::kSmem <= 227 * 1024 && Layout<256, 2>::kSmem <= 227 * 1024 && Layout<256, 1>::kSmem <= 227 * 1024 &&
+                  Layout<128, 3>::kSmem <= 227 * 1024 && Layout<128, 1>::kSmem <= 227 * 1024,
+              "single-CTA GEMM stages must fit shared memory");
+static_assert(PairLayout<256, 3>::kSmem <= 227 * 1024 && PairLayout<256, 2>::kSmem <= 227 * 1024 && PairLayout<256, 1>::kSmem <= 227 * 1024,
+              "pair GEMM stages must fit shared memory");
+static_assert(Layout<256, 3>::kStages >= 2 && PairLayout<256, 3>::kStages >= 2, "at least two stages in flight");
+
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
